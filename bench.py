@@ -1,0 +1,327 @@
+#!/usr/bin/env python
+"""MoE-layer forward benchmark (tokens/s) on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl swiftmoe|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload: the Mixtral-shaped MoE layer, bf16: d_model=4096, 8 experts, top-2 softmax
+gating, SwiGLU d_ff=14336, 16384 tokens per GPU ~ N(0,1), weights N(0, 0.02), no
+router bias, no capacity limit (synthetic, seeded; no dataset is involved).  At N GPUs
+the experts are split 8/N per GPU (expert parallelism, all-to-all over NCCL) and every
+GPU routes its own 16384 tokens (weak scaling).
+
+One step = one forward of the layer over one batch.  `value` is the whole-job
+throughput with the input already resident in HBM; `e2e` is the same forward through
+the public module API with the input copied from pinned host memory and the output
+copied back inside the timed region.  `--impl reference` times the reference algorithm
+on the host CPU (the numpy restatement in oracle/, since the reference is pure Python
+torch with no SwiGLU expert) on a bounded token sample of the same layer.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer fwd tokens/sec at 1/2/4/8 B200; exposed all-to-all ms; % of roofline"
+D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = 4096, 8, 2, 14336, 16384
+WORKLOAD = "mixtral-moe-layer-fwd: d_model 4096, 8 experts top-2 softmax, SwiGLU d_ff 14336, 16384 tok/GPU, bf16"
+# dram__bytes_read.sum + dram__bytes_write.sum of one grouped SwiGLU (gate/up) GEMM launch,
+# from the ncu capture summarised in profiles/grouped_swiglu_gemm_mixtral.md (None until captured)
+GEMM1_DRAM_BYTES_PER_LAUNCH = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="swiftmoe", choices=["swiftmoe", "reference"])
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            parts = [p.strip() for p in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names[1:], parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------- CPU arm
+def cpu_reference(tokens_budget_s: float, sample_tokens: int = 64, seed: int = 0):
+    """Time the numpy restatement of the reference forward on this host's cores."""
+    import numpy as np
+    from threadpoolctl import threadpool_info
+
+    from oracle import moe_oracle as O
+
+    rng = np.random.default_rng(seed)
+    E, d, F = N_EXPERTS, D_MODEL, D_FF
+
+    def w(shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * 0.02)
+
+    p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
+    x = rng.standard_normal((sample_tokens, d), dtype=np.float32)
+    O.moe_forward([x[:8]], p, k=TOP_K)  # warm BLAS
+    done, t0 = 0, time.perf_counter()
+    while True:
+        O.moe_forward([x], p, k=TOP_K)
+        done += sample_tokens
+        el = time.perf_counter() - t0
+        if el >= tokens_budget_s:
+            break
+    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    return {"value": done / el, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+            "sample": f"{done} tokens in batches of {sample_tokens} through the full layer "
+                      f"(numpy fp32, oracle/moe_oracle.py), {el:.1f} s"}, p, x
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from threadpoolctl import threadpool_info
+
+    from oracle import moe_oracle as O
+    rng = np.random.default_rng(0)
+    E, d, F = N_EXPERTS, D_MODEL, D_FF
+
+    def w(shape):
+        return rng.standard_normal(shape, dtype=np.float32) * 0.02
+
+    p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
+    sample = 64
+    x = rng.standard_normal((sample, d), dtype=np.float32)
+    for _ in range(args.warmup):
+        O.moe_forward([x], p, k=TOP_K)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.moe_forward([x], p, k=TOP_K)
+    el = time.perf_counter() - t0
+    v = sample * args.steps / el
+    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "parallelism": "host CPU", "sample_tokens_per_step": sample},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+                             "sample": f"{sample} tokens per step through the full layer (numpy fp32 "
+                                       f"restatement of the reference forward, oracle/moe_oracle.py)"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import swiftmoe_b200 as S
+    from swiftmoe_b200 import _lib as L
+
+    T = args.tokens
+    torch.manual_seed(1234)
+    model = S.UltimateMoE(N_EXPERTS, D_MODEL, use_fp16=False, use_nccl_opt=False, dtype=torch.bfloat16,
+                          top_k=TOP_K, expert_type="swiglu", d_ff=D_FF, device=dev,
+                          enable_profiling=(ws > 1))
+    with torch.no_grad():
+        g = torch.Generator(device=dev).manual_seed(7)   # identical gate on every rank
+        model.gate_weight.copy_(torch.randn(model.gate_weight.shape, generator=g, device=dev) * 0.02)
+    x = torch.randn((T, D_MODEL), device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(100 + rank))
+    out = torch.empty_like(x)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier(device_ids=[local])
+
+    def step(events=None):
+        if ws == 1:
+            return model._forward_fused(x, events, out=out)
+        return model(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    model.reset_profiling()
+    barrier()
+    torch.cuda.synchronize()
+    evs = [L.StageEvents() for _ in range(args.steps)] if ws == 1 else None
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t_start.record()
+        for i in range(args.steps):
+            step(evs[i] if evs else None)
+        t_end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    if ws > 1:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    value = T * ws / (ms / 1e3)
+
+    # per-stage / per-kernel times from the events recorded in the timed region
+    if ws == 1:
+        st = {"Router": [], "Dispatch_Comm": [], "Expert_GEMM1": [], "Expert_GEMM2": [], "Combine_Comm": []}
+        for e in evs:
+            st["Router"].append(e.elapsed(0, 1))
+            st["Dispatch_Comm"].append(e.elapsed(1, 2))
+            st["Expert_GEMM1"].append(e.elapsed(2, 3))
+            st["Expert_GEMM2"].append(e.elapsed(3, 4))
+            st["Combine_Comm"].append(e.elapsed(4, 5))
+        stage_ms = {k: statistics.mean(v) for k, v in st.items()}
+        exposed = 0.0
+    else:
+        s = model.get_profile_summary()
+        stage_ms = {k: v for k, v in s.items()}
+        exposed = s.get("Exposed_A2A", 0.0)
+    burst, sustained, hbm, src = peaks()
+    S_rows = T * TOP_K
+    if ws == 1:
+        gemm1_ms = stage_ms["Expert_GEMM1"]
+        flops = 2.0 * S_rows * D_MODEL * 2 * D_FF
+        kname = "grouped SwiGLU gate/up GEMM (tcgen05)"
+    else:
+        gemm1_ms = stage_ms["Expert_Compute"]
+        flops = 6.0 * S_rows * D_MODEL * D_FF
+        kname = "expert FFN (both grouped GEMMs, tcgen05); rows assumed balanced (T*k per rank)"
+    achieved = flops / (gemm1_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": sustained,
+                "peak_kind": f"bf16_tflops_sustained ({src})", "unit": "TFLOP/s", "frac": achieved / sustained,
+                "traffic": GEMM1_DRAM_BYTES_PER_LAUNCH, "algorithmic_flops_per_launch": flops,
+                "launch_ms": gemm1_ms}
+    layer_flops = 6.0 * S_rows * D_MODEL * D_FF + 2.0 * T * D_MODEL * N_EXPERTS
+    layer_frac = layer_flops / (ms / 1e3) / 1e12 / sustained
+
+    # end-to-end through the public API: pinned host input -> forward -> pinned host output
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(2):
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(model(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(model(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        tm = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms_e2e = float(tm.item())
+    e2e = {"value": T * ws / (ms_e2e / 1e3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+           "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+           "d2h_bytes_per_step": oh.numel() * oh.element_size()}
+
+    launches_per_step = 8 if ws == 1 else 11
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        try:
+            cpu, _, _ = cpu_reference(args.cpu_seconds)
+        except Exception as ex:  # reported, never fatal
+            cpu = {"value": None, "error": repr(ex)}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: x ~ N(0,1), weights N(0,0.02), seeded",
+                "config": {"workload": WORKLOAD, "d_model": D_MODEL, "num_experts": N_EXPERTS, "top_k": TOP_K,
+                           "d_ff": D_FF, "tokens_per_gpu": T, "parallelism": f"ep{ws}",
+                           "l2": "inputs larger than L2: x 128 MiB and 2.82 GB of expert weights read every step"},
+                "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+                "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,
+                "cpu_baseline": cpu, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,202 @@
+/*
+ * swiftmoe.h -- C ABI of the B200 (sm_100a) MoE-layer forward library (libswiftmoe.so).
+ *
+ * Every entry point takes plain device pointers and sizes, enqueues its work on the
+ * given CUDA stream and returns an int status (SMOE_OK or a negative SMOE_ERR_*).
+ * Nothing allocates device memory except smoe_ep_* (the expert-parallel exchange
+ * buffers) ; scratch space is passed in by the caller and sized by the matching
+ * *_workspace_size() query.  No call synchronises the host with the device unless its
+ * comment says so.
+ *
+ * Each entry point names the SwiftMoE reference code it replaces (file:line in the
+ * reference project).  Tensor layouts are row-major; "[A, B]" means B is contiguous.
+ */
+#ifndef SWIFTMOE_H_
+#define SWIFTMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* smoe_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define SMOE_API __attribute__((visibility("default")))
+#else
+#define SMOE_API
+#endif
+
+/* ----------------------------------------------------------------------------- status */
+#define SMOE_OK 0
+#define SMOE_ERR_INVALID (-1)     /* bad argument: null pointer, bad size, k > E, ... */
+#define SMOE_ERR_CUDA (-2)        /* a CUDA runtime / driver call failed               */
+#define SMOE_ERR_TIMEOUT (-3)     /* a device-side bounded wait gave up                */
+#define SMOE_ERR_UNSUPPORTED (-4) /* valid but unsupported shape / dtype combination   */
+#define SMOE_ERR_WORKSPACE (-5)   /* workspace too small                               */
+
+/* ------------------------------------------------------------------------------ dtypes */
+#define SMOE_F32 0
+#define SMOE_F16 1
+#define SMOE_BF16 2
+
+/* ----------------------------------------------------------------------- expert kinds */
+#define SMOE_EXPERT_LINEAR 0 /* y = x W_e^T           (one bias-free d x d linear)      */
+#define SMOE_EXPERT_SWIGLU 1 /* y = w2(silu(w1 x) * w3 x)                               */
+
+SMOE_API const char* smoe_version(void);
+SMOE_API const char* smoe_status_string(int status);
+/* Number of SMs of the current device (used to size persistent grids). */
+SMOE_API int smoe_device_sm_count(void);
+/* Read and clear the device-side error word set by bounded waits inside kernels.
+ * Synchronises the stream.  *flag receives 0 when no wait timed out. */
+SMOE_API int smoe_read_device_error(int* flag, smoe_stream_t stream);
+
+/* ------------------------------------------------------------------------------ router
+ * logits[t,e] = sum_i x[t,i] * wg[e,i] (+ logit_bias[e]) accumulated in fp32; top-k over
+ * e with ties to the LOWER expert index and NaN ranked highest; w = softmax of the k
+ * selected logits (fp32).  Outputs idx [T,k] int32 (values descending), w [T,k] fp32,
+ * and, when logits_out != NULL, the fp32 gate logits [T,E] before logit_bias is added.
+ * k <= min(E, 32), E <= 1024.
+ * Replaces: models/ultimate_moe.py:34-101 (fused_router_dispatch_kernel), :288-295
+ * (torch routing fallback) and models/baseline_moe.py:56-67 (_route_tokens).        */
+SMOE_API int smoe_router_fwd(const void* x, const void* wg, int dtype, const float* logit_bias,
+                     int T, int d, int E, int k, int32_t* idx, float* w, float* logits_out,
+                     void* workspace, size_t workspace_bytes, smoe_stream_t stream);
+SMOE_API size_t smoe_router_workspace_size(int T, int d, int E, int dtype);
+
+/* Top-k + softmax from given fp32 logits [T,E] (bit-exact routing entry point).
+ * Replaces: torch.topk + torch.softmax at models/baseline_moe.py:62-65 and
+ * models/ultimate_moe.py:290-291.                                                    */
+SMOE_API int smoe_topk_from_logits(const float* logits, int T, int E, int k, int32_t* idx, float* w,
+                          smoe_stream_t stream);
+
+/* ---------------------------------------------------------------------- dispatch plan
+ * Groups the T*k (token, slot) pairs by expert in index order (token-major, then slot)
+ * without any host round trip.  Outputs:
+ *   expert_counts [E]   : rows routed to each expert (before the capacity cut)
+ *   expert_offsets[E+1] : start row of each expert's segment (exclusive scan of the kept
+ *                         counts, each rounded up to row_align); [E] = total rows
+ *   slot_row  [T*k]     : destination row of every slot, -1 when dropped by capacity
+ *   row_token [rows_cap]: source token of every row, -1 for alignment padding
+ * capacity <= 0 means unlimited; otherwise at most `capacity` rows per expert are kept,
+ * the lowest (token, slot) indices winning.  rows_cap must be >= smoe_plan_rows_cap().
+ * Replaces: bincount / argsort / repeat_interleave bookkeeping at
+ * models/ultimate_moe.py:118-125 and :224-231, models/baseline_moe.py:80-98.        */
+SMOE_API size_t smoe_plan_workspace_size(int T, int k, int E);
+SMOE_API int64_t smoe_plan_rows_cap(int T, int k, int E, int capacity, int row_align);
+SMOE_API int smoe_dispatch_plan(const int32_t* idx, int T, int k, int E, int capacity, int row_align,
+                       int32_t* expert_counts, int32_t* expert_offsets, int32_t* slot_row,
+                       int32_t* row_token, int64_t rows_cap, void* workspace,
+                       size_t workspace_bytes, smoe_stream_t stream);
+
+/* rows[r,:] = x[row_token[r],:] for r < expert_offsets[E] (zero rows for token -1).
+ * Replaces: x.repeat_interleave(2)[sort_idx] and recv_x[expert_order]
+ * (models/ultimate_moe.py:123,225).                                                  */
+SMOE_API int smoe_permute_rows(const void* x, int dtype, int T, int d, const int32_t* row_token,
+                      const int32_t* expert_offsets, int E, int64_t rows_cap, void* rows,
+                      smoe_stream_t stream);
+
+/* out[t,:] = sum_{j<k} w[t,j] * y[slot_row[t,j],:] (slots in order 0..k-1, fp32
+ * accumulation, dropped slots skipped) + (shared ? shared[t,:] : 0).
+ * Replaces: combined_x[sort_idx_rev].view(M,2,d).sum(dim=1) and the gate weighting
+ * (models/ultimate_moe.py:154-155,245; models/baseline_moe.py:162,188-189).         */
+SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, const float* w, int T,
+                 int k, int d, const void* shared, void* out, smoe_stream_t stream);
+
+/* --------------------------------------------------------------------- expert GEMMs
+ * Grouped GEMM over G groups of rows.  Group g owns rows [offsets[g], offsets[g+1]) of
+ * A [rows_cap, K] and multiplies them by B_g^T where B is [G, N, K] (nn.Linear layout,
+ * K contiguous).  offsets lives in device memory and is read by the kernel.
+ *   epilogue SMOE_EPI_STORE  : C[r, n] = acc                       (C is [rows_cap, N])
+ *   epilogue SMOE_EPI_SWIGLU : C[r, n] = silu(A B1_g^T) * (A B3_g^T) (B3 = B2 arg, C [rows_cap, N])
+ * bf16 / fp16 run on tcgen05 tensor cores (TMEM accumulators, TMA-fed shared memory,
+ * requires K % 8 == 0 and N % 8 == 0); fp32 runs on FFMA (SIMT) for full fp32 accuracy.
+ * C may be fp32 for the bf16/fp16 STORE epilogue when out_dtype == SMOE_F32.
+ * Replaces: the per-expert loop of torch.mm at models/ultimate_moe.py:237-250 and
+ * nn.Linear experts at models/baseline_moe.py:151-162.                               */
+#define SMOE_EPI_STORE 0
+#define SMOE_EPI_SWIGLU 1
+SMOE_API int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype,
+                      int out_dtype, int epilogue, const int32_t* offsets, int G,
+                      int64_t rows_cap, int N, int K, smoe_stream_t stream);
+
+/* dst[g, c, r] = src[g, r, c] for G matrices of [R, C] (weight relayout, e.g. the
+ * reference's x@W expert_weights [E, d_in, d_out] -> nn.Linear layout [E, d_out, d_in]). */
+SMOE_API int smoe_transpose_batched(const void* src, void* dst, int dtype, int G, int R, int C,
+                           smoe_stream_t stream);
+
+/* dst[r,:] = src[index[r],:] for r < n_rows, zero rows where index[r] is -1.
+ * Replaces: combined_x[sort_idx_rev] / expert_out[argsort(expert_order)] gathers
+ * (models/ultimate_moe.py:154,252).                                                  */
+SMOE_API int smoe_gather_rows(const void* src, int dtype, int d, const int32_t* index, int64_t n_rows,
+                              void* dst, smoe_stream_t stream);
+
+/* ------------------------------------------------------------ expert parallelism
+ * Receive side of the dispatch all-to-all: rows arrive grouped by source rank, then by
+ * local expert (recv_counts is [ws, E_l], row-major).  Builds the expert-major layout
+ * the grouped GEMM consumes, applying the capacity cut in (source rank, token, slot)
+ * order:
+ *   expert_counts [E_l]   rows received per local expert (before the cut)
+ *   expert_offsets[E_l+1] start row of each local expert; [E_l] = total kept rows
+ *   row_src [>= n_recv]   received row that feeds each expert row
+ *   recv_dst[n_recv]      expert row of each received row, -1 when dropped
+ * Replaces: the receive-side bookkeeping of models/ultimate_moe.py:128-141 and the
+ * regrouping by local expert at :224-231.                                             */
+SMOE_API size_t smoe_ep_regroup_workspace_size(int ws, int E_l);
+SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity, int64_t n_recv,
+                                  int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_src,
+                                  int32_t* recv_dst, void* workspace, size_t workspace_bytes,
+                                  smoe_stream_t stream);
+
+/* -------------------------------------------------------------------- whole layer
+ * One-GPU MoE forward: router -> plan -> permute -> expert FFN -> combine (+ shared
+ * expert).  Replaces UltimateMoE.forward (models/ultimate_moe.py:254-342) and
+ * StandardMoE.forward (models/baseline_moe.py:191-213) at world size 1.             */
+typedef struct smoe_layer_args {
+  int32_t tokens, d_model, num_experts, top_k;
+  int32_t expert_type; /* SMOE_EXPERT_*                                              */
+  int32_t d_ff;        /* SwiGLU hidden size (ignored for linear)                    */
+  int32_t dtype;       /* SMOE_F32 / SMOE_F16 / SMOE_BF16                             */
+  int32_t capacity;    /* rows per expert, <= 0 = unlimited                           */
+  int32_t num_shared;  /* 0 or 1 always-on SwiGLU shared expert                       */
+  int32_t d_ff_shared;
+  const void* x;          /* [T, d]                                                   */
+  const void* gate_w;     /* [E, d]                                                   */
+  const float* logit_bias; /* [E] or NULL                                              */
+  const void* w1;         /* SwiGLU [E, F, d]                                          */
+  const void* w3;         /* SwiGLU [E, F, d]                                          */
+  const void* w2;         /* SwiGLU [E, d, F]                                          */
+  const void* w_lin;      /* linear [E, d_out, d_in]                                   */
+  const void* sw1;        /* shared [F_s, d]                                           */
+  const void* sw3;        /* shared [F_s, d]                                           */
+  const void* sw2;        /* shared [d, F_s]                                           */
+  void* out;              /* [T, d]                                                    */
+  int32_t* topk_idx;      /* optional [T, k] output (NULL: kept in workspace)          */
+  float* topk_w;          /* optional [T, k] output                                    */
+  int32_t* expert_counts; /* optional [E] output                                       */
+  void* workspace;
+  size_t workspace_bytes;
+  /* Optional cudaEvent_t handles (from smoe_event_create) recorded on the stream at the
+   * stage boundaries: [0] start, [1] router done, [2] dispatch plan + permute done,
+   * [3] expert GEMM 1 done, [4] expert GEMM 2 + shared expert done, [5] combine done.
+   * NULL entries are skipped.                                                          */
+  void* stage_events[6];
+} smoe_layer_args;
+
+/* Timing events usable in smoe_layer_args.stage_events (cudaEventDefault flags).
+ * smoe_event_elapsed waits for `end` and returns the milliseconds between the two.   */
+SMOE_API int smoe_event_create(void** event);
+SMOE_API int smoe_event_destroy(void* event);
+SMOE_API int smoe_event_record(void* event, smoe_stream_t stream);
+SMOE_API int smoe_event_elapsed(void* start, void* end, float* ms);
+
+SMOE_API size_t smoe_layer_workspace_size(const smoe_layer_args* a);
+SMOE_API int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SWIFTMOE_H_ */

@@ -1,0 +1,277 @@
+"""Shared forward machinery of the drop-in MoE modules.
+
+The forward is the reference's route -> dispatch -> experts -> combine pipeline
+(models/ultimate_moe.py:254-342, models/baseline_moe.py:191-213) executed by
+libswiftmoe:
+
+* world size 1, no profiling: ONE C-ABI call (``smoe_layer_fwd``) that enqueues the
+  router, dispatch plan, permute, grouped expert GEMMs and combine on the current
+  stream with no host synchronisation;
+* profiling or expert parallelism: the same kernels called stage by stage, with CUDA
+  events between the stages (read lazily, no synchronisation inside forward) and the
+  all-to-all exchange of ``ep.ExpertParallelExchange``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+from . import kernels as K
+
+STAGES = ("Router", "Dispatch_Comm", "Expert_Compute", "Combine_Comm")
+
+
+def resolve_dtype(use_fp16: bool, dtype) -> torch.dtype:
+    if dtype is None:
+        return torch.float16 if use_fp16 else torch.float32
+    if isinstance(dtype, str):
+        dtype = {"fp32": torch.float32, "float32": torch.float32, "fp16": torch.float16, "float16": torch.float16,
+                 "bf16": torch.bfloat16, "bfloat16": torch.bfloat16}[dtype]
+    if dtype not in L.DTYPE_CODE:
+        raise ValueError(f"unsupported dtype {dtype}")
+    return dtype
+
+
+def capacity_rows(capacity_factor: Optional[float], tokens_per_rank: int, world_size: int, k: int,
+                  num_experts: int) -> int:
+    """Per-expert capacity ``ceil(cf * T * ws * k / E)``; 0 means unlimited."""
+    if capacity_factor is None:
+        return 0
+    return int(math.ceil(capacity_factor * tokens_per_rank * world_size * k / num_experts))
+
+
+class _StageTimer:
+    """CUDA-event stage timing without host synchronisation inside forward."""
+
+    def __init__(self):
+        self.pending: List[tuple] = []
+        self.data: Dict[str, List[float]] = {s: [] for s in STAGES}
+        self.data["Exposed_A2A"] = []
+
+    def mark(self, device) -> torch.cuda.Event:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(device))
+        return ev
+
+    def add(self, events: List[torch.cuda.Event], exposed_a2a: Optional[tuple] = None):
+        self.pending.append(("torch", events, exposed_a2a))
+
+    def add_library(self, ev: "L.StageEvents"):
+        """Events recorded inside smoe_layer_fwd: start, router, dispatch, gemm1, gemm2, combine."""
+        self.pending.append(("lib", ev, None))
+
+    def flush(self):
+        for kind, events, a2a in self.pending:
+            if kind == "lib":
+                spans = [(0, 1), (1, 2), (2, 4), (4, 5)]
+                for name, (i, j) in zip(STAGES, spans):
+                    self.data[name].append(events.elapsed(i, j))
+                continue
+            events[-1].synchronize()
+            for name, a, b in zip(STAGES, events[:-1], events[1:]):
+                self.data[name].append(a.elapsed_time(b))
+            if a2a is not None:
+                self.data["Exposed_A2A"].append(sum(s.elapsed_time(e) for s, e in a2a))
+        self.pending.clear()
+
+
+class MoECore(nn.Module):
+    """Base class; subclasses provide the parameter accessors."""
+
+    # ---- filled by subclasses
+    num_experts: int
+    d_model: int
+    top_k: int
+    expert_type: str
+    d_ff: int
+    ws: int
+    exp_per_rank: int
+    capacity_factor: Optional[float]
+    num_shared_experts: int
+    d_ff_shared: int
+    compute_dtype: torch.dtype
+
+    def _init_core(self, enable_profiling: bool):
+        self.enable_profiling = enable_profiling
+        self._timer = _StageTimer()
+        self._ws_buf: Optional[torch.Tensor] = None
+        self._wcache: Dict[str, tuple] = {}
+        self.comm = None
+
+    # ------------------------------------------------------------ accessors
+    def _gate(self) -> torch.Tensor:
+        raise NotImplementedError
+
+    def _linear_kmajor(self) -> torch.Tensor:
+        """Linear expert weights as [E_l, d_out, d_in] (K contiguous)."""
+        raise NotImplementedError
+
+    def _swiglu(self):
+        raise NotImplementedError
+
+    def _shared(self):
+        return None
+
+    def _logit_bias(self) -> Optional[torch.Tensor]:
+        b = getattr(self, "logit_bias", None)
+        if b is None:
+            return None
+        return b.float().contiguous() if (b.dtype != torch.float32 or not b.is_contiguous()) else b
+
+    def _cached(self, key: str, sources: List[torch.Tensor], build):
+        sig = tuple((t.data_ptr(), t._version, t.device) for t in sources)
+        hit = self._wcache.get(key)
+        if hit is not None and hit[0] == sig:
+            return hit[1]
+        val = build()
+        self._wcache[key] = (sig, val)
+        return val
+
+    def _workspace(self, nbytes: int, device) -> torch.Tensor:
+        if self._ws_buf is None or self._ws_buf.numel() < nbytes or self._ws_buf.device != device:
+            self._ws_buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        return self._ws_buf
+
+    # ------------------------------------------------------------ forward
+    def _prepare_input(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() != 2 or x.shape[1] != self.d_model:
+            raise ValueError(f"expected x of shape [M, {self.d_model}], got {tuple(x.shape)}")
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        if not x.is_cuda:
+            raise L.SwiftMoEError("swiftmoe_b200 runs on CUDA devices only (no CPU fallback); move the module "
+                                  "and the input to a GPU")
+        return x.contiguous()
+
+    def _capacity(self, T: int) -> int:
+        return capacity_rows(self.capacity_factor, T, self.ws, self.top_k, self.num_experts)
+
+    _force_staged = False   # tests: run the stage-by-stage path at world size 1 too
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = self._prepare_input(x)
+        if self.ws == 1 and not self._force_staged:
+            ev = None
+            if self.enable_profiling:
+                ev = L.StageEvents()
+                self._timer.add_library(ev)
+            return self._forward_fused(x, ev)
+        return self._forward_staged(x)
+
+    def _layer_args(self, x: torch.Tensor, out: torch.Tensor) -> L.LayerArgs:
+        a = L.LayerArgs()
+        T = x.shape[0]
+        a.tokens, a.d_model, a.num_experts, a.top_k = T, self.d_model, self.num_experts, self.top_k
+        a.dtype = L.dtype_code(self.compute_dtype)
+        a.capacity = self._capacity(T)
+        a.x, a.gate_w, a.out = x.data_ptr(), self._gate().data_ptr(), out.data_ptr()
+        bias = self._logit_bias()
+        a.logit_bias = bias.data_ptr() if bias is not None else None
+        keep = [bias]
+        if self.expert_type == "swiglu":
+            w1, w3, w2 = self._swiglu()
+            a.expert_type, a.d_ff = L.SMOE_EXPERT_SWIGLU, self.d_ff
+            a.w1, a.w3, a.w2 = w1.data_ptr(), w3.data_ptr(), w2.data_ptr()
+            keep += [w1, w3, w2]
+        else:
+            wl = self._linear_kmajor()
+            a.expert_type, a.d_ff = L.SMOE_EXPERT_LINEAR, 0
+            a.w_lin = wl.data_ptr()
+            keep.append(wl)
+        sh = self._shared()
+        if sh is not None:
+            s1, s3, s2 = sh
+            a.num_shared, a.d_ff_shared = 1, s1.shape[0]
+            a.sw1, a.sw3, a.sw2 = s1.data_ptr(), s3.data_ptr(), s2.data_ptr()
+            keep += [s1, s3, s2]
+        self._keep_alive = keep
+        return a
+
+    def _forward_fused(self, x: torch.Tensor, events: Optional["L.StageEvents"] = None,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        lib = L.load()
+        if out is None:
+            out = torch.empty_like(x)
+        a = self._layer_args(x, out)
+        need = lib.smoe_layer_workspace_size(C.byref(a))
+        ws = self._workspace(need, x.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        if events is not None:
+            events.attach(a)
+        L.check(lib.smoe_layer_fwd(C.byref(a), L.stream_handle(x.device)), "smoe_layer_fwd")
+        return out
+
+    def _experts(self, xe: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+        if self.expert_type == "swiglu":
+            w1, w3, w2 = self._swiglu()
+            h = K.grouped_gemm(xe, w1, offsets, B3=w3, epilogue=L.SMOE_EPI_SWIGLU)
+            return K.grouped_gemm(h, w2, offsets)
+        return K.grouped_gemm(xe, self._linear_kmajor(), offsets)
+
+    def _shared_out(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+        sh = self._shared()
+        if sh is None:
+            return None
+        s1, s3, s2 = sh
+        T = x.shape[0]
+        soff = torch.tensor([0, T], dtype=torch.int32).to(x.device, non_blocking=True)
+        hs = K.grouped_gemm(x, s1.unsqueeze(0), soff, B3=s3.unsqueeze(0), epilogue=L.SMOE_EPI_SWIGLU)
+        return K.grouped_gemm(hs, s2.unsqueeze(0), soff)
+
+    def _forward_staged(self, x: torch.Tensor) -> torch.Tensor:
+        prof = self.enable_profiling
+        dev = x.device
+        T = x.shape[0]
+        ev = [self._timer.mark(dev)] if prof else None
+        idx, w = K.router(x, self._gate(), self.top_k, self._logit_bias())
+        if prof:
+            ev.append(self._timer.mark(dev))
+        a2a = None
+        if self.ws == 1:
+            plan = K.dispatch_plan(idx, self.num_experts, self._capacity(T))
+            xe = K.permute_rows(x, plan["row_token"], plan["offsets"], plan["rows_cap"])
+            offsets = plan["offsets"]
+        else:
+            xe, offsets, st = self.comm.dispatch(x, idx, self._capacity(T))
+        if prof:
+            ev.append(self._timer.mark(dev))
+        y = self._experts(xe, offsets)
+        shared = self._shared_out(x)
+        if prof:
+            ev.append(self._timer.mark(dev))
+        if self.ws == 1:
+            out = K.combine(y, plan["slot_row"], w, T, self.top_k, shared=shared)
+        else:
+            out = self.comm.combine(y, st, w, shared=shared)
+        if prof:
+            ev.append(self._timer.mark(dev))
+            if self.ws > 1:
+                # the exchange runs on the compute stream, so all of it is exposed
+                a2a = [(ev[1], ev[2]), (ev[3], ev[4])]
+            self._timer.add(ev, a2a)
+        return out
+
+    # ------------------------------------------------------------ profiling API
+    def get_profile_summary(self) -> Dict[str, float]:
+        """Mean milliseconds per stage (models/ultimate_moe.py:344-352) + Exposed_A2A."""
+        self._timer.flush()
+        out = {}
+        for k_, v in self._timer.data.items():
+            out[k_] = float(sum(v) / len(v)) if v else 0.0
+        return out
+
+    def reset_profiling(self):
+        """models/ultimate_moe.py:354-357."""
+        self._timer.flush()
+        for v in self._timer.data.values():
+            v.clear()
+
+    @property
+    def profile_data(self):
+        self._timer.flush()
+        return self._timer.data

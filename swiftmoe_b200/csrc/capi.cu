@@ -1,0 +1,645 @@
+// libswiftmoe.so: the C ABI declared in include/swiftmoe.h.
+//
+// Single translation unit: the kernels live in the *.cuh files included below so that
+// one device-side error word is shared by all of them without relocatable device code.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "dispatch.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "router.cuh"
+
+using namespace smoe;
+
+namespace {
+
+#define SMOE_CK(expr)                                   \
+  do {                                                  \
+    cudaError_t e_ = (expr);                            \
+    if (e_ != cudaSuccess) {                            \
+      report_cuda_error(e_, #expr, __FILE__, __LINE__); \
+      return SMOE_ERR_CUDA;                             \
+    }                                                   \
+  } while (0)
+
+void report_cuda_error(cudaError_t e, const char* what, const char* file, int line) {
+  if (getenv("SMOE_VERBOSE")) fprintf(stderr, "swiftmoe: %s failed: %s (%s:%d)\n", what, cudaGetErrorString(e), file, line);
+}
+
+inline int elt_size(int dtype) {
+  switch (dtype) {
+    case SMOE_F32: return 4;
+    case SMOE_F16:
+    case SMOE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+constexpr int kMaxDevices = 64;
+
+int device_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  static int cache[kMaxDevices] = {0};
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// Raise a kernel's dynamic shared-memory limit once per device.
+template <typename K>
+cudaError_t ensure_smem(K kernel, int bytes, unsigned long long* done_mask) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (*done_mask & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) *done_mask |= bit;
+  return e;
+}
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a row-major [rows, K] 16-bit matrix; box = 64 (K) x 128 rows, 128 B swizzle.
+bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t rows, int64_t K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D map over [G, N, K] weights; box = 64 (K) x 128 (N) x 1 group.
+bool make_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t G, int64_t N, int64_t K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, (cuuint64_t)G};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+__global__ void fill_two_kernel(int32_t* p, int32_t a, int32_t b) {
+  p[0] = a;
+  p[1] = b;
+}
+
+// ------------------------------------------------------------------ grouped GEMM
+template <int EPI, typename OutT>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
+              const int32_t* offsets, int G, int64_t rows_cap, int N, int K, uint32_t idesc, cudaStream_t st) {
+  static unsigned long long done = 0;
+  auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
+  SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
+  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, G, N,
+                                                         K, (int)rows_cap, idesc);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
+                      const int32_t* offsets, int G, int64_t rows_cap, int N, int K, cudaStream_t st) {
+  if (!A || !B || !C || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
+  if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU) return SMOE_ERR_INVALID;
+  if (epi == SMOE_EPI_SWIGLU && !B3) return SMOE_ERR_INVALID;
+  if (elt_size(dtype) == 0 || elt_size(out_dtype) == 0) return SMOE_ERR_INVALID;
+  if (rows_cap == 0) return SMOE_OK;
+  if (rows_cap > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
+  if (dtype == SMOE_F32) {
+    if (out_dtype != SMOE_F32 || G > simt::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
+    dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, 32) : cdiv(N, simt::BN)));
+    if (epi == SMOE_EPI_SWIGLU)
+      simt::grouped_gemm_f32_kernel<SMOE_EPI_SWIGLU><<<grid, simt::THREADS, 0, st>>>(
+          (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, offsets, G, N, K, (int)rows_cap);
+    else
+      simt::grouped_gemm_f32_kernel<SMOE_EPI_STORE><<<grid, simt::THREADS, 0, st>>>(
+          (const float*)A, (const float*)B, nullptr, (float*)C, N, offsets, G, N, K, (int)rows_cap);
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
+  // 16-bit inputs on tensor cores
+  if (G > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
+  if (K % 8 != 0 || N % 8 != 0) return SMOE_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (B3 && !aligned16(B3))) return SMOE_ERR_UNSUPPORTED;
+  if (epi == SMOE_EPI_SWIGLU && out_dtype != dtype) return SMOE_ERR_UNSUPPORTED;
+  if (out_dtype != SMOE_F32 && out_dtype != dtype) return SMOE_ERR_UNSUPPORTED;
+  const CUtensorMapDataType dt = dtype == SMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mb, mb3;
+  if (!make_map_2d(&ma, A, dt, rows_cap, K)) return SMOE_ERR_CUDA;
+  if (!make_map_3d(&mb, B, dt, G, N, K)) return SMOE_ERR_CUDA;
+  if (epi == SMOE_EPI_SWIGLU) {
+    if (!make_map_3d(&mb3, B3, dt, G, N, K)) return SMOE_ERR_CUDA;
+  } else {
+    mb3 = mb;
+  }
+  const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
+  if (epi == SMOE_EPI_SWIGLU) {
+    return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st)
+                              : launch_tc<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
+  }
+  if (out_dtype == SMOE_F32) return launch_tc<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
+  return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st)
+                            : launch_tc<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
+}
+
+// ------------------------------------------------------------------ router
+enum RouterPath { kRouterSmall, kRouterGemm, kRouterGeneric };
+
+RouterPath router_path(int d, int E, int dtype) {
+  const size_t smem = (size_t)E * d * elt_size(dtype);
+  if (E <= 32 && smem <= 200 * 1024) return kRouterSmall;
+  if (dtype == SMOE_F32) return kRouterGemm;
+  if (E % 8 == 0 && d % 8 == 0) return kRouterGemm;
+  return kRouterGeneric;
+}
+
+template <typename T, int EMAX, int TOK, int VEC>
+int launch_router_small(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
+                        float* w, float* logits, cudaStream_t st) {
+  static unsigned long long done = 0;
+  auto kern = router_small_kernel<T, EMAX, TOK, VEC>;
+  const int smem = E * d * (int)sizeof(T);
+  SMOE_CK(ensure_smem(kern, std::max(smem, 1), &done));
+  int per_sm = 1;
+  SMOE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
+  per_sm = std::max(per_sm, 1);
+  const int64_t groups = cdiv(T_, TOK);
+  const int64_t want = cdiv(groups, 8);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)device_sms() * per_sm));
+  kern<<<grid, 256, smem, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w, logits);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+template <typename T, int VEC>
+int router_small_dispatch_e(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k,
+                            int32_t* idx, float* w, float* logits, cudaStream_t st) {
+  if (E <= 8) return launch_router_small<T, 8, 4, VEC>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+  if (E <= 16) return launch_router_small<T, 16, 2, VEC>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+  return launch_router_small<T, 32, 1, VEC>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+}
+
+template <typename T>
+int router_small_dispatch(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
+                          float* w, float* logits, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  if (d % V == 0 && aligned16(x) && aligned16(wg))
+    return router_small_dispatch_e<T, V>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+  return router_small_dispatch_e<T, 1>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+}
+
+// Generic fallback router kernel for shapes the other two paths do not take
+// (16-bit, E > 32 with E or d not a multiple of 8): one warp per token, one dot
+// product per expert, fp32 logits into the workspace.
+template <typename T>
+__global__ void __launch_bounds__(256) router_logits_generic_kernel(const T* __restrict__ x, const T* __restrict__ wg,
+                                                                    int T_, int d, int E, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T_) return;
+  for (int e = 0; e < E; ++e) {
+    float s = 0.f;
+    for (int i = lane; i < d; i += 32) s = fmaf(Num<T>::to_f(x[(size_t)t * d + i]), Num<T>::to_f(wg[(size_t)e * d + i]), s);
+    s = warp_sum(s);
+    if (lane == 0) logits[(size_t)t * E + e] = s;
+  }
+}
+
+}  // namespace
+
+// =============================================================================== C ABI
+extern "C" {
+
+const char* smoe_version(void) { return "swiftmoe-b200 0.1 (sm_100a)"; }
+
+const char* smoe_status_string(int s) {
+  switch (s) {
+    case SMOE_OK: return "ok";
+    case SMOE_ERR_INVALID: return "invalid argument";
+    case SMOE_ERR_CUDA: return "CUDA error";
+    case SMOE_ERR_TIMEOUT: return "device wait timed out";
+    case SMOE_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case SMOE_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int smoe_device_sm_count(void) { return device_sms(); }
+
+int smoe_read_device_error(int* flag, smoe_stream_t stream) {
+  if (!flag) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaStreamSynchronize((cudaStream_t)stream));
+  int v = 0;
+  SMOE_CK(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  const int zero = 0;
+  SMOE_CK(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  *flag = v;
+  return SMOE_OK;
+}
+
+size_t smoe_router_workspace_size(int T, int d, int E, int dtype) {
+  if (T <= 0 || E <= 0 || elt_size(dtype) == 0) return 0;
+  if (router_path(d, E, dtype) == kRouterSmall) return 0;
+  return align_up((size_t)T * E * sizeof(float), 256) + 256;
+}
+
+int smoe_router_fwd(const void* x, const void* wg, int dtype, const float* logit_bias, int T, int d, int E, int k,
+                    int32_t* idx, float* w, float* logits_out, void* workspace, size_t workspace_bytes,
+                    smoe_stream_t stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (T < 0 || d < 1 || E < 1 || k < 1 || k > E || k > 32 || E > 32 * 32 || elt_size(dtype) == 0)
+    return SMOE_ERR_INVALID;
+  if (T == 0) return SMOE_OK;
+  if (!x || !wg || !idx || !w) return SMOE_ERR_INVALID;
+  const RouterPath path = router_path(d, E, dtype);
+  if (path == kRouterSmall) {
+    switch (dtype) {
+      case SMOE_F32: return router_small_dispatch<float>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st);
+      case SMOE_F16: return router_small_dispatch<__half>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st);
+      default: return router_small_dispatch<__nv_bfloat16>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st);
+    }
+  }
+  // logits through a GEMM (or the generic kernel), then top-k
+  float* logits = logits_out;
+  int32_t* offs = nullptr;
+  const size_t need = smoe_router_workspace_size(T, d, E, dtype);
+  if (!workspace || workspace_bytes < need) return SMOE_ERR_WORKSPACE;
+  unsigned char* wsb = static_cast<unsigned char*>(workspace);
+  if (!logits) logits = reinterpret_cast<float*>(wsb);
+  offs = reinterpret_cast<int32_t*>(wsb + align_up((size_t)T * E * sizeof(float), 256));
+  if (path == kRouterGemm) {
+    fill_two_kernel<<<1, 1, 0, st>>>(offs, 0, T);
+    SMOE_CK(cudaGetLastError());
+    const int rc = grouped_gemm_impl(x, wg, nullptr, logits, dtype, SMOE_F32, SMOE_EPI_STORE, offs, 1, T, E, d, st);
+    if (rc != SMOE_OK) return rc;
+  } else {
+    const unsigned grid = (unsigned)cdiv(T, 8);
+    if (dtype == SMOE_F16)
+      router_logits_generic_kernel<__half><<<grid, 256, 0, st>>>((const __half*)x, (const __half*)wg, T, d, E, logits);
+    else
+      router_logits_generic_kernel<__nv_bfloat16>
+          <<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)wg, T, d, E, logits);
+    SMOE_CK(cudaGetLastError());
+  }
+  topk_from_logits_kernel<<<(unsigned)cdiv(T, 8), 256, 0, st>>>(logits, logit_bias, T, E, k, idx, w);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_topk_from_logits(const float* logits, int T, int E, int k, int32_t* idx, float* w, smoe_stream_t stream) {
+  if (T < 0 || E < 1 || k < 1 || k > E || k > 32 || E > 32 * 32) return SMOE_ERR_INVALID;
+  if (T == 0) return SMOE_OK;
+  if (!logits || !idx || !w) return SMOE_ERR_INVALID;
+  topk_from_logits_kernel<<<(unsigned)cdiv(T, 8), 256, 0, (cudaStream_t)stream>>>(logits, nullptr, T, E, k, idx, w);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+// ------------------------------------------------------------------ dispatch plan
+size_t smoe_plan_workspace_size(int T, int k, int E) {
+  if (T < 0 || k < 1 || E < 1) return 0;
+  const int64_t nb = std::max<int64_t>(1, cdiv((int64_t)T * k, kPlanChunk));
+  return 2 * align_up((size_t)nb * E * sizeof(int32_t), 256);
+}
+
+int64_t smoe_plan_rows_cap(int T, int k, int E, int capacity, int row_align) {
+  if (T < 0 || k < 1 || E < 1 || row_align < 1) return 0;
+  int64_t kept = (int64_t)T * k;
+  if (capacity > 0) kept = std::min<int64_t>(kept, (int64_t)capacity * E);
+  return kept + (int64_t)E * (row_align - 1);
+}
+
+int smoe_dispatch_plan(const int32_t* idx, int T, int k, int E, int capacity, int row_align, int32_t* expert_counts,
+                       int32_t* expert_offsets, int32_t* slot_row, int32_t* row_token, int64_t rows_cap,
+                       void* workspace, size_t workspace_bytes, smoe_stream_t stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (T < 0 || k < 1 || E < 1 || E > 4096 || row_align < 1 || row_align > 1024) return SMOE_ERR_INVALID;
+  if (!expert_counts || !expert_offsets) return SMOE_ERR_INVALID;
+  if (rows_cap < smoe_plan_rows_cap(T, k, E, capacity, row_align)) return SMOE_ERR_INVALID;
+  if (T > 0 && (!idx || !slot_row || !row_token)) return SMOE_ERR_INVALID;
+  const size_t need = smoe_plan_workspace_size(T, k, E);
+  if (!workspace || workspace_bytes < need) return SMOE_ERR_WORKSPACE;
+  const int64_t n_slots = (int64_t)T * k;
+  if (n_slots > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
+  const int nb = (int)std::max<int64_t>(1, cdiv(n_slots, kPlanChunk));
+  int32_t* hist = static_cast<int32_t*>(workspace);
+  int32_t* base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
+                                             align_up((size_t)nb * E * sizeof(int32_t), 256));
+  const int smem_w = kPlanWarps * E * (int)sizeof(int);
+  static unsigned long long done_c = 0, done_s = 0;
+  SMOE_CK(ensure_smem(plan_count_kernel, smem_w, &done_c));
+  SMOE_CK(ensure_smem(plan_scatter_kernel, smem_w, &done_s));
+  plan_count_kernel<<<nb, kPlanThreads, smem_w, st>>>(idx, n_slots, E, hist);
+  SMOE_CK(cudaGetLastError());
+  plan_scan_kernel<<<1, 1024, E * sizeof(int), st>>>(hist, nb, E, capacity, row_align, base, expert_counts,
+                                                     expert_offsets, row_token);
+  SMOE_CK(cudaGetLastError());
+  if (n_slots > 0) {
+    plan_scatter_kernel<<<nb, kPlanThreads, smem_w, st>>>(idx, n_slots, k, E, capacity, base, expert_offsets,
+                                                          slot_row, row_token);
+    SMOE_CK(cudaGetLastError());
+  }
+  return SMOE_OK;
+}
+
+int smoe_permute_rows(const void* x, int dtype, int T, int d, const int32_t* row_token, const int32_t* expert_offsets,
+                      int E, int64_t rows_cap, void* rows, smoe_stream_t stream) {
+  const int es = elt_size(dtype);
+  if (es == 0 || T < 0 || d < 1 || E < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!row_token || !expert_offsets || !rows || (T > 0 && !x)) return SMOE_ERR_INVALID;
+  const int64_t row_bytes = (int64_t)d * es;
+  const bool vec = row_bytes % 16 == 0 && aligned16(x) && aligned16(rows);
+  const int64_t blocks = std::min<int64_t>(cdiv(rows_cap, 8), (int64_t)device_sms() * 16);
+  permute_rows_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const unsigned char*>(x), row_bytes, vec, row_token, expert_offsets, E,
+      static_cast<unsigned char*>(rows));
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_combine(const void* y, int dtype, const int32_t* slot_row, const float* w, int T, int k, int d,
+                 const void* shared, void* out, smoe_stream_t stream) {
+  const int es = elt_size(dtype);
+  if (es == 0 || T < 0 || k < 1 || d < 1) return SMOE_ERR_INVALID;
+  if (T == 0) return SMOE_OK;
+  if (!slot_row || !w || !out || !y) return SMOE_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int V = 16 / es;
+  const bool vec = d % V == 0 && aligned16(y) && aligned16(out) && (!shared || aligned16(shared));
+  const int64_t items = (int64_t)T * (vec ? d / V : d);
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(items, 256), (int64_t)device_sms() * 32);
+#define SMOE_COMBINE(TY, VV)                                                                                  \
+  combine_kernel<TY, VV><<<grid, 256, 0, st>>>((const TY*)y, slot_row, w, T, k, d, (const TY*)shared, (TY*)out)
+  switch (dtype) {
+    case SMOE_F32:
+      if (vec) SMOE_COMBINE(float, 4); else SMOE_COMBINE(float, 1);
+      break;
+    case SMOE_F16:
+      if (vec) SMOE_COMBINE(__half, 8); else SMOE_COMBINE(__half, 1);
+      break;
+    default:
+      if (vec) SMOE_COMBINE(__nv_bfloat16, 8); else SMOE_COMBINE(__nv_bfloat16, 1);
+  }
+#undef SMOE_COMBINE
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epilogue,
+                      const int32_t* offsets, int G, int64_t rows_cap, int N, int K, smoe_stream_t stream) {
+  return grouped_gemm_impl(A, B, B3, C, dtype, out_dtype, epilogue, offsets, G, rows_cap, N, K, (cudaStream_t)stream);
+}
+
+int smoe_transpose_batched(const void* src, void* dst, int dtype, int G, int R, int C, smoe_stream_t stream) {
+  const int es = elt_size(dtype);
+  if (es == 0 || G < 0 || R < 0 || C < 0) return SMOE_ERR_INVALID;
+  if ((int64_t)G * R * C == 0) return SMOE_OK;
+  if (!src || !dst || src == dst) return SMOE_ERR_INVALID;
+  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(R, 32), (unsigned)G), block(32, 8);
+  if (es == 4)
+    transpose_batched_kernel<float><<<grid, block, 0, (cudaStream_t)stream>>>((const float*)src, (float*)dst, R, C);
+  else
+    transpose_batched_kernel<unsigned short>
+        <<<grid, block, 0, (cudaStream_t)stream>>>((const unsigned short*)src, (unsigned short*)dst, R, C);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_gather_rows(const void* src, int dtype, int d, const int32_t* index, int64_t n_rows, void* dst,
+                     smoe_stream_t stream) {
+  const int es = elt_size(dtype);
+  if (es == 0 || d < 1 || n_rows < 0) return SMOE_ERR_INVALID;
+  if (n_rows == 0) return SMOE_OK;
+  if (!src || !index || !dst) return SMOE_ERR_INVALID;
+  const int64_t row_bytes = (int64_t)d * es;
+  const bool vec = row_bytes % 16 == 0 && aligned16(src) && aligned16(dst);
+  const int64_t blocks = std::min<int64_t>(cdiv(n_rows, 8), (int64_t)device_sms() * 16);
+  gather_rows_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const unsigned char*>(src), row_bytes, vec, index, n_rows, static_cast<unsigned char*>(dst));
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+size_t smoe_ep_regroup_workspace_size(int ws, int E_l) {
+  if (ws < 1 || E_l < 1) return 0;
+  return 2 * align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256);
+}
+
+int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity, int64_t n_recv,
+                         int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_src, int32_t* recv_dst,
+                         void* workspace, size_t workspace_bytes, smoe_stream_t stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (ws < 1 || E_l < 1 || n_recv < 0 || n_recv > INT32_MAX || (int64_t)ws * E_l > (1 << 20)) return SMOE_ERR_INVALID;
+  if (!recv_counts || !expert_counts || !expert_offsets) return SMOE_ERR_INVALID;
+  if (n_recv > 0 && (!row_src || !recv_dst)) return SMOE_ERR_INVALID;
+  if (!workspace || workspace_bytes < smoe_ep_regroup_workspace_size(ws, E_l)) return SMOE_ERR_WORKSPACE;
+  int32_t* seg_start = static_cast<int32_t*>(workspace);
+  int32_t* src_base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
+                                                 align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256));
+  const int smem = (E_l + ws) * (int)sizeof(int);
+  static unsigned long long done = 0;
+  SMOE_CK(ensure_smem(ep_regroup_scan_kernel, smem, &done));
+  ep_regroup_scan_kernel<<<1, 1024, smem, st>>>(recv_counts, ws, E_l, capacity, expert_counts, expert_offsets,
+                                                seg_start, src_base);
+  SMOE_CK(cudaGetLastError());
+  if (n_recv > 0) {
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n_recv, 256), (int64_t)device_sms() * 8);
+    ep_regroup_rows_kernel<<<grid, 256, 0, st>>>(seg_start, src_base, expert_offsets, ws * E_l, E_l, capacity, n_recv,
+                                                 row_src, recv_dst);
+    SMOE_CK(cudaGetLastError());
+  }
+  return SMOE_OK;
+}
+
+// ------------------------------------------------------------------ whole layer
+namespace {
+struct LayerPlan {
+  size_t off_idx, off_w, off_counts, off_offsets, off_slot_row, off_row_token, off_plan_ws, off_router_ws, off_xrows,
+      off_h, off_y, off_hs, off_ys, off_soff, total;
+  size_t plan_ws, router_ws;
+  int64_t rows_cap;
+};
+
+bool layer_plan(const smoe_layer_args* a, LayerPlan* p) {
+  const int es = elt_size(a->dtype);
+  if (es == 0) return false;
+  const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k;
+  const int64_t F = a->expert_type == SMOE_EXPERT_SWIGLU ? a->d_ff : 0;
+  const int64_t Fs = a->num_shared > 0 ? a->d_ff_shared : 0;
+  p->rows_cap = smoe_plan_rows_cap((int)T, (int)k, (int)E, a->capacity, 1);
+  p->plan_ws = smoe_plan_workspace_size((int)T, (int)k, (int)E);
+  p->router_ws = smoe_router_workspace_size((int)T, (int)d, (int)E, a->dtype);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  p->off_idx = take(T * k * 4);
+  p->off_w = take(T * k * 4);
+  p->off_counts = take(E * 4);
+  p->off_offsets = take((E + 1) * 4);
+  p->off_slot_row = take(T * k * 4);
+  p->off_row_token = take(std::max<int64_t>(p->rows_cap, 1) * 4);
+  p->off_plan_ws = take(p->plan_ws);
+  p->off_router_ws = take(p->router_ws);
+  p->off_xrows = take(p->rows_cap * d * es);
+  p->off_h = take(p->rows_cap * F * es);
+  p->off_y = take(p->rows_cap * d * es);
+  p->off_hs = take(T * Fs * es);
+  p->off_ys = take(Fs > 0 ? T * d * es : 0);
+  p->off_soff = take(16);
+  p->total = o;
+  return true;
+}
+}  // namespace
+
+int smoe_event_create(void** event) {
+  if (!event) return SMOE_ERR_INVALID;
+  cudaEvent_t e;
+  SMOE_CK(cudaEventCreate(&e));
+  *event = e;
+  return SMOE_OK;
+}
+
+int smoe_event_destroy(void* event) {
+  if (!event) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaEventDestroy((cudaEvent_t)event));
+  return SMOE_OK;
+}
+
+int smoe_event_record(void* event, smoe_stream_t stream) {
+  if (!event) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
+  return SMOE_OK;
+}
+
+int smoe_event_elapsed(void* start, void* end, float* ms) {
+  if (!start || !end || !ms) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaEventSynchronize((cudaEvent_t)end));
+  SMOE_CK(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
+  return SMOE_OK;
+}
+
+size_t smoe_layer_workspace_size(const smoe_layer_args* a) {
+  LayerPlan p;
+  if (!a || !layer_plan(a, &p)) return 0;
+  return p.total;
+}
+
+int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
+  if (!a) return SMOE_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k;
+  if (T < 0 || d < 1 || E < 1 || k < 1 || k > E || elt_size(a->dtype) == 0) return SMOE_ERR_INVALID;
+  if (a->expert_type != SMOE_EXPERT_LINEAR && a->expert_type != SMOE_EXPERT_SWIGLU) return SMOE_ERR_INVALID;
+  if (a->expert_type == SMOE_EXPERT_SWIGLU && (a->d_ff < 1 || !a->w1 || !a->w3 || !a->w2)) return SMOE_ERR_INVALID;
+  if (a->expert_type == SMOE_EXPERT_LINEAR && !a->w_lin) return SMOE_ERR_INVALID;
+  if (a->num_shared < 0 || a->num_shared > 1) return SMOE_ERR_UNSUPPORTED;
+  if (a->num_shared == 1 && (a->d_ff_shared < 1 || !a->sw1 || !a->sw3 || !a->sw2)) return SMOE_ERR_INVALID;
+  if (!a->gate_w || !a->out || (T > 0 && !a->x)) return SMOE_ERR_INVALID;
+  LayerPlan p;
+  layer_plan(a, &p);
+  if (!a->workspace || a->workspace_bytes < p.total) return SMOE_ERR_WORKSPACE;
+  if (T == 0) {
+    for (int i = 0; i < 6; ++i)
+      if (a->stage_events[i]) SMOE_CK(cudaEventRecord((cudaEvent_t)a->stage_events[i], st));
+    return SMOE_OK;
+  }
+  unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+  int32_t* idx = a->topk_idx ? a->topk_idx : reinterpret_cast<int32_t*>(ws + p.off_idx);
+  float* w = a->topk_w ? a->topk_w : reinterpret_cast<float*>(ws + p.off_w);
+  int32_t* counts = a->expert_counts ? a->expert_counts : reinterpret_cast<int32_t*>(ws + p.off_counts);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + p.off_offsets);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + p.off_slot_row);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + p.off_row_token);
+  void* xrows = ws + p.off_xrows;
+  void* h = ws + p.off_h;
+  void* y = ws + p.off_y;
+  const int dt = a->dtype;
+  const int F = a->d_ff;
+  auto mark = [&](int i) -> int {
+    if (a->stage_events[i]) SMOE_CK(cudaEventRecord((cudaEvent_t)a->stage_events[i], st));
+    return SMOE_OK;
+  };
+  int rc;
+  if ((rc = mark(0))) return rc;
+  rc = smoe_router_fwd(a->x, a->gate_w, dt, a->logit_bias, T, d, E, k, idx, w, nullptr, ws + p.off_router_ws,
+                       p.router_ws, stream);
+  if (rc) return rc;
+  if ((rc = mark(1))) return rc;
+  rc = smoe_dispatch_plan(idx, T, k, E, a->capacity, 1, counts, offsets, slot_row, row_token, p.rows_cap,
+                          ws + p.off_plan_ws, p.plan_ws, stream);
+  if (rc) return rc;
+  rc = smoe_permute_rows(a->x, dt, T, d, row_token, offsets, E, p.rows_cap, xrows, stream);
+  if (rc) return rc;
+  if ((rc = mark(2))) return rc;
+  if (a->expert_type == SMOE_EXPERT_SWIGLU) {
+    rc = grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, E, p.rows_cap, F, d, st);
+    if (rc) return rc;
+    if ((rc = mark(3))) return rc;
+    rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, E, p.rows_cap, d, F, st);
+    if (rc) return rc;
+  } else {
+    rc = grouped_gemm_impl(xrows, a->w_lin, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, E, p.rows_cap, d, d, st);
+    if (rc) return rc;
+    if ((rc = mark(3))) return rc;
+  }
+  void* ys = nullptr;
+  if (a->num_shared == 1) {
+    int32_t* soff = reinterpret_cast<int32_t*>(ws + p.off_soff);
+    fill_two_kernel<<<1, 1, 0, st>>>(soff, 0, T);
+    SMOE_CK(cudaGetLastError());
+    void* hs = ws + p.off_hs;
+    ys = ws + p.off_ys;
+    rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, hs, dt, dt, SMOE_EPI_SWIGLU, soff, 1, T, a->d_ff_shared, d, st);
+    if (rc) return rc;
+    rc = grouped_gemm_impl(hs, a->sw2, nullptr, ys, dt, dt, SMOE_EPI_STORE, soff, 1, T, d, a->d_ff_shared, st);
+    if (rc) return rc;
+  }
+  if ((rc = mark(4))) return rc;
+  rc = smoe_combine(y, dt, slot_row, w, T, k, d, ys, a->out, stream);
+  if (rc) return rc;
+  return mark(5);
+}
+
+}  // extern "C"

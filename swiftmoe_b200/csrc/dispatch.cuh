@@ -1,0 +1,391 @@
+// Dispatch plan (histogram -> scan -> stable scatter), row permutation, combine and a
+// batched transpose.
+//
+// The reference groups the T*2 (token, slot) pairs by target rank with an unstable
+// argsort (models/ultimate_moe.py:120), replicates tokens with repeat_interleave
+// (:123) and groups again by local expert (:224-231).  Here the plan is built in one
+// pass over the routing indices: per-block histograms, a scan over (expert, block) and
+// a scatter that numbers the pairs of each expert in (token, slot) order using warp
+// match/ballot ranks, so the result is deterministic and bit-exact across runs.
+#pragma once
+#include "common.cuh"
+
+namespace smoe {
+
+constexpr int kPlanThreads = 256;                  // 8 warps
+constexpr int kPlanWarps = kPlanThreads / 32;
+constexpr int kPlanSlotsPerWarp = 256;             // 8 steps of 32 slots
+constexpr int kPlanChunk = kPlanWarps * kPlanSlotsPerWarp;  // slots per block
+
+// Per-warp counts of each expert over the warp's slot range; cnt is [kPlanWarps][E].
+__device__ __forceinline__ void plan_warp_counts(const int32_t* __restrict__ idx, int64_t n_slots, int E,
+                                                 int64_t slot0, int* cnt) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int* my = cnt + warp * E;
+  for (int step = 0; step < kPlanSlotsPerWarp / 32; ++step) {
+    const int64_t s = slot0 + warp * kPlanSlotsPerWarp + step * 32 + lane;
+    int e = -1;
+    if (s < n_slots) {
+      e = idx[s];
+      if (e < 0 || e >= E) {
+        set_device_error(kErrBadExpertIndex);
+        e = -1;
+      }
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) my[e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// Kernel 1: hist[b][e] = number of slots of block b routed to expert e.
+__global__ void __launch_bounds__(kPlanThreads) plan_count_kernel(const int32_t* __restrict__ idx, int64_t n_slots,
+                                                                  int E, int32_t* __restrict__ hist) {
+  extern __shared__ int cnt[];  // [kPlanWarps][E]
+  for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t slot0 = (int64_t)blockIdx.x * kPlanChunk;
+  plan_warp_counts(idx, n_slots, E, slot0, cnt);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int s = 0;
+    for (int w = 0; w < kPlanWarps; ++w) s += cnt[w * E + e];
+    hist[(size_t)blockIdx.x * E + e] = s;
+  }
+}
+
+// Kernel 2 (one block): per-expert running base over blocks, totals, capacity cut and
+// the exclusive scan of aligned kept counts into expert_offsets.
+__global__ void __launch_bounds__(1024) plan_scan_kernel(const int32_t* __restrict__ hist, int nblocks, int E,
+                                                         int capacity, int row_align, int32_t* __restrict__ base,
+                                                         int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                                                         int32_t* __restrict__ row_token) {
+  extern __shared__ int s_kept[];  // [E] aligned kept counts, then scanned in place
+  __shared__ int s_warp[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int b = 0; b < nblocks; ++b) {
+      base[(size_t)b * E + e] = run;
+      run += hist[(size_t)b * E + e];
+    }
+    counts[e] = run;
+    const int kept = capacity > 0 ? min(run, capacity) : run;
+    s_kept[e] = ((kept + row_align - 1) / row_align) * row_align;
+  }
+  __syncthreads();
+  // block-wide exclusive scan of s_kept[0..E): each thread owns a contiguous strip
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int lo = min(E, (int)threadIdx.x * per), hi = min(E, lo + per);
+  int local = 0;
+  for (int e = lo; e < hi; ++e) local += s_kept[e];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int v = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    if (lane < nw) s_warp[lane] = v;  // inclusive per-warp totals
+  }
+  __syncthreads();
+  int run = (incl - local) + (warp > 0 ? s_warp[warp - 1] : 0);
+  for (int e = lo; e < hi; ++e) {
+    const int a = s_kept[e];
+    offsets[e] = run;
+    run += a;
+  }
+  if (threadIdx.x == blockDim.x - 1) offsets[E] = run;  // last strip ends at the total
+  if (E == 0 && threadIdx.x == 0) offsets[0] = 0;
+  __syncthreads();
+  // alignment padding rows carry token -1
+  if (row_align > 1) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int kept = capacity > 0 ? min(counts[e], capacity) : counts[e];
+      for (int r = offsets[e] + kept; r < offsets[e + 1]; ++r) row_token[r] = -1;
+    }
+  }
+}
+
+// Kernel 3: stable scatter.  Slot s of expert e gets row offsets[e] + (number of
+// earlier slots of e); slots at or beyond the capacity are dropped (-1).
+__global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(const int32_t* __restrict__ idx, int64_t n_slots,
+                                                                    int k, int E, int capacity,
+                                                                    const int32_t* __restrict__ base,
+                                                                    const int32_t* __restrict__ offsets,
+                                                                    int32_t* __restrict__ slot_row,
+                                                                    int32_t* __restrict__ row_token) {
+  extern __shared__ int cnt[];  // [kPlanWarps][E], turned into per-warp running positions
+  for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t slot0 = (int64_t)blockIdx.x * kPlanChunk;
+  plan_warp_counts(idx, n_slots, E, slot0, cnt);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = base[(size_t)blockIdx.x * E + e];
+    for (int w = 0; w < kPlanWarps; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int* pos = cnt + warp * E;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int step = 0; step < kPlanSlotsPerWarp / 32; ++step) {
+    const int64_t s = slot0 + warp * kPlanSlotsPerWarp + step * 32 + lane;
+    int e = -1;
+    if (s < n_slots) {
+      e = idx[s];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int p = 0;
+    if (e >= 0) p = pos[e] + __popc(peers & lt);
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) pos[e] += __popc(peers);
+    __syncwarp();
+    if (s < n_slots) {
+      if (e < 0 || (capacity > 0 && p >= capacity)) {
+        slot_row[s] = -1;
+      } else {
+        const int row = offsets[e] + p;
+        slot_row[s] = row;
+        row_token[row] = (int32_t)(s / k);
+      }
+    }
+  }
+}
+
+// rows[r,:] = x[row_token[r],:] for r < offsets[E]; one warp per row, 16-byte vectors
+// when every row starts on a 16-byte boundary.
+__global__ void __launch_bounds__(256) permute_rows_kernel(const unsigned char* __restrict__ x, int64_t row_bytes,
+                                                           bool vec, const int32_t* __restrict__ row_token,
+                                                           const int32_t* __restrict__ offsets, int E,
+                                                           unsigned char* __restrict__ rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t total = offsets[E];
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total; r += warps) {
+    const int t = row_token[r];
+    unsigned char* dst = rows + r * row_bytes;
+    if (vec) {
+      const int nv = (int)(row_bytes >> 4);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      if (t >= 0) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
+        for (int i = lane; i < nv; i += 32) d4[i] = s4[i];
+      } else {
+        for (int i = lane; i < nv; i += 32) d4[i] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      const unsigned char* src = x + (int64_t)(t >= 0 ? t : 0) * row_bytes;
+      for (int64_t i = lane; i < row_bytes; i += 32) dst[i] = t >= 0 ? src[i] : 0;
+    }
+  }
+}
+
+// out[t, c..c+VEC) = sum_j w[t,j] * y[slot_row[t,j], c..] (+ shared[t, c..]).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ slot_row,
+                                                      const float* __restrict__ w, int T_, int k, int d,
+                                                      const T* __restrict__ shared, T* __restrict__ out) {
+  const int per_row = d / VEC;
+  const int64_t total = (int64_t)T_ * per_row;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(g / per_row);
+    const int c = (int)(g - (int64_t)t * per_row) * VEC;
+    float acc[VEC];
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) acc[q] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int r = slot_row[(size_t)t * k + j];
+      if (r < 0) continue;
+      const float wj = w[(size_t)t * k + j];
+      float v[VEC];
+      load_vec_f<T, VEC>(y + (size_t)r * d + c, v);
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+    }
+    if (shared != nullptr) {
+      float v[VEC];
+      load_vec_f<T, VEC>(shared + (size_t)t * d + c, v);
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) acc[q] += v[q];
+    }
+    if constexpr (VEC == 1) {
+      out[(size_t)t * d + c] = Num<T>::from_f(acc[0]);
+    } else {
+      union {
+        uint4 u;
+        T e[VEC];
+      } o;
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) o.e[q] = Num<T>::from_f(acc[q]);
+      *reinterpret_cast<uint4*>(out + (size_t)t * d + c) = o.u;
+    }
+  }
+}
+
+// dst[r,:] = src[index[r],:] for r < n_rows (zero rows where index is -1).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const unsigned char* __restrict__ src, int64_t row_bytes,
+                                                          bool vec, const int32_t* __restrict__ index, int64_t n_rows,
+                                                          unsigned char* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows; r += warps) {
+    const int i = index[r];
+    unsigned char* o = dst + r * row_bytes;
+    if (vec) {
+      const int nv = (int)(row_bytes >> 4);
+      uint4* o4 = reinterpret_cast<uint4*>(o);
+      if (i >= 0) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src + (int64_t)i * row_bytes);
+        for (int j = lane; j < nv; j += 32) o4[j] = s4[j];
+      } else {
+        for (int j = lane; j < nv; j += 32) o4[j] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      const unsigned char* s = src + (int64_t)(i >= 0 ? i : 0) * row_bytes;
+      for (int64_t j = lane; j < row_bytes; j += 32) o[j] = i >= 0 ? s[j] : 0;
+    }
+  }
+}
+
+// Block-wide exclusive scan of data[0..n) in shared memory (in place); returns the total
+// to every thread.  scratch holds 32 ints.
+__device__ int block_exclusive_scan(int* data, int n, int* scratch) {
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, (int)threadIdx.x * per), hi = min(n, lo + per);
+  int local = 0;
+  for (int e = lo; e < hi; ++e) local += data[e];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  __syncthreads();
+  if (lane == 31) scratch[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int v = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    if (lane < nw) scratch[lane] = v;
+  }
+  __syncthreads();
+  int run = (incl - local) + (warp > 0 ? scratch[warp - 1] : 0);
+  for (int e = lo; e < hi; ++e) {
+    const int a = data[e];
+    data[e] = run;
+    run += a;
+  }
+  const int total = scratch[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return total;
+}
+
+// Expert-parallel receive plan, part 1 (one block).  rc is recv_counts [ws][El].
+// Writes seg_start[ws*El+1] (receive row where segment (s, le) starts), src_base[ws*El]
+// (position inside expert le of the segment's first row), expert counts and offsets.
+__global__ void __launch_bounds__(1024) ep_regroup_scan_kernel(const int32_t* __restrict__ rc, int ws, int El,
+                                                               int capacity, int32_t* __restrict__ counts,
+                                                               int32_t* __restrict__ offsets,
+                                                               int32_t* __restrict__ seg_start,
+                                                               int32_t* __restrict__ src_base) {
+  extern __shared__ int sh[];  // [El] kept counts, then [ws] row totals
+  __shared__ int scratch[32];
+  int* s_kept = sh;
+  int* s_row = sh + El;
+  for (int le = threadIdx.x; le < El; le += blockDim.x) {
+    int run = 0;
+    for (int s = 0; s < ws; ++s) {
+      src_base[s * El + le] = run;
+      run += rc[s * El + le];
+    }
+    counts[le] = run;
+    s_kept[le] = capacity > 0 ? min(run, capacity) : run;
+  }
+  for (int s = threadIdx.x; s < ws; s += blockDim.x) {
+    int run = 0;
+    for (int le = 0; le < El; ++le) {
+      seg_start[s * El + le] = run;  // row-local prefix for now
+      run += rc[s * El + le];
+    }
+    s_row[s] = run;
+  }
+  __syncthreads();
+  const int kept_total = block_exclusive_scan(s_kept, El, scratch);
+  const int recv_total = block_exclusive_scan(s_row, ws, scratch);
+  for (int le = threadIdx.x; le < El; le += blockDim.x) offsets[le] = s_kept[le];
+  if (threadIdx.x == 0) {
+    offsets[El] = kept_total;
+    seg_start[ws * El] = recv_total;
+  }
+  for (int i = threadIdx.x; i < ws * El; i += blockDim.x) seg_start[i] += s_row[i / El];
+}
+
+// Part 2: one thread per received row.
+__global__ void __launch_bounds__(256) ep_regroup_rows_kernel(const int32_t* __restrict__ seg_start,
+                                                              const int32_t* __restrict__ src_base,
+                                                              const int32_t* __restrict__ offsets, int nseg, int El,
+                                                              int capacity, int64_t n_recv,
+                                                              int32_t* __restrict__ row_src,
+                                                              int32_t* __restrict__ recv_dst) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_recv; r += (int64_t)gridDim.x * blockDim.x) {
+    int lo = 0, hi = nseg - 1;  // last segment whose start <= r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seg_start[mid] <= r) lo = mid; else hi = mid - 1;
+    }
+    const int le = lo % El;
+    const int pos = src_base[lo] + (int)(r - seg_start[lo]);
+    if (capacity > 0 && pos >= capacity) {
+      recv_dst[r] = -1;
+    } else {
+      const int dst = offsets[le] + pos;
+      recv_dst[r] = dst;
+      row_src[dst] = (int32_t)r;
+    }
+  }
+}
+
+// dst[g][c][r] = src[g][r][c]; 32x32 tiles through shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_batched_kernel(const T* __restrict__ src, T* __restrict__ dst, int R,
+                                                                int C) {
+  __shared__ T tile[32][33];
+  const int g = blockIdx.z;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const T* s = src + (size_t)g * R * C;
+  T* o = dst + (size_t)g * R * C;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[i][threadIdx.x] = s[(size_t)r * C + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) o[(size_t)c * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+}  // namespace smoe

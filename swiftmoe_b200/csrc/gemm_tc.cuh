@@ -1,0 +1,293 @@
+// Grouped GEMM on the sm_100a 5th-generation tensor cores.
+//
+// Replaces the reference's per-expert host loop of torch.mm (models/ultimate_moe.py:237-250)
+// and the nn.Linear experts (models/baseline_moe.py:151-162) with ONE persistent kernel over
+// all experts' tiles:
+//   * tiles of 128 rows x 256 accumulator columns, K in steps of 64 (one 128-byte swizzle
+//     row of 16-bit elements);
+//   * warp 0: one thread issues TMA loads (A rows of the group, B rows of the group's
+//     weights through a 3-D tensor map so ragged N never reads the next expert) into a
+//     4-stage shared-memory ring guarded by mbarriers;
+//   * warp 1: one thread issues tcgen05.mma (M=128, N=256, K=16) into one of two TMEM
+//     accumulators (2 x 256 columns = all 512), committing each stage back to the
+//     producer and each finished tile to the epilogue;
+//   * warps 2-5: read the accumulator with tcgen05.ld, apply the epilogue (plain store,
+//     or SwiGLU silu(gate) * up on the fused [gate | up] halves of the tile) and store to
+//     global memory while the tensor cores already work on the next tile.
+// Every mbarrier wait is bounded (see mbar_wait); on a timeout the kernel records the
+// error, drains its in-flight copies and MMAs and frees its TMEM before returning.
+#pragma once
+#include "common.cuh"
+
+namespace smoe {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int BN = 256;  // accumulator columns per tile
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int MAX_GROUPS = 1024;
+constexpr int GM = 16;  // m-tiles per rasterisation band
+constexpr int NUM_BARS = 2 * STAGES + 5;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 2 * (MAX_GROUPS + 1) * 4;
+constexpr uint64_t kDrainLimitNs = 200000000ull;  // 200 ms
+
+// Wait used while draining on the way out: ignores the error word, bounded by time.
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kDrainLimitNs) {
+      set_device_error(kErrWaitTimeout);
+      return;
+    }
+  }
+}
+
+struct TileCoord {
+  int g, row0, rows_valid, nb;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(int L, const int* s_ts, const int* s_off, int G, int NB) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_ts[mid] <= L) lo = mid; else hi = mid - 1;
+  }
+  TileCoord t;
+  t.g = lo;
+  const int local = L - s_ts[lo];
+  const int rows = s_off[lo + 1] - s_off[lo];
+  const int mt_g = (rows + BM - 1) / BM;
+  const int band = local / (GM * NB);
+  const int m_first = band * GM;
+  const int gm = min(mt_g - m_first, GM);
+  const int r = local - band * GM * NB;
+  const int mt = m_first + r % gm;
+  t.nb = r / gm;
+  t.row0 = s_off[lo] + mt * BM;
+  t.rows_valid = min(BM, s_off[lo + 1] - t.row0);
+  return t;
+}
+
+template <typename OutT> struct Store;
+template <> struct Store<float> {
+  // 32 fp32 columns starting at col0 (N % 4 == 0)
+  static __device__ __forceinline__ void cols32(float* row, int col0, int N, const uint32_t (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (col0 + 4 * j < N)
+        *reinterpret_cast<uint4*>(row + col0 + 4 * j) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+};
+template <typename H> struct Store16 {
+  static __device__ __forceinline__ void cols32(H* row, int col0, int N, const float (&f)[32]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (col0 + 8 * j < N) {
+        uint4 u;
+        u.x = pack2<H>(f[8 * j + 0], f[8 * j + 1]);
+        u.y = pack2<H>(f[8 * j + 2], f[8 * j + 3]);
+        u.z = pack2<H>(f[8 * j + 4], f[8 * j + 5]);
+        u.w = pack2<H>(f[8 * j + 6], f[8 * j + 7]);
+        *reinterpret_cast<uint4*>(row + col0 + 8 * j) = u;
+      }
+  }
+};
+
+// EPI: SMOE_EPI_STORE or SMOE_EPI_SWIGLU.  OutT: float, __nv_bfloat16 or __half.
+template <int EPI, typename OutT>
+__global__ void __launch_bounds__(THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
+                        const int32_t* __restrict__ offsets, int G, int N, int K, int rows_cap,
+                        uint32_t idesc) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
+  int* s_off = reinterpret_cast<int*>(s_tmem + 4);
+  int* s_ts = s_off + (MAX_GROUPS + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NB = (EPI == SMOE_EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
+  const int KB = (K + BK - 1) / BK;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+  const uint32_t mma_done_bar = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    // group boundaries, forced monotonic and inside [0, rows_cap] so that no tile can
+    // read or write past the row buffers whatever the caller passed
+    int prev = 0;
+    for (int i = 0; i <= G; ++i) {
+      prev = min(max(offsets[i], prev), rows_cap);
+      s_off[i] = prev;
+    }
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);  // one arrive per epilogue warp
+    }
+    mbar_init(mma_done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (EPI == SMOE_EPI_SWIGLU) tma_prefetch_desc(&tmB3);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(s_tmem), 2 * BN);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < G; ++g) {
+      s_ts[g] = acc;
+      acc += ((s_off[g + 1] - s_off[g] + BM - 1) / BM) * NB;
+    }
+    s_ts[G] = acc;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total = s_ts[G];
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
+        const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
+        const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1)) { ok = false; break; }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
+          tma_load_2d(a_dst, &tmA, fb, kb * BK, t.row0);
+          tma_load_3d(b_dst, &tmB, fb, kb * BK, n0, t.g);
+          if (EPI == SMOE_EPI_SWIGLU) tma_load_3d(b_dst + B_BYTES / 2, &tmB3, fb, kb * BK, n0, t.g);
+          else tma_load_3d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128, t.g);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: the last armed phase of every stage must have landed before exit
+      for (int s = 0; s < STAGES; ++s) {
+        const int64_t cnt = issued / STAGES + (s < issued % STAGES ? 1 : 0);
+        if (cnt > 0) mbar_wait_drain(full_bar(s), (uint32_t)((cnt - 1) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      umma_commit(mma_done_bar);
+      mbar_wait_drain(mma_done_bar, 0);
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int L = blockIdx.x; L < total; L += gridDim.x) {
+      const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
+      if (!mbar_wait(tfull_bar(acc), acc_phase)) break;
+      tc_fence_after();
+      const bool row_ok = r < t.rows_valid;
+      OutT* crow = C + (int64_t)(t.row0 + (row_ok ? r : 0)) * ldc;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (EPI == SMOE_EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t gv[32], uv[32];
+          tmem_ld32(tbase + c * 32, gv);
+          tmem_ld32(tbase + 128 + c * 32, uv);
+          tmem_ld_wait();
+          float h[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float g = __uint_as_float(gv[j]);
+            const float u = __uint_as_float(uv[j]);
+            h[j] = g / (1.0f + __expf(-g)) * u;
+          }
+          if (row_ok) Store16<OutT>::cols32(crow, t.nb * 128 + c * 32, N, h);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tbase + c * 32, v);
+          tmem_ld_wait();
+          if (row_ok) {
+            if constexpr (sizeof(OutT) == 4) {
+              Store<float>::cols32(reinterpret_cast<float*>(crow), t.nb * BN + c * 32, N, v);
+            } else {
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+              Store16<OutT>::cols32(crow, t.nb * BN + c * 32, N, f);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace tc
+}  // namespace smoe

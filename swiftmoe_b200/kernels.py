@@ -1,0 +1,164 @@
+"""Tensor-level wrappers over the C ABI.  Each function checks its tensors (CUDA,
+contiguous, dtype), allocates outputs with torch and calls exactly one libswiftmoe
+entry point on the current CUDA stream.  They never fall back to another
+implementation: a non-CUDA tensor or a failed call raises."""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise L.SwiftMoEError("swiftmoe_b200 kernels need CUDA tensors (no CPU fallback)")
+            if not t.is_contiguous():
+                raise L.SwiftMoEError("swiftmoe_b200 kernels need contiguous tensors")
+
+
+def _workspace(device, nbytes: int) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def router(x: torch.Tensor, gate_w: torch.Tensor, k: int, logit_bias: Optional[torch.Tensor] = None,
+           return_logits: bool = False):
+    """idx [T,k] int32, w [T,k] fp32 (and fp32 gate logits [T,E] before the offsets)."""
+    _need_cuda(x, gate_w, logit_bias)
+    T, d = x.shape
+    E = gate_w.shape[0]
+    if gate_w.dtype != x.dtype:
+        raise L.SwiftMoEError("gate weight dtype must match x")
+    lib = L.load()
+    dt = L.dtype_code(x.dtype)
+    idx = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    logits = torch.empty((T, E), dtype=torch.float32, device=x.device) if return_logits else None
+    ws = _workspace(x.device, lib.smoe_router_workspace_size(T, d, E, dt))
+    bias = logit_bias.float().contiguous() if logit_bias is not None else None
+    L.check(lib.smoe_router_fwd(L.ptr(x), L.ptr(gate_w), dt, L.ptr(bias), T, d, E, k, L.ptr(idx), L.ptr(w),
+                                L.ptr(logits), L.ptr(ws), ws.numel(), L.stream_handle(x.device)), "smoe_router_fwd")
+    return (idx, w, logits) if return_logits else (idx, w)
+
+
+def topk_from_logits(logits: torch.Tensor, k: int):
+    _need_cuda(logits)
+    if logits.dtype != torch.float32:
+        raise L.SwiftMoEError("logits must be float32")
+    T, E = logits.shape
+    idx = torch.empty((T, k), dtype=torch.int32, device=logits.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=logits.device)
+    L.check(L.load().smoe_topk_from_logits(L.ptr(logits), T, E, k, L.ptr(idx), L.ptr(w),
+                                           L.stream_handle(logits.device)), "smoe_topk_from_logits")
+    return idx, w
+
+
+def dispatch_plan(idx: torch.Tensor, num_experts: int, capacity: int = 0, row_align: int = 1):
+    """Returns dict(counts [E], offsets [E+1], slot_row [T*k], row_token [rows_cap], rows_cap)."""
+    _need_cuda(idx)
+    if idx.dtype != torch.int32:
+        raise L.SwiftMoEError("idx must be int32")
+    T, k = idx.shape
+    E = num_experts
+    lib = L.load()
+    rows_cap = int(lib.smoe_plan_rows_cap(T, k, E, capacity, row_align))
+    dev = idx.device
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    slot_row = torch.empty(T * k, dtype=torch.int32, device=dev)
+    row_token = torch.empty(max(rows_cap, 1), dtype=torch.int32, device=dev)
+    ws = _workspace(dev, lib.smoe_plan_workspace_size(T, k, E))
+    L.check(lib.smoe_dispatch_plan(L.ptr(idx), T, k, E, capacity, row_align, L.ptr(counts), L.ptr(offsets),
+                                   L.ptr(slot_row), L.ptr(row_token), max(rows_cap, 1), L.ptr(ws), ws.numel(),
+                                   L.stream_handle(dev)), "smoe_dispatch_plan")
+    return dict(counts=counts, offsets=offsets, slot_row=slot_row, row_token=row_token, rows_cap=rows_cap)
+
+
+def permute_rows(x: torch.Tensor, row_token: torch.Tensor, offsets: torch.Tensor, rows_cap: int,
+                 out: Optional[torch.Tensor] = None):
+    _need_cuda(x, row_token, offsets)
+    T, d = x.shape
+    E = offsets.numel() - 1
+    if out is None:
+        out = torch.empty((max(rows_cap, 1), d), dtype=x.dtype, device=x.device)
+    L.check(L.load().smoe_permute_rows(L.ptr(x), L.dtype_code(x.dtype), T, d, L.ptr(row_token), L.ptr(offsets), E,
+                                       rows_cap, L.ptr(out), L.stream_handle(x.device)), "smoe_permute_rows")
+    return out
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor, n_rows: int, out: Optional[torch.Tensor] = None):
+    _need_cuda(src, index)
+    d = src.shape[1]
+    if out is None:
+        out = torch.empty((max(n_rows, 1), d), dtype=src.dtype, device=src.device)
+    L.check(L.load().smoe_gather_rows(L.ptr(src), L.dtype_code(src.dtype), d, L.ptr(index), n_rows, L.ptr(out),
+                                      L.stream_handle(src.device)), "smoe_gather_rows")
+    return out
+
+
+def combine(y: torch.Tensor, slot_row: torch.Tensor, w: torch.Tensor, T: int, k: int,
+            shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
+    _need_cuda(y, slot_row, w, shared)
+    d = y.shape[1]
+    if out is None:
+        out = torch.empty((T, d), dtype=y.dtype, device=y.device)
+    L.check(L.load().smoe_combine(L.ptr(y), L.dtype_code(y.dtype), L.ptr(slot_row), L.ptr(w), T, k, d,
+                                  L.ptr(shared), L.ptr(out), L.stream_handle(y.device)), "smoe_combine")
+    return out
+
+
+def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, *, B3: Optional[torch.Tensor] = None,
+                 epilogue: int = L.SMOE_EPI_STORE, out_dtype: Optional[torch.dtype] = None,
+                 out: Optional[torch.Tensor] = None):
+    """C[rows_cap, N] for groups defined by device offsets [G+1]; B is [G, N, K]."""
+    _need_cuda(A, B, B3, offsets)
+    rows_cap, K = A.shape
+    G, N, K2 = B.shape
+    if K2 != K:
+        raise L.SwiftMoEError("K mismatch")
+    od = out_dtype or A.dtype
+    if out is None:
+        out = torch.empty((max(rows_cap, 1), N), dtype=od, device=A.device)
+    L.check(L.load().smoe_grouped_gemm(L.ptr(A), L.ptr(B), L.ptr(B3), L.ptr(out), L.dtype_code(A.dtype),
+                                       L.dtype_code(od), epilogue, L.ptr(offsets), G, rows_cap, N, K,
+                                       L.stream_handle(A.device)), "smoe_grouped_gemm")
+    return out
+
+
+def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
+    """[G, R, C] -> [G, C, R]."""
+    _need_cuda(src)
+    G, R, Cc = src.shape
+    if out is None:
+        out = torch.empty((G, Cc, R), dtype=src.dtype, device=src.device)
+    L.check(L.load().smoe_transpose_batched(L.ptr(src), L.ptr(out), L.dtype_code(src.dtype), G, R, Cc,
+                                            L.stream_handle(src.device)), "smoe_transpose_batched")
+    return out
+
+
+def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int):
+    """recv_counts [ws, E_l] int32 -> dict(counts, offsets, row_src, recv_dst, rows_cap)."""
+    _need_cuda(recv_counts)
+    ws_, El = recv_counts.shape
+    lib = L.load()
+    dev = recv_counts.device
+    rows_cap = n_recv if capacity <= 0 else min(n_recv, capacity * El)
+    counts = torch.empty(El, dtype=torch.int32, device=dev)
+    offsets = torch.empty(El + 1, dtype=torch.int32, device=dev)
+    row_src = torch.empty(max(rows_cap, 1), dtype=torch.int32, device=dev)
+    recv_dst = torch.empty(max(n_recv, 1), dtype=torch.int32, device=dev)
+    wsb = _workspace(dev, lib.smoe_ep_regroup_workspace_size(ws_, El))
+    L.check(lib.smoe_ep_regroup_plan(L.ptr(recv_counts), ws_, El, capacity, n_recv, L.ptr(counts), L.ptr(offsets),
+                                     L.ptr(row_src), L.ptr(recv_dst), L.ptr(wsb), wsb.numel(), L.stream_handle(dev)),
+            "smoe_ep_regroup_plan")
+    return dict(counts=counts, offsets=offsets, row_src=row_src, recv_dst=recv_dst, rows_cap=rows_cap)
+
+
+def read_device_error(device) -> int:
+    import ctypes as C
+    flag = C.c_int(0)
+    L.check(L.load().smoe_read_device_error(C.byref(flag), L.stream_handle(device)), "smoe_read_device_error")
+    return flag.value

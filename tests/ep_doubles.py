@@ -1,0 +1,79 @@
+"""CPU test double of the swiftmoe_b200.kernels operations used by the expert-parallel
+exchange, so that its collective choreography runs on gloo ranks without a GPU.
+Each function follows the contract of the C-ABI entry point of the same name."""
+import numpy as np
+import torch
+
+
+def dispatch_plan(idx, num_experts, capacity=0, row_align=1):
+    idx_n = idx.numpy()
+    T, k = idx_n.shape
+    E = num_experts
+    counts = np.bincount(idx_n.ravel(), minlength=E).astype(np.int32)
+    kept = np.minimum(counts, capacity) if capacity > 0 else counts
+    offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
+    slot_row = -np.ones(T * k, np.int32)
+    row_token = -np.ones(max(int(offsets[-1]), 1), np.int32)
+    seen = np.zeros(E, np.int64)
+    for s in range(T * k):
+        e = idx_n.ravel()[s]
+        if capacity <= 0 or seen[e] < capacity:
+            r = offsets[e] + seen[e]
+            slot_row[s] = r
+            row_token[r] = s // k
+        seen[e] += 1
+    return dict(counts=torch.from_numpy(counts), offsets=torch.from_numpy(offsets),
+                slot_row=torch.from_numpy(slot_row), row_token=torch.from_numpy(row_token),
+                rows_cap=int(max(offsets[-1], 1)))
+
+
+def permute_rows(x, row_token, offsets, rows_cap, out=None):
+    total = int(offsets[-1])
+    rt = row_token.numpy()[:total]
+    xr = x.numpy()
+    rows = np.zeros((max(rows_cap, 1), x.shape[1]), xr.dtype)
+    rows[:total] = np.where(rt[:, None] >= 0, xr[np.maximum(rt, 0)], 0)
+    return torch.from_numpy(rows)
+
+
+def gather_rows(src, index, n_rows, out=None):
+    ind = index.numpy()[:n_rows]
+    s = src.numpy()
+    o = np.zeros((max(n_rows, 1), src.shape[1]), s.dtype)
+    o[:n_rows] = np.where(ind[:, None] >= 0, s[np.maximum(ind, 0)], 0)
+    return torch.from_numpy(o)
+
+
+def ep_regroup_plan(recv_counts, capacity, n_recv):
+    rc = recv_counts.numpy()
+    ws, El = rc.shape
+    tot = rc.sum(0)
+    kept = np.minimum(tot, capacity) if capacity > 0 else tot
+    offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
+    recv_dst = -np.ones(max(n_recv, 1), np.int32)
+    row_src = -np.ones(max(int(offsets[-1]), 1), np.int32)
+    r = 0
+    for s in range(ws):
+        for le in range(El):
+            for i in range(rc[s, le]):
+                pos = rc[:s, le].sum() + i
+                if capacity <= 0 or pos < capacity:
+                    recv_dst[r] = offsets[le] + pos
+                    row_src[offsets[le] + pos] = r
+                r += 1
+    return dict(counts=torch.from_numpy(tot.astype(np.int32)), offsets=torch.from_numpy(offsets),
+                row_src=torch.from_numpy(row_src), recv_dst=torch.from_numpy(recv_dst),
+                rows_cap=int(max(offsets[-1], 1)))
+
+
+def combine(y, slot_row, w, T, k, shared=None, out=None):
+    sr = slot_row.numpy().reshape(T, k)
+    yn = y.numpy().astype(np.float64)
+    wn = w.numpy()
+    o = np.zeros((T, y.shape[1]))
+    for j in range(k):
+        m = sr[:, j] >= 0
+        o[m] += wn[m, j, None] * yn[sr[m, j]]
+    if shared is not None:
+        o += shared.numpy()
+    return torch.from_numpy(o.astype(np.float32))

@@ -1,0 +1,129 @@
+"""Dispatch plan / permute / combine / gather / EP regroup kernels (C ABI), bit-exact
+against the oracle's index-order plan."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from util import max_abs_err, rounded, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    from swiftmoe_b200 import kernels
+    return kernels
+
+
+def expected_plan(idx: np.ndarray, E: int, capacity: int, row_align: int):
+    T, k = idx.shape
+    plan, kept = O.dispatch_plan([idx], E, 1, capacity if capacity > 0 else None)
+    counts = np.bincount(idx.ravel(), minlength=E)
+    kept_n = np.array([len(p) for p in plan])
+    aligned = (kept_n + row_align - 1) // row_align * row_align
+    offsets = np.concatenate([[0], np.cumsum(aligned)]).astype(np.int64)
+    slot_row = -np.ones(T * k, np.int64)
+    row_token = {}
+    for e in range(E):
+        for n, (_, t, j) in enumerate(plan[e]):
+            slot_row[t * k + j] = offsets[e] + n
+            row_token[offsets[e] + n] = t
+        for r in range(offsets[e] + kept_n[e], offsets[e + 1]):
+            row_token[r] = -1
+    return counts, offsets, slot_row, row_token
+
+
+@pytest.mark.parametrize("T,k,E,cap,align", [(0, 2, 8, 0, 1), (1, 2, 8, 0, 1), (63, 2, 8, 0, 1), (64, 2, 8, 0, 1),
+                                             (65, 2, 8, 0, 128), (1000, 2, 8, 0, 1), (5000, 8, 128, 0, 1),
+                                             (3000, 2, 64, 100, 1), (777, 3, 7, 50, 16), (9000, 2, 8, 2000, 1),
+                                             (20000, 8, 130, 900, 8)])
+def test_plan_bit_exact(K, T, k, E, cap, align):
+    rng = np.random.default_rng(T + E)
+    # skewed routing: some experts much more popular
+    p = rng.dirichlet(np.ones(E) * 0.3)
+    p = (p + 1e-3) / (p + 1e-3).sum()
+    idx = np.array([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)], dtype=np.int32).reshape(T, k)
+    plan = K.dispatch_plan(to_dev(idx, torch.int32), E, cap, align)
+    counts, offsets, slot_row, row_token = expected_plan(idx, E, cap, align)
+    assert (plan["counts"].cpu().numpy() == counts).all()
+    assert (plan["offsets"].cpu().numpy() == offsets).all()
+    assert (plan["slot_row"].cpu().numpy() == slot_row).all()
+    rt = plan["row_token"].cpu().numpy()
+    for r, t in row_token.items():
+        assert rt[r] == t
+    assert plan["rows_cap"] >= offsets[-1]
+
+
+def test_plan_all_to_one_expert(K):
+    T, k, E = 4097, 2, 8
+    idx = np.zeros((T, k), np.int32)
+    idx[:, 1] = 5
+    plan = K.dispatch_plan(to_dev(idx, torch.int32), E, 0, 1)
+    counts, offsets, slot_row, _ = expected_plan(idx, E, 0, 1)
+    assert (plan["offsets"].cpu().numpy() == offsets).all()
+    assert (plan["slot_row"].cpu().numpy() == slot_row).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,d,k,E", [(1, 64, 2, 8), (129, 512, 2, 8), (300, 36, 3, 5), (1000, 2048, 8, 64)])
+def test_permute_combine(K, dtype, T, d, k, E):
+    rng = np.random.default_rng(d + T)
+    idx = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    x = rounded(rng.standard_normal((T, d)).astype(np.float32), dtype)
+    w = rng.random((T, k)).astype(np.float32)
+    cap = max(1, (T * k) // E)  # forces drops
+    plan = K.dispatch_plan(to_dev(idx, torch.int32), E, cap, 1)
+    rows = K.permute_rows(to_dev(x, dtype), plan["row_token"], plan["offsets"], plan["rows_cap"])
+    total = int(plan["offsets"][-1])
+    rt = plan["row_token"].cpu().numpy()[:total]
+    assert (rows[:total].float().cpu().numpy() == x[rt]).all()        # bit-exact copy
+    # combine: y = rows * 2 + 1 (any row function), weighted sum over kept slots
+    y = rows.float() * 2 + 1
+    y = y.to(dtype)
+    shared = rounded(rng.standard_normal((T, d)).astype(np.float32), dtype)
+    out = K.combine(y, plan["slot_row"], to_dev(w), T, k, shared=to_dev(shared, dtype))
+    sr = plan["slot_row"].cpu().numpy().reshape(T, k)
+    yn = y.float().cpu().numpy()
+    ref = shared.astype(np.float64).copy()
+    for j in range(k):
+        m = sr[:, j] >= 0
+        ref[m] += w[m, j, None] * yn[sr[m, j]]
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert max_abs_err(out.float().cpu().numpy(), ref) <= tol * max(1.0, np.abs(ref).max())
+
+
+def test_gather_rows(K):
+    rng = np.random.default_rng(3)
+    src = rng.standard_normal((50, 24)).astype(np.float32)
+    index = rng.integers(-1, 50, size=80).astype(np.int32)
+    out = K.gather_rows(to_dev(src), to_dev(index, torch.int32), 80).cpu().numpy()
+    ref = np.where(index[:, None] >= 0, src[np.maximum(index, 0)], 0)
+    assert (out == ref).all()
+
+
+@pytest.mark.parametrize("ws,El,cap", [(2, 4, 0), (4, 2, 5), (8, 1, 0), (3, 5, 7)])
+def test_ep_regroup_plan(K, ws, El, cap):
+    rng = np.random.default_rng(ws * 10 + El)
+    rc = rng.integers(0, 9, size=(ws, El)).astype(np.int32)
+    n_recv = int(rc.sum())
+    rg = K.ep_regroup_plan(to_dev(rc, torch.int32), cap, n_recv)
+    # reference: receive rows are (src, le)-major; expert rows are (le, src, i)-major
+    seg = []
+    for s in range(ws):
+        for le in range(El):
+            seg += [(s, le, i) for i in range(rc[s, le])]
+    kept = [min(int(rc[:, le].sum()), cap) if cap > 0 else int(rc[:, le].sum()) for le in range(El)]
+    offsets = np.concatenate([[0], np.cumsum(kept)])
+    recv_dst = []
+    for (s, le, i) in seg:
+        pos = int(rc[:s, le].sum()) + i
+        recv_dst.append(-1 if (cap > 0 and pos >= cap) else offsets[le] + pos)
+    assert (rg["counts"].cpu().numpy() == rc.sum(0)).all()
+    assert (rg["offsets"].cpu().numpy() == offsets).all()
+    got = rg["recv_dst"].cpu().numpy()[:n_recv]
+    assert (got == np.array(recv_dst, dtype=np.int64)).all()
+    rs = rg["row_src"].cpu().numpy()
+    for r, dst in enumerate(recv_dst):
+        if dst >= 0:
+            assert rs[dst] == r

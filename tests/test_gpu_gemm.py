@@ -1,0 +1,105 @@
+"""Grouped GEMM kernels (tcgen05 for bf16/fp16, FFMA for fp32) against a plain PyTorch
+fp32 reference of the same op on the same rounded inputs."""
+import numpy as np
+import pytest
+import torch
+
+from util import max_abs_err, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    from swiftmoe_b200 import kernels
+    return kernels
+
+
+def make_groups(sizes, K_, N, dtype, seed=0, std=0.05):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    rows = int(sum(sizes))
+    A = torch.randn((max(rows, 1), K_), generator=g).to(dtype)
+    B = (torch.randn((len(sizes), N, K_), generator=g) * std).to(dtype)
+    B3 = (torch.randn((len(sizes), N, K_), generator=g) * std).to(dtype)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]), dtype=torch.int32)
+    return A, B, B3, offs, rows
+
+
+def ref_store(A, B, offs):
+    out = torch.zeros((A.shape[0], B.shape[1]), dtype=torch.float64)
+    o = offs.tolist()
+    for g in range(B.shape[0]):
+        out[o[g]:o[g + 1]] = A[o[g]:o[g + 1]].double() @ B[g].double().T
+    return out
+
+
+def ref_swiglu(A, B1, B3, offs):
+    g_ = ref_store(A, B1, offs)
+    u_ = ref_store(A, B3, offs)
+    return torch.nn.functional.silu(g_) * u_
+
+
+SHAPES = [
+    ([128], 64, 256),            # one full tile
+    ([1], 64, 256),              # one row
+    ([0, 300, 0, 77], 128, 256),  # empty groups, ragged rows
+    ([129, 255, 3], 72, 200),    # K % 64 != 0, N % 256 != 0
+    ([513, 64, 1000], 256, 512),
+    ([37] * 16, 512, 128),       # many small groups
+    ([2048, 1536], 1024, 768),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sizes,K_,N", SHAPES)
+def test_grouped_store_tc(K, dtype, sizes, K_, N):
+    A, B, _, offs, rows = make_groups(sizes, K_, N, dtype, seed=len(sizes) + K_)
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
+    ref = ref_store(A, B, offs)[:rows]
+    assert max_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2
+    assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sizes,K_,N", SHAPES)
+def test_grouped_store_tc_fp32_out(K, dtype, sizes, K_, N):
+    A, B, _, offs, rows = make_groups(sizes, K_, N, dtype, seed=7 + K_)
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda(), out_dtype=torch.float32)
+    ref = ref_store(A, B, offs)[:rows].numpy()
+    # exact products, fp32 accumulation: error ~ sqrt(K) * 2^-24 * |terms|
+    assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * np.sqrt(K_) * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sizes,K_,N", SHAPES)
+def test_grouped_swiglu_tc(K, dtype, sizes, K_, N):
+    A, B, B3, offs, rows = make_groups(sizes, K_, N, dtype, seed=11 + N)
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda(), B3=B3.cuda(), epilogue=1)
+    ref = ref_swiglu(A, B, B3, offs)[:rows]
+    assert max_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2
+
+
+@pytest.mark.parametrize("sizes,K_,N", [([1], 8, 8), ([0, 65, 3], 30, 70), ([200, 130], 512, 256),
+                                         ([64] * 9, 96, 64)])
+def test_grouped_fp32_simt(K, sizes, K_, N):
+    A, B, B3, offs, rows = make_groups(sizes, K_, N, torch.float32, seed=3)
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
+    assert max_abs_err(out[:rows].cpu().numpy(), ref_store(A, B, offs)[:rows].numpy()) <= 1e-5
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda(), B3=B3.cuda(), epilogue=1)
+    assert max_abs_err(out[:rows].cpu().numpy(), ref_swiglu(A, B, B3, offs)[:rows].numpy()) <= 1e-5
+
+
+def test_grouped_large_mixtral_slice(K):
+    """A slice of the Mixtral expert shapes: d=4096 -> 2x14336 gate/up, ragged experts."""
+    sizes = [700, 0, 1290, 513]
+    A, B, B3, offs, rows = make_groups(sizes, 4096, 1024, torch.bfloat16, seed=5, std=0.02)
+    out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda(), B3=B3.cuda(), epilogue=1)
+    ref = ref_swiglu(A, B, B3, offs)[:rows]
+    assert max_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2
+
+
+def test_transpose_batched(K):
+    x = torch.randn(3, 70, 45).cuda()
+    assert torch.equal(K.transpose_batched(x), x.transpose(1, 2).contiguous())
+    xb = x.bfloat16()
+    assert torch.equal(K.transpose_batched(xb), xb.transpose(1, 2).contiguous())

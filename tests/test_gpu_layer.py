@@ -1,0 +1,158 @@
+"""Whole-layer parity of the drop-in modules: reference fixtures (fp32, max-abs 1e-5)
+and the oracle on rounded inputs (bf16 / fp16, max-rel 2e-2)."""
+import numpy as np
+import pytest
+import torch
+
+import fixtures as fx
+import synth
+from oracle import moe_oracle as O
+from util import max_abs_err, max_rel_err, rounded, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def M():
+    import swiftmoe_b200
+    return swiftmoe_b200
+
+
+def _std_from_params(M, p, E, d, dtype, **kw):
+    m = M.StandardMoE(E, d, use_fp16=False, dtype=dtype, **kw).cuda()
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy(p.gate))
+        if p.expert_type == "linear":
+            for i in range(E):
+                m.experts[i].weight.copy_(torch.from_numpy(p.expert_w[i].T.copy()))
+        else:
+            for i in range(E):
+                m.experts[i].w1.weight.copy_(torch.from_numpy(p.w1[i]))
+                m.experts[i].w3.weight.copy_(torch.from_numpy(p.w3[i]))
+                m.experts[i].w2.weight.copy_(torch.from_numpy(p.w2[i]))
+    return m
+
+
+@pytest.mark.parametrize("name", fx.STD_LINEAR)
+def test_standard_linear_fp32_vs_reference(M, name):
+    f, p = fx.std_linear(name)
+    m = _std_from_params(M, p, f["E"], f["d"], torch.float32)
+    out = m(to_dev(f["x"])).cpu().numpy()
+    assert out.shape == f["out"].shape
+    assert max_abs_err(out, f["out"]) <= 1e-5
+
+
+@pytest.mark.parametrize("name", fx.STD_SWIGLU)
+def test_standard_swiglu_fp32_vs_reference(M, name):
+    f, p = fx.std_swiglu(name)
+    m = _std_from_params(M, p, f["E"], f["d"], torch.float32, expert_type="swiglu", d_ff=f["F"])
+    out = m(to_dev(f["x"])).cpu().numpy()
+    assert max_abs_err(out, f["out"]) <= 1e-5
+
+
+def test_ultimate_linear_fp32_vs_reference_ws1(M):
+    f, p = fx.ult_linear("ult_linear_fp32_ws1_E8_d64_M50")
+    m = M.UltimateMoE(f["E"], f["d"], use_fp16=False).cuda()
+    with torch.no_grad():
+        m.gate_weight.copy_(torch.from_numpy(p.gate))
+        m.expert_weights.copy_(torch.from_numpy(p.expert_w))
+    out = m(to_dev(f["x"][0])).cpu().numpy()
+    assert max_abs_err(out, f["out"][0]) <= 1e-5
+
+
+def test_standard_linear_fp16_vs_reference(M):
+    f, p = fx.std_linear("std_linear_fp16_E8_d128_M33")
+    m = _std_from_params(M, p, f["E"], f["d"], torch.float16)
+    out = m(to_dev(f["x"], torch.float16)).float().cpu().numpy()
+    ref = f["out"]
+    assert np.abs(out - ref).max() <= 2e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,d,E,k,F,cf,shared,bias", [
+    (1, 256, 8, 2, 512, None, False, False),
+    (257, 512, 8, 2, 1024, None, False, False),
+    (1000, 256, 64, 2, 256, 1.25, False, False),
+    (600, 256, 32, 8, 128, None, True, True),
+    (2048, 512, 128, 8, 128, 1.25, True, True),
+])
+def test_swiglu_layer_vs_oracle(M, dtype, T, d, E, k, F, cf, shared, bias):
+    rng_seed = T + E
+    w1, w3, w2 = synth.swiglu_weights(rng_seed, E, d, F, init="normal", std=0.02)
+    g = synth.normal(rng_seed + 5, (E, d), 0.02)
+    x = synth.normal(rng_seed + 9, (T, d), 1.0)
+    lb = synth.normal(rng_seed + 2, (E,), 1.5) if bias else None
+    sw = synth.swiglu_weights(rng_seed + 1, 1, d, F, init="normal", std=0.02) if shared else None
+    r = lambda a: rounded(a, dtype)
+    m = M.UltimateMoE(E, d, use_fp16=False, dtype=dtype, top_k=k, expert_type="swiglu", d_ff=F,
+                      capacity_factor=cf, num_shared_experts=1 if shared else 0, d_ff_shared=F).cuda()
+    with torch.no_grad():
+        m.gate_weight.copy_(torch.from_numpy(g))
+        m.w1.copy_(torch.from_numpy(w1)); m.w3.copy_(torch.from_numpy(w3)); m.w2.copy_(torch.from_numpy(w2))
+        if shared:
+            m.shared_w1.copy_(torch.from_numpy(sw[0][0])); m.shared_w3.copy_(torch.from_numpy(sw[1][0]))
+            m.shared_w2.copy_(torch.from_numpy(sw[2][0]))
+    if bias:
+        m.set_logit_bias(torch.from_numpy(lb))
+    out = m(to_dev(x, dtype)).float().cpu().numpy()
+    p = O.MoEParams(gate=r(g), expert_type="swiglu", w1=r(w1), w3=r(w3), w2=r(w2), logit_bias=lb)
+    if shared:
+        p.sw1, p.sw3, p.sw2 = r(sw[0]), r(sw[1]), r(sw[2])
+    (ref,), aux = O.moe_forward([r(x)], p, k=k, capacity_factor=cf, acc=np.float64, return_aux=True)
+    # routing may only differ on near-ties; compare rows whose routing agrees exactly
+    idx, _ = __import__("swiftmoe_b200").kernels.router(to_dev(x, dtype), m.gate_weight, k,
+                                                        m.logit_bias)
+    same = (idx.cpu().numpy() == aux["routed"][0][0]).all(1)
+    assert same.mean() > 0.99
+    if cf is None:
+        assert max_rel_err(out[same], ref[same]) <= 2e-2
+    else:
+        # a routing flip can move the capacity cut for later tokens; require agreement
+        # on the rows before the first flip
+        first = np.argmin(same) if not same.all() else T
+        assert max_rel_err(out[:first], ref[:first]) <= 2e-2
+
+
+def test_layer_empty_and_single(M):
+    m = M.UltimateMoE(8, 64, use_fp16=False, dtype=torch.bfloat16, expert_type="swiglu", d_ff=128).cuda()
+    assert m(torch.empty((0, 64), device="cuda", dtype=torch.bfloat16)).shape == (0, 64)
+    assert m(torch.randn((1, 64), device="cuda", dtype=torch.bfloat16)).shape == (1, 64)
+
+
+def test_fp16_default_reference_smoke_shape(M):
+    """scripts/test_setup.py:545-575: StandardMoE(8,128) / UltimateMoE(8,128), 32 tokens fp16."""
+    for m in (M.StandardMoE(num_experts=8, d_model=128, use_fp16=True),
+              M.UltimateMoE(num_experts=8, d_model=128, use_fp16=True, use_triton=False)):
+        m = m.cuda()
+        x = torch.randn(32, 128, device="cuda", dtype=torch.float16)
+        with torch.no_grad():
+            assert m(x).shape == x.shape
+
+
+def test_profiling_summary(M):
+    m = M.UltimateMoE(8, 256, use_fp16=False, dtype=torch.bfloat16, expert_type="swiglu", d_ff=512,
+                      enable_profiling=True).cuda()
+    x = torch.randn(300, 256, device="cuda", dtype=torch.bfloat16)
+    ref = None
+    for _ in range(3):
+        out = m(x)
+    s = m.get_profile_summary()
+    assert set(s) >= {"Router", "Dispatch_Comm", "Expert_Compute", "Combine_Comm", "Exposed_A2A"}
+    assert all(v >= 0 for v in s.values()) and s["Expert_Compute"] > 0
+    m.reset_profiling()
+    assert m.get_profile_summary()["Router"] == 0
+    m.enable_profiling = False
+    torch.testing.assert_close(m(x), out, rtol=0, atol=0)
+    m._force_staged = True
+    torch.testing.assert_close(m(x), out, rtol=0, atol=0)   # staged == fused, bit for bit
+
+
+def test_staged_private_methods_match_forward(M):
+    m = M.StandardMoE(8, 128, use_fp16=False, dtype=torch.bfloat16).cuda()
+    x = torch.randn(77, 128, device="cuda", dtype=torch.bfloat16)
+    idx, w = m._route_tokens(x)
+    rows, offs, wf, s, r_, plan = m._dispatch_tokens(x, idx, w)
+    y = m._expert_forward(rows, offs)
+    out = m._combine_tokens(y, s, r_, plan, x.shape[0], weights=wf)
+    full = m(x)
+    assert max_rel_err(out.float().cpu().numpy(), full.float().cpu().numpy()) <= 2e-2
