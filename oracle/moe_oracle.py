@@ -75,9 +75,11 @@ def topk_lower_index(logits: np.ndarray, k: int):
     """Top-k per row, values descending, ties broken toward the LOWER expert index.
 
     Restates ``torch.topk(gate_logits, k=2, dim=-1)`` (``models/baseline_moe.py:62``,
-    ``models/ultimate_moe.py:290``) as torch's CPU kernel behaves: equal values keep the
-    lower index first, and NaN ranks above every number (lower index first among NaNs).
-    Returns (values float32 [T,k], indices int32 [T,k]).
+    ``models/ultimate_moe.py:290``): the same selected values as torch, NaN ranked above
+    every number.  Among EQUAL values torch's CPU kernel orders by its partial-sort /
+    nth_element pass, which is not index order; this restatement (and the GPU router)
+    takes the lower expert index first, a deterministic rule.  Without ties the indices
+    are identical to torch's.  Returns (values float32 [T,k], indices int32 [T,k]).
     """
     logits = np.asarray(logits, dtype=np.float32)
     T, E = logits.shape
@@ -181,12 +183,17 @@ def swiglu_expert(x, w1, w3, w2, acc=np.float32, round_hidden=None):
     """SwiGLU expert ``w2(silu(w1 x) * w3 x)`` (extension; nn.Linear layouts).
 
     w1, w3: [F, d]; w2: [d, F].  ``round_hidden`` optionally rounds the hidden activation
-    (the GPU path stores it in the compute dtype between the two GEMMs)."""
+    and the expert output to the storage dtype of a 16-bit pipeline (a bf16/fp16 layer
+    keeps both in the compute dtype between its GEMMs, as the reference's torch path does
+    for every intermediate)."""
     x = np.asarray(x, acc)
     h = silu(x @ np.asarray(w1, acc).T) * (x @ np.asarray(w3, acc).T)
     if round_hidden is not None:
         h = round_hidden(h.astype(np.float32)).astype(acc)
-    return h @ np.asarray(w2, acc).T
+    y = h @ np.asarray(w2, acc).T
+    if round_hidden is not None:
+        y = round_hidden(y.astype(np.float32)).astype(acc)
+    return y
 
 
 # --------------------------------------------------------------------------- layer
@@ -228,6 +235,8 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
     does (``models/ultimate_moe.py:245``); ``"post"`` after it (``baseline_moe.py:162``).
     SwiGLU experts always use post-weighting.  Dropped rows contribute zero and the kept
     weights are not renormalised.  The shared expert output is added unweighted.
+    ``round_hidden`` (e.g. ``bf16_round``) rounds the intermediates a 16-bit pipeline
+    stores: the SwiGLU hidden activation and each expert's output before weighting.
     """
     E = p.num_experts
     if E % ws:
@@ -255,7 +264,10 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
             if weighting == "pre":
                 y = linear_expert_pre(xin, wts, p.expert_w[e], acc)
             else:
-                y = linear_expert_post(xin, wts, p.expert_w[e].T, acc)
+                y = linear_expert_post(xin, np.ones_like(wts), p.expert_w[e].T, acc)
+                if round_hidden is not None:
+                    y = round_hidden(y.astype(np.float32)).astype(acc)
+                y = y * wts[:, None]
         elif p.expert_type == "swiglu":
             y = swiglu_expert(xin, p.w1[e], p.w3[e], p.w2[e], acc, round_hidden) * wts[:, None]
         else:

@@ -60,16 +60,21 @@ int device_sms() {
   return cache[dev];
 }
 
-// Raise a kernel's dynamic shared-memory limit once per device.
+// Per-device record of the dynamic shared-memory limit already granted to one kernel.
+struct SmemGrant {
+  int bytes[kMaxDevices] = {0};
+};
+
+// Raise (never lower) a kernel's dynamic shared-memory limit on the current device.
 template <typename K>
-cudaError_t ensure_smem(K kernel, int bytes, unsigned long long* done_mask) {
+cudaError_t ensure_smem(K kernel, int bytes, SmemGrant* grant) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (*done_mask & bit) return cudaSuccess;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (grant->bytes[dev] >= bytes) return cudaSuccess;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) *done_mask |= bit;
+  if (e == cudaSuccess) grant->bytes[dev] = bytes;
   return e;
 }
 
@@ -126,7 +131,7 @@ __global__ void fill_two_kernel(int32_t* p, int32_t a, int32_t b) {
 template <int EPI, typename OutT>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
               const int32_t* offsets, int G, int64_t rows_cap, int N, int K, uint32_t idesc, cudaStream_t st) {
-  static unsigned long long done = 0;
+  static SmemGrant done;
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
   kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, G, N,
@@ -194,7 +199,7 @@ RouterPath router_path(int d, int E, int dtype) {
 template <typename T, int EMAX, int TOK, int VEC>
 int launch_router_small(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
                         float* w, float* logits, cudaStream_t st) {
-  static unsigned long long done = 0;
+  static SmemGrant done;
   auto kern = router_small_kernel<T, EMAX, TOK, VEC>;
   const int smem = E * d * (int)sizeof(T);
   SMOE_CK(ensure_smem(kern, std::max(smem, 1), &done));
@@ -364,7 +369,7 @@ int smoe_dispatch_plan(const int32_t* idx, int T, int k, int E, int capacity, in
   int32_t* base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
                                              align_up((size_t)nb * E * sizeof(int32_t), 256));
   const int smem_w = kPlanWarps * E * (int)sizeof(int);
-  static unsigned long long done_c = 0, done_s = 0;
+  static SmemGrant done_c, done_s;
   SMOE_CK(ensure_smem(plan_count_kernel, smem_w, &done_c));
   SMOE_CK(ensure_smem(plan_scatter_kernel, smem_w, &done_s));
   plan_count_kernel<<<nb, kPlanThreads, smem_w, st>>>(idx, n_slots, E, hist);
@@ -476,7 +481,7 @@ int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capaci
   int32_t* src_base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
                                                  align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256));
   const int smem = (E_l + ws) * (int)sizeof(int);
-  static unsigned long long done = 0;
+  static SmemGrant done;
   SMOE_CK(ensure_smem(ep_regroup_scan_kernel, smem, &done));
   ep_regroup_scan_kernel<<<1, 1024, smem, st>>>(recv_counts, ws, E_l, capacity, expert_counts, expert_offsets,
                                                 seg_start, src_base);

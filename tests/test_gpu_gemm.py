@@ -83,10 +83,13 @@ def test_grouped_swiglu_tc(K, dtype, sizes, K_, N):
                                          ([64] * 9, 96, 64)])
 def test_grouped_fp32_simt(K, sizes, K_, N):
     A, B, B3, offs, rows = make_groups(sizes, K_, N, torch.float32, seed=3)
+    # fp32 FFMA accumulation: 1e-5 absolute at unit output scale
     out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
-    assert max_abs_err(out[:rows].cpu().numpy(), ref_store(A, B, offs)[:rows].numpy()) <= 1e-5
+    ref = ref_store(A, B, offs)[:rows].numpy()
+    assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * max(1.0, np.abs(ref).max())
     out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda(), B3=B3.cuda(), epilogue=1)
-    assert max_abs_err(out[:rows].cpu().numpy(), ref_swiglu(A, B, B3, offs)[:rows].numpy()) <= 1e-5
+    ref = ref_swiglu(A, B, B3, offs)[:rows].numpy()
+    assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * max(1.0, np.abs(ref).max())
 
 
 def test_grouped_large_mixtral_slice(K):
