@@ -42,7 +42,7 @@ GEMM1_DRAM_BYTES_PER_LAUNCH = None
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="swiftmoe", choices=["swiftmoe", "reference"])
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
@@ -61,6 +61,8 @@ def peaks():
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi sampled every 100 ms in a background reader; samples are host-stamped so
+    that only those taken inside the timed region are summarised."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -68,31 +70,46 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.samples = []
+        self.window = (0.0, float("inf"))
 
-    def __enter__(self):
+    def start(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                if line.strip():
+                    self.samples.append((time.time(), line.strip()))
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 5:   # wait for the first sample
+            time.sleep(0.02)
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        lo, hi = self.window
+        sel = [l for (t, l) in self.samples if lo <= t <= hi]
+        if not sel:   # region shorter than the sampling period: take the sample right after it
+            sel = [l for (t, l) in self.samples if t >= lo][:1]
+        for l in sel:
             parts = [p.strip() for p in l.split(",")]
             if len(parts) < 9:
                 continue
@@ -101,7 +118,7 @@ class ClockSampler:
                 mx = float(parts[2])
             except ValueError:
                 continue
-            for n, v in zip(names[1:], parts[5:9]):
+            for n, v in zip(names, parts[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
@@ -226,12 +243,14 @@ def main():
     evs = [L.StageEvents() for _ in range(args.steps)] if ws == 1 else None
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        t_start.record()
-        for i in range(args.steps):
-            step(evs[i] if evs else None)
-        t_end.record()
-        torch.cuda.synchronize()
+    clk = ClockSampler(local).start()
+    h0 = time.time()
+    t_start.record()
+    for i in range(args.steps):
+        step(evs[i] if evs else None)
+    t_end.record()
+    torch.cuda.synchronize()
+    clk.window = (h0, time.time())
     barrier()
     ms = t_start.elapsed_time(t_end) / args.steps
     if ws > 1:
@@ -319,6 +338,7 @@ def main():
                 "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,
                 "cpu_baseline": cpu, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
+    clk.stop()
     if ws > 1:
         dist.destroy_process_group()
 

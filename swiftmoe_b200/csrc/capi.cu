@@ -581,7 +581,7 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
   if (a->expert_type == SMOE_EXPERT_LINEAR && !a->w_lin) return SMOE_ERR_INVALID;
   if (a->num_shared < 0 || a->num_shared > 1) return SMOE_ERR_UNSUPPORTED;
   if (a->num_shared == 1 && (a->d_ff_shared < 1 || !a->sw1 || !a->sw3 || !a->sw2)) return SMOE_ERR_INVALID;
-  if (!a->gate_w || !a->out || (T > 0 && !a->x)) return SMOE_ERR_INVALID;
+  if (!a->gate_w || (T > 0 && (!a->x || !a->out))) return SMOE_ERR_INVALID;
   LayerPlan p;
   layer_plan(a, &p);
   if (!a->workspace || a->workspace_bytes < p.total) return SMOE_ERR_WORKSPACE;

@@ -53,3 +53,14 @@ STD_SWIGLU = ["std_swiglu_fp32_E4_d32_F64_M29", "std_swiglu_fp32_E8_d128_F256_M7
               "std_swiglu_fp32_E8_d512_F2048_M8", "std_swiglu_fp32_E8_d512_F2048_M64"]
 ULT_LINEAR = ["ult_linear_fp32_ws1_E8_d64_M50", "ult_linear_fp32_ws2_E8_d32_M23",
               "ult_linear_fp32_ws4_E8_d32_M17"]
+
+
+def std_swiglu_lowp(name: str):
+    """16-bit reference run: weights are synth.swiglu_weights(seed, init='normal')."""
+    f = load(name)
+    E, d, F, M, seed = [int(v) for v in f["meta"]]
+    w1, w3, w2 = synth.swiglu_weights(seed, E, d, F, init="normal", std=0.02)
+    g = synth.normal(seed + 5, (E, d), 0.02)
+    p = MoEParams(gate=g, expert_type="swiglu", w1=w1, w3=w3, w2=w2)
+    f.update(E=E, d=d, F=F, M=M)
+    return f, p

@@ -94,6 +94,25 @@ def standard_swiglu(torch, nn, StandardMoE, name, E, d, F, M, seed, x_only_seed=
                         meta=np.array([E, d, F, M, seed, -1 if x_only_seed is None else x_only_seed]))
 
 
+def standard_swiglu_lowp(torch, nn, StandardMoE, name, E, d, F, M, seed, dtype_name):
+    """The reference's StandardMoE run in a 16-bit dtype with SwiGLU experts substituted:
+    its own low-precision output, for comparing a 16-bit implementation against it."""
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype_name]
+    w1, w3, w2 = synth.swiglu_weights(seed, E, d, F, init="normal", std=0.02)
+    g = synth.normal(seed + 5, (E, d), 0.02)
+    x = synth.normal(seed + 7, (M, d), 1.0)
+    m = StandardMoE(num_experts=E, d_model=d, use_fp16=False)
+    m.experts = nn.ModuleList([_swiglu_module(torch, nn, w1[i], w3[i], w2[i]) for i in range(E)])
+    m = m.to(dt)
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy(g))
+        xt = torch.from_numpy(x).to(dt)
+        idx, w = m._route_tokens(xt)
+        out = m(xt)
+    np.savez_compressed(HERE / f"{name}.npz", x=xt.float().numpy(), topk_idx=idx.int().numpy(),
+                        out=out.float().numpy(), meta=np.array([E, d, F, M, seed]))
+
+
 def _ult_worker(rank, ws, port, ref, E, d, M, seed, out_path):
     import torch
     import torch.distributed as dist
@@ -172,6 +191,7 @@ def main(ref: str):
                     x_only_seed=1000)
     standard_swiglu(torch, nn, StandardMoE, "std_swiglu_fp32_E8_d512_F2048_M64", 8, 512, 2048, 64, 0,
                     x_only_seed=1001)
+    standard_swiglu_lowp(torch, nn, StandardMoE, "std_swiglu_bf16_E8_d512_F1024_M64", 8, 512, 1024, 64, 51, "bf16")
     ultimate_linear("ult_linear_fp32_ws1_E8_d64_M50", ref, 8, 64, 50, 31, 1)
     ultimate_linear("ult_linear_fp32_ws2_E8_d32_M23", ref, 8, 32, 23, 32, 2)
     ultimate_linear("ult_linear_fp32_ws4_E8_d32_M17", ref, 8, 32, 17, 33, 4)

@@ -98,13 +98,8 @@ def test_swiglu_layer_vs_oracle(M, dtype, T, d, E, k, F, cf, shared, bias):
     p = O.MoEParams(gate=r(g), expert_type="swiglu", w1=r(w1), w3=r(w3), w2=r(w2), logit_bias=lb)
     if shared:
         p.sw1, p.sw3, p.sw2 = r(sw[0]), r(sw[1]), r(sw[2])
-    rnd = O.bf16_round if dtype == torch.bfloat16 else O.f16_round
-    # the oracle mirrors the two intermediates the 16-bit path stores in the compute
-    # dtype (SwiGLU hidden activation, expert output); a second, looser check compares
-    # against the fully fp32 oracle
-    (ref,), aux = O.moe_forward([r(x)], p, k=k, capacity_factor=cf, acc=np.float64, return_aux=True,
-                                round_hidden=rnd)
-    (ref32,) = O.moe_forward([r(x)], p, k=k, capacity_factor=cf, acc=np.float64)
+    # fp32 (here float64) oracle on the same rounded inputs and weights
+    (ref,), aux = O.moe_forward([r(x)], p, k=k, capacity_factor=cf, acc=np.float64, return_aux=True)
     # routing may only differ on near-ties; compare rows whose routing agrees exactly
     idx, _ = __import__("swiftmoe_b200").kernels.router(to_dev(x, dtype), m.gate_weight, k,
                                                         m.logit_bias)
@@ -114,7 +109,7 @@ def test_swiglu_layer_vs_oracle(M, dtype, T, d, E, k, F, cf, shared, bias):
     # (with a capacity a routing flip can move the cut for later tokens: compare the rows
     # before the first flip)
     assert max_rel_err(out[rows], ref[rows]) <= 2e-2
-    nrm = np.linalg.norm(out[rows] - ref32[rows]) / max(np.linalg.norm(ref32[rows]), 1e-30)
+    nrm = np.linalg.norm(out[rows] - ref[rows]) / max(np.linalg.norm(ref[rows]), 1e-30)
     assert nrm <= 1e-2
 
 
@@ -164,3 +159,14 @@ def test_staged_private_methods_match_forward(M):
     y = m._expert_forward(rows, offs)
     out = m._combine_tokens(y, s, r_, plan, x.shape[0], weights=wf)
     torch.testing.assert_close(out, m(x), rtol=0, atol=0)   # same kernels, same bits
+
+
+def test_bf16_layer_vs_reference_bf16_output(M):
+    """Our bf16 layer against the reference's OWN bf16 forward on identical inputs."""
+    f, p = fx.std_swiglu_lowp("std_swiglu_bf16_E8_d512_F1024_M64")
+    m = _std_from_params(M, p, f["E"], f["d"], torch.bfloat16, expert_type="swiglu", d_ff=f["F"])
+    out = m(to_dev(f["x"], torch.bfloat16)).float().cpu().numpy()
+    idx, _ = m._route_tokens(to_dev(f["x"], torch.bfloat16))
+    same = (idx.cpu().numpy() == f["topk_idx"]).all(1)
+    assert same.mean() > 0.95
+    assert max_rel_err(out[same], f["out"][same]) <= 2e-2
