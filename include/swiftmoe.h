@@ -36,6 +36,7 @@ typedef struct CUstream_st* smoe_stream_t; /* == cudaStream_t */
 #define SMOE_ERR_TIMEOUT (-3)     /* a device-side bounded wait gave up                */
 #define SMOE_ERR_UNSUPPORTED (-4) /* valid but unsupported shape / dtype combination   */
 #define SMOE_ERR_WORKSPACE (-5)   /* workspace too small                               */
+#define SMOE_ERR_TOO_LARGE (-6)   /* size beyond a fixed, documented maximum           */
 
 /* ------------------------------------------------------------------------------ dtypes */
 #define SMOE_F32 0
@@ -91,6 +92,27 @@ SMOE_API int smoe_dispatch_plan(const int32_t* idx, int T, int k, int E, int cap
                        int32_t* expert_counts, int32_t* expert_offsets, int32_t* slot_row,
                        int32_t* row_token, int64_t rows_cap, void* workspace,
                        size_t workspace_bytes, smoe_stream_t stream);
+
+/* Allocation-free variant of smoe_dispatch_plan.  No counterpart in the reference.
+ * For callers that cannot allocate device memory at all -- e.g. a host that owns every
+ * byte of device memory in its own arena or caching allocator, where a cudaMalloc from
+ * a library would bypass that budget and synchronise the device mid-step.  It takes no
+ * workspace and allocates nothing: its scratch (per-block histograms and bases) is a
+ * fixed 512 KiB static device array inside the library, held by every GPU that loads
+ * the library until the process exits.  Same inputs, outputs and results as
+ * smoe_dispatch_plan.  Limits: T*k <= SMOE_NOALLOC_PLAN_MAX_SLOTS and
+ * E <= SMOE_NOALLOC_PLAN_MAX_EXPERTS, else SMOE_ERR_TOO_LARGE and nothing is launched.
+ * The first call on a device resolves the scratch array's device address with that
+ * device current (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the one scratch array, so calls that overlap on the GPU
+ * (other streams, other host threads) race and must be serialised by the caller.     */
+#define SMOE_NOALLOC_PLAN_MAX_SLOTS (1 << 19)
+#define SMOE_NOALLOC_PLAN_MAX_EXPERTS 256
+SMOE_API int smoe_dispatch_plan_noalloc(const int32_t* idx, int T, int k, int E, int capacity,
+                                        int row_align, int32_t* expert_counts,
+                                        int32_t* expert_offsets, int32_t* slot_row,
+                                        int32_t* row_token, int64_t rows_cap,
+                                        smoe_stream_t stream);
 
 /* rows[r,:] = x[row_token[r],:] for r < expert_offsets[E] (zero rows for token -1).
  * Replaces: x.repeat_interleave(2)[sort_idx] and recv_x[expert_order]

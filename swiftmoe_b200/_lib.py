@@ -49,6 +49,7 @@ SIGNATURES = {
     "smoe_plan_workspace_size": (_sz, [_i32, _i32, _i32]),
     "smoe_plan_rows_cap": (_i64, [_i32, _i32, _i32, _i32, _i32]),
     "smoe_dispatch_plan": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _sz, _vp]),
+    "smoe_dispatch_plan_noalloc": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
     "smoe_permute_rows": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i64, _vp, _vp]),
     "smoe_combine": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
     "smoe_grouped_gemm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32, _i64, _i32, _i32, _vp]),

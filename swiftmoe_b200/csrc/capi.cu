@@ -263,6 +263,7 @@ const char* smoe_status_string(int s) {
     case SMOE_ERR_TIMEOUT: return "device wait timed out";
     case SMOE_ERR_UNSUPPORTED: return "unsupported shape or dtype";
     case SMOE_ERR_WORKSPACE: return "workspace too small";
+    case SMOE_ERR_TOO_LARGE: return "size beyond the fixed maximum of this entry point";
     default: return "unknown status";
   }
 }
@@ -648,3 +649,6 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
 }
 
 }  // extern "C"
+
+// Allocation-free dispatch plan (static device scratch); see noalloc_plan.cu.
+#include "noalloc_plan.cu"
