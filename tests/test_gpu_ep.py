@@ -1,0 +1,97 @@
+"""Expert parallelism on 2+ GPUs (NCCL): the drop-in UltimateMoE on every rank against
+the oracle's multi-rank forward (experts split in contiguous blocks, capacity cut in
+(source rank, token, slot) order).  Skipped on machines with fewer than two GPUs."""
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, ws, port, cfg, out_dir):
+    sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "tests" / "golden")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
+                      NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    import synth
+    from oracle import moe_oracle as O
+    from util import max_rel_err, rounded
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    T, d, E, k, F, cf, shared = cfg
+    dt = torch.bfloat16
+    w1, w3, w2 = synth.swiglu_weights(3, E, d, F, init="normal", std=0.02)
+    g = synth.normal(4, (E, d), 0.02)
+    sw = synth.swiglu_weights(5, 1, d, F, init="normal", std=0.02) if shared else None
+    xs = [rounded(synth.normal(100 + r, (T, d), 1.0), dt) for r in range(ws)]
+    import swiftmoe_b200 as S
+    m = S.UltimateMoE(E, d, use_fp16=False, dtype=dt, top_k=k, expert_type="swiglu", d_ff=F,
+                      capacity_factor=cf, num_shared_experts=1 if shared else 0, d_ff_shared=F,
+                      use_nccl_opt=False, device=dev)
+    El = E // ws
+    sl = slice(rank * El, (rank + 1) * El)
+    with torch.no_grad():
+        m.gate_weight.copy_(torch.from_numpy(g))
+        m.w1.copy_(torch.from_numpy(w1[sl])); m.w3.copy_(torch.from_numpy(w3[sl])); m.w2.copy_(torch.from_numpy(w2[sl]))
+        if shared:
+            m.shared_w1.copy_(torch.from_numpy(sw[0][0])); m.shared_w3.copy_(torch.from_numpy(sw[1][0]))
+            m.shared_w2.copy_(torch.from_numpy(sw[2][0]))
+    out = m(torch.from_numpy(xs[rank]).to(dev, dt)).float().cpu().numpy()
+    out2 = m(torch.from_numpy(xs[rank]).to(dev, dt)).float().cpu().numpy()   # second call: same bits
+    r = lambda a: rounded(a, dt)
+    p = O.MoEParams(gate=r(g), expert_type="swiglu", w1=r(w1), w3=r(w3), w2=r(w2))
+    if shared:
+        p.sw1, p.sw3, p.sw2 = r(sw[0]), r(sw[1]), r(sw[2])
+    refs, aux = O.moe_forward(xs, p, ws=ws, k=k, capacity_factor=cf, acc=np.float64, return_aux=True)
+    from swiftmoe_b200 import kernels
+    same = []
+    for rr in range(ws):
+        idx, _ = kernels.router(torch.from_numpy(xs[rr]).to(dev, dt), m.gate_weight, k)
+        same.append((idx.cpu().numpy() == aux["routed"][rr][0]).all(1))
+    if cf is None:
+        rows = same[rank]
+        err = max_rel_err(out[rows], refs[rank][rows])
+    else:
+        # with a capacity, a near-tie routing flip on any rank can move the cut; compare
+        # only when routing agrees everywhere
+        err = max_rel_err(out, refs[rank]) if all(s.all() for s in same) else 0.0
+    np.save(os.path.join(out_dir, f"r{rank}.npy"),
+            np.array([err, float(np.array_equal(out, out2)), float(same[rank].mean())]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+CASES = [(300, 256, 8, 2, 512, None, False), (257, 256, 16, 2, 256, 1.0, False),
+         (200, 128, 32, 8, 128, None, True)]
+
+
+@pytest.mark.parametrize("cfg", CASES)
+def test_ep_layer_matches_oracle(tmp_path, cfg):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two or more GPUs")
+    ws = 4 if n >= 4 and cfg[2] % 4 == 0 else 2
+    mp.spawn(_worker, args=(ws, _port(), cfg, str(tmp_path)), nprocs=ws, join=True)
+    for r in range(ws):
+        err, same_bits, agree = np.load(tmp_path / f"r{r}.npy")
+        assert agree > 0.99
+        assert err <= 2e-2, (r, err)
+        assert same_bits == 1.0
