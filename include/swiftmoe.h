@@ -165,13 +165,17 @@ SMOE_API int smoe_gather_rows(const void* src, int dtype, int d, const int32_t* 
  *   expert_offsets[E_l+1] start row of each local expert; [E_l] = total kept rows
  *   row_src [>= n_recv]   received row that feeds each expert row
  *   recv_dst[n_recv]      expert row of each received row, -1 when dropped
+ * pos_base [ws, E_l] (device, may be NULL): position, in expert le's global
+ * (source rank, token, slot) order, of the first row of segment (s, le) -- used when a
+ * batch is exchanged in token chunks, so the capacity cut stays the whole batch's.
+ * NULL means the segments of this call are the whole batch.
  * Replaces: the receive-side bookkeeping of models/ultimate_moe.py:128-141 and the
  * regrouping by local expert at :224-231.                                             */
 SMOE_API size_t smoe_ep_regroup_workspace_size(int ws, int E_l);
-SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity, int64_t n_recv,
-                                  int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_src,
-                                  int32_t* recv_dst, void* workspace, size_t workspace_bytes,
-                                  smoe_stream_t stream);
+SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity,
+                                  const int32_t* pos_base, int64_t n_recv, int32_t* expert_counts,
+                                  int32_t* expert_offsets, int32_t* row_src, int32_t* recv_dst,
+                                  void* workspace, size_t workspace_bytes, smoe_stream_t stream);
 
 /* -------------------------------------------------------------------- whole layer
  * One-GPU MoE forward: router -> plan -> permute -> expert FFN -> combine (+ shared

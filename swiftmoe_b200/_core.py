@@ -7,9 +7,10 @@ libswiftmoe:
 * world size 1, no profiling: ONE C-ABI call (``smoe_layer_fwd``) that enqueues the
   router, dispatch plan, permute, grouped expert GEMMs and combine on the current
   stream with no host synchronisation;
-* profiling or expert parallelism: the same kernels called stage by stage, with CUDA
-  events between the stages (read lazily, no synchronisation inside forward) and the
-  all-to-all exchange of ``ep.ExpertParallelExchange``.
+* world size 1 with profiling: the same call with the library recording its stage
+  events (read lazily in get_profile_summary, no synchronisation inside forward);
+* expert parallelism: the kernels called stage by stage around the chunked, overlapped
+  all-to-all of ``ep.ExpertParallelExchange``, with CUDA events at the stage boundaries.
 """
 from __future__ import annotations
 
@@ -61,12 +62,30 @@ class _StageTimer:
     def add(self, events: List[torch.cuda.Event], exposed_a2a: Optional[tuple] = None):
         self.pending.append(("torch", events, exposed_a2a))
 
+    def add_marks(self, marks: List[tuple]):
+        """(name, event) marks of an expert-parallel forward (see ep.ExpertParallelExchange)."""
+        self.pending.append(("marks", marks, None))
+
     def add_library(self, ev: "L.StageEvents"):
         """Events recorded inside smoe_layer_fwd: start, router, dispatch, gemm1, gemm2, combine."""
         self.pending.append(("lib", ev, None))
 
     def flush(self):
         for kind, events, a2a in self.pending:
+            if kind == "marks":
+                ev = dict(events)
+                events[-1][1].synchronize()
+                span = lambda a, b: ev[a].elapsed_time(ev[b])
+                names = [n for n, _ in events]
+                self.data["Router"].append(span("start", "router"))
+                self.data["Dispatch_Comm"].append(span("router", "counts_done"))
+                self.data["Expert_Compute"].append(sum(span(n, n.replace("_start", "_end")) for n in names
+                                                       if n.startswith("experts") and n.endswith("_start")))
+                self.data["Combine_Comm"].append(span("combine_start", "end"))
+                exposed = span("counts_start", "counts_done") + sum(
+                    span(n, n.replace("_before", "_after")) for n in names if n.endswith("_before"))
+                self.data["Exposed_A2A"].append(exposed)
+                continue
             if kind == "lib":
                 spans = [(0, 1), (1, 2), (2, 4), (4, 5)]
                 for name, (i, j) in zip(STAGES, spans):
@@ -227,33 +246,32 @@ class MoECore(nn.Module):
         prof = self.enable_profiling
         dev = x.device
         T = x.shape[0]
-        ev = [self._timer.mark(dev)] if prof else None
+        marks = []
+
+        def mark(name):
+            if prof:
+                marks.append((name, self._timer.mark(dev)))
+
+        mark("start")
         idx, w = K.router(x, self._gate(), self.top_k, self._logit_bias())
-        if prof:
-            ev.append(self._timer.mark(dev))
-        a2a = None
+        mark("router")
+        shared = self._shared_out(x)
         if self.ws == 1:
             plan = K.dispatch_plan(idx, self.num_experts, self._capacity(T))
             xe = K.permute_rows(x, plan["row_token"], plan["offsets"], plan["rows_cap"])
-            offsets = plan["offsets"]
-        else:
-            xe, offsets, st = self.comm.dispatch(x, idx, self._capacity(T))
-        if prof:
-            ev.append(self._timer.mark(dev))
-        y = self._experts(xe, offsets)
-        shared = self._shared_out(x)
-        if prof:
-            ev.append(self._timer.mark(dev))
-        if self.ws == 1:
+            mark("counts_start")
+            mark("counts_done")
+            mark("experts0_start")
+            y = self._experts(xe, plan["offsets"])
+            mark("experts0_end")
+            mark("combine_start")
             out = K.combine(y, plan["slot_row"], w, T, self.top_k, shared=shared)
         else:
-            out = self.comm.combine(y, st, w, shared=shared)
+            out = self.comm.forward(x, idx, w, self._capacity(T), self._experts, shared=shared,
+                                    timer=mark if prof else None)
+        mark("end")
         if prof:
-            ev.append(self._timer.mark(dev))
-            if self.ws > 1:
-                # the exchange runs on the compute stream, so all of it is exposed
-                a2a = [(ev[1], ev[2]), (ev[3], ev[4])]
-            self._timer.add(ev, a2a)
+            self._timer.add_marks(marks)
         return out
 
     # ------------------------------------------------------------ profiling API

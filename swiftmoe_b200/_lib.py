@@ -56,7 +56,7 @@ SIGNATURES = {
     "smoe_transpose_batched": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "smoe_gather_rows": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _vp]),
     "smoe_ep_regroup_workspace_size": (_sz, [_i32, _i32]),
-    "smoe_ep_regroup_plan": (_i32, [_vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "smoe_ep_regroup_plan": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "smoe_event_create": (_i32, [C.POINTER(_vp)]),
     "smoe_event_destroy": (_i32, [_vp]),
     "smoe_event_record": (_i32, [_vp, _vp]),

@@ -467,30 +467,31 @@ int smoe_gather_rows(const void* src, int dtype, int d, const int32_t* index, in
 
 size_t smoe_ep_regroup_workspace_size(int ws, int E_l) {
   if (ws < 1 || E_l < 1) return 0;
-  return 2 * align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256);
+  return 3 * align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256);
 }
 
-int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity, int64_t n_recv,
-                         int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_src, int32_t* recv_dst,
-                         void* workspace, size_t workspace_bytes, smoe_stream_t stream) {
+int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capacity, const int32_t* pos_base,
+                         int64_t n_recv, int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_src,
+                         int32_t* recv_dst, void* workspace, size_t workspace_bytes, smoe_stream_t stream) {
   cudaStream_t st = (cudaStream_t)stream;
   if (ws < 1 || E_l < 1 || n_recv < 0 || n_recv > INT32_MAX || (int64_t)ws * E_l > (1 << 20)) return SMOE_ERR_INVALID;
   if (!recv_counts || !expert_counts || !expert_offsets) return SMOE_ERR_INVALID;
   if (n_recv > 0 && (!row_src || !recv_dst)) return SMOE_ERR_INVALID;
   if (!workspace || workspace_bytes < smoe_ep_regroup_workspace_size(ws, E_l)) return SMOE_ERR_WORKSPACE;
+  const size_t slab = align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256);
   int32_t* seg_start = static_cast<int32_t*>(workspace);
-  int32_t* src_base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
-                                                 align_up(((size_t)ws * E_l + 1) * sizeof(int32_t), 256));
+  int32_t* src_base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + slab);
+  int32_t* kept_base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + 2 * slab);
   const int smem = (E_l + ws) * (int)sizeof(int);
   static SmemGrant done;
   SMOE_CK(ensure_smem(ep_regroup_scan_kernel, smem, &done));
-  ep_regroup_scan_kernel<<<1, 1024, smem, st>>>(recv_counts, ws, E_l, capacity, expert_counts, expert_offsets,
-                                                seg_start, src_base);
+  ep_regroup_scan_kernel<<<1, 1024, smem, st>>>(recv_counts, ws, E_l, capacity, pos_base, expert_counts,
+                                                expert_offsets, seg_start, src_base, kept_base);
   SMOE_CK(cudaGetLastError());
   if (n_recv > 0) {
     const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n_recv, 256), (int64_t)device_sms() * 8);
-    ep_regroup_rows_kernel<<<grid, 256, 0, st>>>(seg_start, src_base, expert_offsets, ws * E_l, E_l, capacity, n_recv,
-                                                 row_src, recv_dst);
+    ep_regroup_rows_kernel<<<grid, 256, 0, st>>>(seg_start, src_base, kept_base, expert_offsets, ws * E_l, E_l,
+                                                 capacity, n_recv, row_src, recv_dst);
     SMOE_CK(cudaGetLastError());
   }
   return SMOE_OK;

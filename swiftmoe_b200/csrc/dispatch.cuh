@@ -307,22 +307,30 @@ __device__ int block_exclusive_scan(int* data, int n, int* scratch) {
 // Writes seg_start[ws*El+1] (receive row where segment (s, le) starts), src_base[ws*El]
 // (position inside expert le of the segment's first row), expert counts and offsets.
 __global__ void __launch_bounds__(1024) ep_regroup_scan_kernel(const int32_t* __restrict__ rc, int ws, int El,
-                                                               int capacity, int32_t* __restrict__ counts,
+                                                               int capacity, const int32_t* __restrict__ pos_base,
+                                                               int32_t* __restrict__ counts,
                                                                int32_t* __restrict__ offsets,
                                                                int32_t* __restrict__ seg_start,
-                                                               int32_t* __restrict__ src_base) {
+                                                               int32_t* __restrict__ src_base,
+                                                               int32_t* __restrict__ kept_base) {
   extern __shared__ int sh[];  // [El] kept counts, then [ws] row totals
   __shared__ int scratch[32];
   int* s_kept = sh;
   int* s_row = sh + El;
   for (int le = threadIdx.x; le < El; le += blockDim.x) {
-    int run = 0;
+    // src_base: global position of the segment's first row (capacity test);
+    // kept_base: rows of this call already kept for le before the segment (layout)
+    int run = 0, kept = 0;
     for (int s = 0; s < ws; ++s) {
-      src_base[s * El + le] = run;
-      run += rc[s * El + le];
+      const int c = rc[s * El + le];
+      const int pos = pos_base != nullptr ? pos_base[s * El + le] : run;
+      src_base[s * El + le] = pos;
+      kept_base[s * El + le] = kept;
+      run += c;
+      kept += capacity > 0 ? max(0, min(c, capacity - pos)) : c;
     }
     counts[le] = run;
-    s_kept[le] = capacity > 0 ? min(run, capacity) : run;
+    s_kept[le] = kept;
   }
   for (int s = threadIdx.x; s < ws; s += blockDim.x) {
     int run = 0;
@@ -346,6 +354,7 @@ __global__ void __launch_bounds__(1024) ep_regroup_scan_kernel(const int32_t* __
 // Part 2: one thread per received row.
 __global__ void __launch_bounds__(256) ep_regroup_rows_kernel(const int32_t* __restrict__ seg_start,
                                                               const int32_t* __restrict__ src_base,
+                                                              const int32_t* __restrict__ kept_base,
                                                               const int32_t* __restrict__ offsets, int nseg, int El,
                                                               int capacity, int64_t n_recv,
                                                               int32_t* __restrict__ row_src,
@@ -357,11 +366,11 @@ __global__ void __launch_bounds__(256) ep_regroup_rows_kernel(const int32_t* __r
       if (seg_start[mid] <= r) lo = mid; else hi = mid - 1;
     }
     const int le = lo % El;
-    const int pos = src_base[lo] + (int)(r - seg_start[lo]);
-    if (capacity > 0 && pos >= capacity) {
+    const int i = (int)(r - seg_start[lo]);
+    if (capacity > 0 && src_base[lo] + i >= capacity) {
       recv_dst[r] = -1;
     } else {
-      const int dst = offsets[le] + pos;
+      const int dst = offsets[le] + kept_base[lo] + i;
       recv_dst[r] = dst;
       row_src[dst] = (int32_t)r;
     }

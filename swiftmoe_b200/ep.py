@@ -1,4 +1,5 @@
-"""Expert-parallel token exchange (dispatch / combine all-to-all) over torch.distributed.
+"""Expert-parallel token exchange (dispatch / combine all-to-all) over torch.distributed,
+overlapped with the expert GEMMs.
 
 Replaces ``MoEAsyncCommHandler`` (models/ultimate_moe.py:104-155) and
 ``StandardMoE._dispatch_tokens`` / ``_combine_tokens`` (models/baseline_moe.py:69-189).
@@ -13,10 +14,14 @@ from the reference:
 * gate weights and local expert ids are NOT sent (the reference sends three payloads,
   :139-141): the receiver derives the local expert of every row from the count matrix
   and the weights are applied by the sender's combine;
-* one device-to-host copy of the count matrix per forward (the reference does four:
+* ONE device-to-host copy of the count matrix per forward (the reference makes four:
   ``.item()``, two ``.tolist()`` and the per-expert ``.cpu()`` at :130,136-137,231);
+* the batch travels in token chunks on a communication stream: the dispatch
+  all-to-all of chunk c+1 and the return all-to-all of chunk c-1 run while the expert
+  GEMMs of chunk c run on the compute stream;
 * the capacity cut (extension) happens on the receiver in (source rank, token, slot)
-  order, and dropped rows travel back as zeros so the sender's combine needs no mask.
+  order over the whole batch, and dropped rows travel back as zeros so the sender's
+  combine needs no mask.
 
 ``kernels`` is the module of device operations.  Production code uses
 ``swiftmoe_b200.kernels`` (CUDA); CPU tests substitute a numpy double to exercise the
@@ -25,8 +30,9 @@ collective choreography on gloo ranks.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Optional
+from typing import Callable, List, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -43,9 +49,28 @@ class DispatchState:
     k: int
 
 
+def chunk_bounds(T: int, chunks: int) -> List[tuple]:
+    c = max(1, min(chunks, T)) if T > 0 else 1
+    edges = [T * i // c for i in range(c + 1)]
+    return [(edges[i], edges[i + 1]) for i in range(c)]
+
+
+def capacity_positions(recv_counts: np.ndarray, capacity: int):
+    """recv_counts [C, ws, E_l] (chunk, source rank, local expert) -> position base
+    [C, ws, E_l]: where each (chunk, source) segment starts in its expert's global
+    (source rank, token, slot) order.  Chunks are token ranges of one source, so the
+    order is source-major, then chunk."""
+    C, ws, El = recv_counts.shape
+    per_src = recv_counts.sum(0)                        # [ws, E_l]
+    src_start = np.cumsum(per_src, 0) - per_src         # rows of earlier sources
+    chunk_start = np.cumsum(recv_counts, 0) - recv_counts
+    return (src_start[None] + chunk_start).astype(np.int32)
+
+
 class ExpertParallelExchange:
     def __init__(self, num_experts: int, world_size: int, rank: int, d_model: int,
-                 group: Optional[dist.ProcessGroup] = None, kernels=None):
+                 group: Optional[dist.ProcessGroup] = None, kernels=None, chunks: int = 4,
+                 min_chunk_tokens: int = 2048):
         if num_experts % world_size:
             raise ValueError("num_experts must be divisible by the world size")
         self.num_experts = num_experts
@@ -54,29 +79,143 @@ class ExpertParallelExchange:
         self.d_model = d_model
         self.exp_per_rank = num_experts // world_size
         self.group = group
+        self.chunks = chunks
+        self.min_chunk_tokens = min_chunk_tokens
         if kernels is None:
             from . import kernels as _k
             kernels = _k
         self.k = kernels
         self._host = None
+        self._comm_stream = {}
+        self.last_rows = 0          # expert rows computed by this rank in the last forward
 
-    def _counts_to_host(self, counts: torch.Tensor, recv_counts: torch.Tensor):
-        """The one host synchronisation of the forward: both count vectors at once."""
-        n = counts.numel()
-        if counts.is_cuda:
-            if self._host is None or self._host.numel() < 2 * n:
-                self._host = torch.empty(2 * n, dtype=torch.int32, pin_memory=True)
-            h = self._host
-            h[:n].copy_(counts, non_blocking=True)
-            h[n:2 * n].copy_(recv_counts, non_blocking=True)
-            torch.cuda.current_stream(counts.device).synchronize()
-            return h[:n].clone(), h[n:2 * n].clone()
-        return counts.clone(), recv_counts.clone()
+    # ------------------------------------------------------------------ helpers
+    def _stream(self, device):
+        if device.type != "cuda":
+            return None
+        s = self._comm_stream.get(device.index)
+        if s is None:
+            s = self._comm_stream[device.index] = torch.cuda.Stream(device)
+        return s
 
+    def _to_host(self, *ts):
+        """The one host synchronisation of the forward: all count vectors at once."""
+        n = sum(t.numel() for t in ts)
+        if ts[0].is_cuda:
+            if self._host is None or self._host.numel() < n:
+                self._host = torch.empty(n, dtype=torch.int32, pin_memory=True)
+            h, o = self._host, 0
+            for t in ts:
+                h[o:o + t.numel()].copy_(t.reshape(-1), non_blocking=True)
+                o += t.numel()
+            torch.cuda.current_stream(ts[0].device).synchronize()
+            out, o = [], 0
+            for t in ts:
+                out.append(h[o:o + t.numel()].clone().numpy().reshape(t.shape))
+                o += t.numel()
+            return out
+        return [t.numpy().copy() for t in ts]
+
+    def n_chunks(self, T: int) -> int:
+        return max(1, min(self.chunks, T // max(self.min_chunk_tokens, 1)))
+
+    # ------------------------------------------------------------------ the layer
+    def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, capacity: int,
+                experts: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
+                shared: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
+        """Dispatch, expert compute (``experts(rows, offsets)``) and combine for one batch.
+
+        ``timer`` (optional) is called with a stage-boundary name at points of the compute
+        stream's timeline; the profiler records an event there.  The spans between
+        ``wait_*_before`` and ``wait_*_after`` are the time the compute stream stalls on
+        communication, i.e. the exposed all-to-all time."""
+        ws, El, E = self.world_size, self.exp_per_rank, self.num_experts
+        T, k = idx.shape
+        d = x.shape[1]
+        dev = x.device
+        bounds = chunk_bounds(T, self.n_chunks(T))
+        C = len(bounds)
+        comp = torch.cuda.current_stream(dev) if dev.type == "cuda" else None
+        comm = self._stream(dev)
+
+        def mark(name):
+            if timer is not None:
+                timer(name)
+
+        # per-chunk send plans and send buffers (compute stream)
+        plans, sends = [], []
+        for (a, b) in bounds:
+            p = self.k.dispatch_plan(idx[a:b], E)
+            plans.append(p)
+            sends.append(self.k.permute_rows(x[a:b], p["row_token"], p["offsets"], p["rows_cap"]))
+        counts = torch.stack([p["counts"] for p in plans]).view(C, ws, El)        # [C, dst, El]
+        send_counts = counts.transpose(0, 1).contiguous()                           # [dst, C, El]
+        recv_counts = torch.empty_like(send_counts)                                 # [src, C, El]
+        mark("counts_start")
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        hc, hr = self._to_host(send_counts, recv_counts)
+        mark("counts_done")
+        hr_c = np.ascontiguousarray(hr.transpose(1, 0, 2))                          # [C, src, El]
+        pos = capacity_positions(hr_c, capacity) if capacity > 0 else None
+        pos_dev = None
+        if pos is not None:
+            pos_dev = torch.from_numpy(pos).to(dev, non_blocking=True)
+
+        send_splits = [[int(v) for v in hc[:, c, :].sum(1)] for c in range(C)]
+        recv_splits = [[int(v) for v in hr[:, c, :].sum(1)] for c in range(C)]
+        recv_rows = [torch.empty((max(sum(recv_splits[c]), 1), d), dtype=x.dtype, device=dev) for c in range(C)]
+        ev_sent = []
+        # dispatch all-to-alls on the communication stream
+        if comm is not None:
+            comm.wait_stream(comp)
+        for c in range(C):
+            with _maybe_stream(comm):
+                dist.all_to_all_single(recv_rows[c][:sum(recv_splits[c])], sends[c][:sum(send_splits[c])],
+                                       recv_splits[c], send_splits[c], group=self.group)
+                ev_sent.append(_record(comm))
+        # expert compute per chunk as its rows arrive (compute stream)
+        backs, states, ev_back = [], [], []
+        rows_total = 0
+        for c in range(C):
+            mark(f"wait_sent{c}_before")
+            _wait(comp, ev_sent[c])
+            mark(f"wait_sent{c}_after")
+            n_recv = sum(recv_splits[c])
+            rg = self.k.ep_regroup_plan(recv_counts[:, c, :].contiguous(), capacity, n_recv,
+                                        pos_base=None if pos_dev is None else pos_dev[c])
+            xe = self.k.permute_rows(recv_rows[c], rg["row_src"], rg["offsets"], rg["rows_cap"])
+            mark(f"experts{c}_start")
+            y = experts(xe, rg["offsets"])
+            mark(f"experts{c}_end")
+            rows_total += rg["rows_cap"]
+            backs.append(self.k.gather_rows(y, rg["recv_dst"], n_recv))
+            ev_back.append(_record(comp))
+            states.append((rg, n_recv))
+        self.last_rows = rows_total
+        # return all-to-alls (communication stream) and combine (compute stream)
+        rets = [torch.empty((max(sum(send_splits[c]), 1), d), dtype=x.dtype, device=dev) for c in range(C)]
+        ev_ret = []
+        for c in range(C):
+            _wait(comm, ev_back[c])
+            with _maybe_stream(comm):
+                dist.all_to_all_single(rets[c][:sum(send_splits[c])], backs[c][:states[c][1]],
+                                       send_splits[c], recv_splits[c], group=self.group)
+                ev_ret.append(_record(comm))
+        out = torch.empty_like(x)
+        mark("combine_start")
+        for c, (a, b) in enumerate(bounds):
+            mark(f"wait_ret{c}_before")
+            _wait(comp, ev_ret[c])
+            mark(f"wait_ret{c}_after")
+            self.k.combine(rets[c], plans[c]["slot_row"], w[a:b], b - a, k,
+                           shared=None if shared is None else shared[a:b], out=out[a:b])
+        return out
+
+
+    # ------------------------------------------------------------------ stage API
     def dispatch(self, x: torch.Tensor, idx: torch.Tensor, capacity: int = 0):
-        """Send every (token, slot) row to the rank owning its expert.
-
-        Returns (rows grouped by local expert [rows, d], expert offsets [E_l+1], state)."""
+        """Unchunked dispatch for the stage-by-stage API (StandardMoE._dispatch_tokens):
+        returns (rows grouped by local expert, expert offsets [E_l+1], state)."""
         ws, El = self.world_size, self.exp_per_rank
         T, k = idx.shape
         plan = self.k.dispatch_plan(idx, self.num_experts)
@@ -84,16 +223,15 @@ class ExpertParallelExchange:
         counts = plan["counts"]
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
-        hc, hr = self._counts_to_host(counts, recv_counts)
-        send_splits = [int(v) for v in hc.view(ws, El).sum(1).tolist()]
-        recv_splits = [int(v) for v in hr.view(ws, El).sum(1).tolist()]
+        hc, hr = self._to_host(counts, recv_counts)
+        send_splits = [int(v) for v in hc.reshape(ws, El).sum(1)]
+        recv_splits = [int(v) for v in hr.reshape(ws, El).sum(1)]
         n_send, n_recv = sum(send_splits), sum(recv_splits)
         recv_rows = torch.empty((max(n_recv, 1), x.shape[1]), dtype=x.dtype, device=x.device)
         dist.all_to_all_single(recv_rows[:n_recv], send_rows[:n_send], recv_splits, send_splits, group=self.group)
         rg = self.k.ep_regroup_plan(recv_counts.view(ws, El), capacity, n_recv)
         xe = self.k.permute_rows(recv_rows, rg["row_src"], rg["offsets"], rg["rows_cap"])
-        st = DispatchState(plan, rg, send_splits, recv_splits, n_send, n_recv, T, k)
-        return xe, rg["offsets"], st
+        return xe, rg["offsets"], DispatchState(plan, rg, send_splits, recv_splits, n_send, n_recv, T, k)
 
     def combine(self, y: torch.Tensor, st: DispatchState, w: torch.Tensor,
                 shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
@@ -102,3 +240,28 @@ class ExpertParallelExchange:
         ret = torch.empty((max(st.n_send, 1), y.shape[1]), dtype=y.dtype, device=y.device)
         dist.all_to_all_single(ret[:st.n_send], back[:st.n_recv], st.send_splits, st.recv_splits, group=self.group)
         return self.k.combine(ret, st.plan["slot_row"], w, st.T, st.k, shared=shared, out=out)
+
+
+class _NullCtx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def _maybe_stream(s):
+    return torch.cuda.stream(s) if s is not None else _NullCtx()
+
+
+def _record(s):
+    if s is None:
+        return None
+    e = torch.cuda.Event()
+    e.record(s)
+    return e
+
+
+def _wait(s, ev):
+    if s is not None and ev is not None:
+        s.wait_event(ev)

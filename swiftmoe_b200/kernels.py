@@ -139,9 +139,12 @@ def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
     return out
 
 
-def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int):
-    """recv_counts [ws, E_l] int32 -> dict(counts, offsets, row_src, recv_dst, rows_cap)."""
-    _need_cuda(recv_counts)
+def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int, pos_base: Optional[torch.Tensor] = None):
+    """recv_counts [ws, E_l] int32 -> dict(counts, offsets, row_src, recv_dst, rows_cap).
+
+    pos_base [ws, E_l] int32 (optional): global position of each segment's first row in
+    its expert's (source rank, token, slot) order, when the batch travels in chunks."""
+    _need_cuda(recv_counts, pos_base)
     ws_, El = recv_counts.shape
     lib = L.load()
     dev = recv_counts.device
@@ -151,7 +154,8 @@ def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int):
     row_src = torch.empty(max(rows_cap, 1), dtype=torch.int32, device=dev)
     recv_dst = torch.empty(max(n_recv, 1), dtype=torch.int32, device=dev)
     wsb = _workspace(dev, lib.smoe_ep_regroup_workspace_size(ws_, El))
-    L.check(lib.smoe_ep_regroup_plan(L.ptr(recv_counts), ws_, El, capacity, n_recv, L.ptr(counts), L.ptr(offsets),
+    L.check(lib.smoe_ep_regroup_plan(L.ptr(recv_counts), ws_, El, capacity, L.ptr(pos_base), n_recv, L.ptr(counts),
+                                     L.ptr(offsets),
                                      L.ptr(row_src), L.ptr(recv_dst), L.ptr(wsb), wsb.numel(), L.stream_handle(dev)),
             "smoe_ep_regroup_plan")
     return dict(counts=counts, offsets=offsets, row_src=row_src, recv_dst=recv_dst, rows_cap=rows_cap)

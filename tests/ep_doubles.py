@@ -44,22 +44,25 @@ def gather_rows(src, index, n_rows, out=None):
     return torch.from_numpy(o)
 
 
-def ep_regroup_plan(recv_counts, capacity, n_recv):
+def ep_regroup_plan(recv_counts, capacity, n_recv, pos_base=None):
     rc = recv_counts.numpy()
     ws, El = rc.shape
     tot = rc.sum(0)
-    kept = np.minimum(tot, capacity) if capacity > 0 else tot
+    base = pos_base.numpy() if pos_base is not None else (np.cumsum(rc, 0) - rc)
+    kept_seg = np.clip(capacity - base, 0, rc) if capacity > 0 else rc
+    kept = kept_seg.sum(0)
     offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
     recv_dst = -np.ones(max(n_recv, 1), np.int32)
     row_src = -np.ones(max(int(offsets[-1]), 1), np.int32)
     r = 0
     for s in range(ws):
         for le in range(El):
+            before = kept_seg[:s, le].sum()
             for i in range(rc[s, le]):
-                pos = rc[:s, le].sum() + i
-                if capacity <= 0 or pos < capacity:
-                    recv_dst[r] = offsets[le] + pos
-                    row_src[offsets[le] + pos] = r
+                if capacity <= 0 or base[s, le] + i < capacity:
+                    dst = offsets[le] + before + i
+                    recv_dst[r] = dst
+                    row_src[dst] = r
                 r += 1
     return dict(counts=torch.from_numpy(tot.astype(np.int32)), offsets=torch.from_numpy(offsets),
                 row_src=torch.from_numpy(row_src), recv_dst=torch.from_numpy(recv_dst),
@@ -76,4 +79,8 @@ def combine(y, slot_row, w, T, k, shared=None, out=None):
         o[m] += wn[m, j, None] * yn[sr[m, j]]
     if shared is not None:
         o += shared.numpy()
-    return torch.from_numpy(o.astype(np.float32))
+    res = torch.from_numpy(o.astype(np.float32))
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res

@@ -21,7 +21,7 @@ def _port():
     return p
 
 
-def _worker(rank, ws, port, E, d, T, k, cap_factor, result_dir):
+def _worker(rank, ws, port, E, d, T, k, cap_factor, chunks, result_dir):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     import torch.distributed as dist
@@ -38,26 +38,35 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, result_dir):
     xs = [np.random.default_rng(10 + r).standard_normal((T, d)).astype(np.float32) for r in range(ws)]
     x = xs[rank]
     idx, w, _ = O.route(x, gate, k)
-    ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles)
+    ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=chunks, min_chunk_tokens=1)
     cap = capacity_rows(cap_factor, T, ws, k, E)
-    xe, offsets, st = ex.dispatch(torch.from_numpy(x), torch.from_numpy(idx), cap)
     El = E // ws
-    off = offsets.numpy()
-    y = np.zeros((xe.shape[0], d), np.float32)
-    for le in range(El):
-        e = rank * El + le
-        y[off[le]:off[le + 1]] = xe.numpy()[off[le]:off[le + 1]] @ W[e].T
-    out = ex.combine(torch.from_numpy(y), st, torch.from_numpy(w)).numpy()
+
+    def experts(xe, offsets):
+        off = offsets.numpy()
+        y = np.zeros((xe.shape[0], d), np.float32)
+        for le in range(El):
+            e = rank * El + le
+            y[off[le]:off[le + 1]] = xe.numpy()[off[le]:off[le + 1]] @ W[e].T
+        return torch.from_numpy(y)
+
+    # chunked, overlapped layer path
+    out = ex.forward(torch.from_numpy(x), torch.from_numpy(idx), torch.from_numpy(w), cap, experts).numpy()
+    # unchunked stage API (dispatch / combine)
+    xe, offsets, st = ex.dispatch(torch.from_numpy(x), torch.from_numpy(idx), cap)
+    out_stage = ex.combine(experts(xe, offsets), st, torch.from_numpy(w)).numpy()
     p = O.MoEParams(gate=gate, expert_type="linear", expert_w=np.ascontiguousarray(W.transpose(0, 2, 1)))
     refs = O.moe_forward(xs, p, ws=ws, k=k, capacity_factor=cap_factor)
-    np.save(os.path.join(result_dir, f"err{rank}.npy"), np.array([np.abs(out - refs[rank]).max()]))
+    np.save(os.path.join(result_dir, f"err{rank}.npy"),
+            np.array([max(np.abs(out - refs[rank]).max(), np.abs(out_stage - refs[rank]).max())]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("ws,E,k,cf", [(2, 8, 2, None), (2, 8, 2, 1.0), (4, 8, 3, None), (4, 16, 2, 0.5)])
-def test_ep_exchange_matches_oracle(tmp_path, ws, E, k, cf):
+@pytest.mark.parametrize("ws,E,k,cf,chunks", [(2, 8, 2, None, 1), (2, 8, 2, 1.0, 3), (4, 8, 3, None, 4),
+                                               (4, 16, 2, 0.5, 2), (2, 4, 2, 0.7, 5)])
+def test_ep_exchange_matches_oracle(tmp_path, ws, E, k, cf, chunks):
     T, d = 23, 12
-    mp.spawn(_worker, args=(ws, _port(), E, d, T, k, cf, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_worker, args=(ws, _port(), E, d, T, k, cf, chunks, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         assert float(np.load(tmp_path / f"err{r}.npy")[0]) <= 1e-5

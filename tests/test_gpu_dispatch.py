@@ -127,3 +127,25 @@ def test_ep_regroup_plan(K, ws, El, cap):
     for r, dst in enumerate(recv_dst):
         if dst >= 0:
             assert rs[dst] == r
+
+
+@pytest.mark.parametrize("ws,El,cap,chunks", [(2, 4, 9, 3), (4, 2, 5, 2), (8, 1, 40, 4)])
+def test_ep_regroup_plan_chunked_capacity(K, ws, El, cap, chunks):
+    """Chunk c of a batch exchanged in token chunks: the capacity cut uses each segment's
+    position in the whole batch's (source rank, token, slot) order (pos_base)."""
+    import ep_doubles
+    from swiftmoe_b200.ep import capacity_positions
+    rng = np.random.default_rng(ws * 100 + El)
+    rc_all = rng.integers(0, 7, size=(chunks, ws, El)).astype(np.int32)
+    pos = capacity_positions(rc_all, cap)
+    for c in range(chunks):
+        rc = rc_all[c]
+        n_recv = int(rc.sum())
+        got = K.ep_regroup_plan(to_dev(rc, torch.int32), cap, n_recv, pos_base=to_dev(pos[c], torch.int32))
+        exp = ep_doubles.ep_regroup_plan(torch.from_numpy(rc), cap, n_recv, torch.from_numpy(pos[c]))
+        assert (got["offsets"].cpu().numpy() == exp["offsets"].numpy()).all()
+        assert (got["recv_dst"].cpu().numpy()[:n_recv] == exp["recv_dst"].numpy()[:n_recv]).all()
+    # the chunks together keep exactly min(total, cap) rows of every expert
+    kept = sum(int(K.ep_regroup_plan(to_dev(rc_all[c], torch.int32), cap, int(rc_all[c].sum()),
+                                     pos_base=to_dev(pos[c], torch.int32))["offsets"][-1]) for c in range(chunks))
+    assert kept == int(np.minimum(rc_all.sum((0, 1)), cap).sum())
