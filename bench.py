@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ep-chunks", type=int, default=None, help="token chunks of the EP exchange")
+    ap.add_argument("--ep-transport", default=None, choices=["p2p", "collective"])
     return ap.parse_args()
 
 
@@ -222,6 +224,11 @@ def main():
     with torch.no_grad():
         g = torch.Generator(device=dev).manual_seed(7)   # identical gate on every rank
         model.gate_weight.copy_(torch.randn(model.gate_weight.shape, generator=g, device=dev) * 0.02)
+    if ws > 1:
+        if args.ep_chunks:
+            model.comm.chunks = args.ep_chunks
+        if args.ep_transport:
+            model.comm.transport = args.ep_transport
     x = torch.randn((T, D_MODEL), device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(100 + rank))
     out = torch.empty_like(x)
 
@@ -361,6 +368,8 @@ def main():
                 "data": "synthetic: x ~ N(0,1), weights N(0,0.02), seeded",
                 "config": {"workload": WORKLOAD, "d_model": D_MODEL, "num_experts": N_EXPERTS, "top_k": TOP_K,
                            "d_ff": D_FF, "tokens_per_gpu": T, "parallelism": f"ep{ws}",
+                           "ep_exchange": None if ws == 1 else
+                           f"{model.comm.transport} transport, {model.comm.n_chunks(T)} token chunks",
                            "l2": "inputs larger than L2: x 128 MiB and 2.82 GB of expert weights read every step"},
                 "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
                 "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,

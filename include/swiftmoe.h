@@ -177,6 +177,22 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
                                   int32_t* expert_offsets, int32_t* row_src, int32_t* recv_dst,
                                   void* workspace, size_t workspace_bytes, smoe_stream_t stream);
 
+/* Expert-parallel exchange buffers.  These are the only allocations of the library:
+ * each rank allocates its receive / return buffers once (grown when a batch needs
+ * more), exports a CUDA IPC handle, and every rank opens every peer's buffer, so rows
+ * move with plain device-to-device copies over NVLink (copy engines, no SMs), in the
+ * place of the reference's payload all_to_all_single calls
+ * (models/ultimate_moe.py:139-141,152).  ipc_handle points to 64 bytes.             */
+#define SMOE_IPC_HANDLE_BYTES 64
+SMOE_API int smoe_ep_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);
+SMOE_API int smoe_ep_buffer_destroy(void* dev_ptr);
+SMOE_API int smoe_ep_peer_open(const void* ipc_handle, void** peer_ptr);
+SMOE_API int smoe_ep_peer_close(void* peer_ptr);
+/* n device-to-device copies dst[i] <- src[i] (bytes[i]) on the stream, in order; the
+ * pointers may be IPC-opened peer buffers.  One cudaMemcpyAsync per segment.         */
+SMOE_API int smoe_copy_segments(void* const* dst, const void* const* src, const size_t* bytes, int n,
+                                smoe_stream_t stream);
+
 /* -------------------------------------------------------------------- whole layer
  * One-GPU MoE forward: router -> plan -> permute -> expert FFN -> combine (+ shared
  * expert).  Replaces UltimateMoE.forward (models/ultimate_moe.py:254-342) and

@@ -57,6 +57,11 @@ SIGNATURES = {
     "smoe_gather_rows": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _vp]),
     "smoe_ep_regroup_workspace_size": (_sz, [_i32, _i32]),
     "smoe_ep_regroup_plan": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "smoe_ep_buffer_create": (_i32, [_sz, C.POINTER(_vp), _vp]),
+    "smoe_ep_buffer_destroy": (_i32, [_vp]),
+    "smoe_ep_peer_open": (_i32, [_vp, C.POINTER(_vp)]),
+    "smoe_ep_peer_close": (_i32, [_vp]),
+    "smoe_copy_segments": (_i32, [C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_sz), _i32, _vp]),
     "smoe_event_create": (_i32, [C.POINTER(_vp)]),
     "smoe_event_destroy": (_i32, [_vp]),
     "smoe_event_record": (_i32, [_vp, _vp]),

@@ -540,6 +540,55 @@ bool layer_plan(const smoe_layer_args* a, LayerPlan* p) {
 }
 }  // namespace
 
+int smoe_ep_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return SMOE_ERR_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == SMOE_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  SMOE_CK(cudaMalloc(&p, bytes));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    report_cuda_error(e, "cudaIpcGetMemHandle", __FILE__, __LINE__);
+    return SMOE_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return SMOE_OK;
+}
+
+int smoe_ep_buffer_destroy(void* dev_ptr) {
+  if (!dev_ptr) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaFree(dev_ptr));
+  return SMOE_OK;
+}
+
+int smoe_ep_peer_open(const void* ipc_handle, void** peer_ptr) {
+  if (!ipc_handle || !peer_ptr) return SMOE_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  SMOE_CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *peer_ptr = p;
+  return SMOE_OK;
+}
+
+int smoe_ep_peer_close(void* peer_ptr) {
+  if (!peer_ptr) return SMOE_ERR_INVALID;
+  SMOE_CK(cudaIpcCloseMemHandle(peer_ptr));
+  return SMOE_OK;
+}
+
+int smoe_copy_segments(void* const* dst, const void* const* src, const size_t* bytes, int n, smoe_stream_t stream) {
+  if (n < 0 || (n > 0 && (!dst || !src || !bytes))) return SMOE_ERR_INVALID;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] == 0) continue;
+    if (!dst[i] || !src[i]) return SMOE_ERR_INVALID;
+    SMOE_CK(cudaMemcpyAsync(dst[i], src[i], bytes[i], cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  }
+  return SMOE_OK;
+}
+
 int smoe_event_create(void** event) {
   if (!event) return SMOE_ERR_INVALID;
   cudaEvent_t e;

@@ -70,7 +70,7 @@ def capacity_positions(recv_counts: np.ndarray, capacity: int):
 class ExpertParallelExchange:
     def __init__(self, num_experts: int, world_size: int, rank: int, d_model: int,
                  group: Optional[dist.ProcessGroup] = None, kernels=None, chunks: int = 4,
-                 min_chunk_tokens: int = 2048):
+                 min_chunk_tokens: int = 2048, transport: str = "auto"):
         if num_experts % world_size:
             raise ValueError("num_experts must be divisible by the world size")
         self.num_experts = num_experts
@@ -88,6 +88,11 @@ class ExpertParallelExchange:
         self._host = None
         self._comm_stream = {}
         self.last_rows = 0          # expert rows computed by this rank in the last forward
+        if transport not in ("auto", "p2p", "collective"):
+            raise ValueError("transport must be 'auto', 'p2p' or 'collective'")
+        self.transport = transport
+        self._bufs = None           # (receive, return) PeerBuffers of the p2p transport
+        self._flag = None
 
     # ------------------------------------------------------------------ helpers
     def _stream(self, device):
@@ -124,6 +129,16 @@ class ExpertParallelExchange:
                 experts: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
                 shared: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
         """Dispatch, expert compute (``experts(rows, offsets)``) and combine for one batch.
+
+        CUDA tensors use the peer-copy transport (``_forward_p2p``) unless
+        ``transport="collective"``; CPU tensors (gloo) use all_to_all_single."""
+        use_p2p = self.transport == "p2p" or (self.transport == "auto" and x.is_cuda)
+        if use_p2p:
+            return self._forward_p2p(x, idx, w, capacity, experts, shared, timer)
+        return self._forward_collective(x, idx, w, capacity, experts, shared, timer)
+
+    def _forward_collective(self, x, idx, w, capacity, experts, shared=None, timer=None):
+        """Payload exchange through ``all_to_all_single`` (NCCL or gloo).
 
         ``timer`` (optional) is called with a stage-boundary name at points of the compute
         stream's timeline; the profiler records an event there.  The spans between
@@ -211,6 +226,122 @@ class ExpertParallelExchange:
                            shared=None if shared is None else shared[a:b], out=out[a:b])
         return out
 
+
+    # ------------------------------------------------------------------ peer copies
+    def _barrier(self, stream):
+        """Orders this rank's copies issued on `stream` before every rank's next work on
+        its own `stream`: a one-int all-reduce, which on each rank starts only after that
+        rank's earlier copies completed."""
+        if self._flag is None or self._flag.device != stream.device:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=stream.device)
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self._flag, group=self.group)
+
+    def _forward_p2p(self, x, idx, w, capacity, experts, shared=None, timer=None):
+        """Rows travel by device-to-device copies into the peers' receive / return buffers
+        (copy engines over NVLink), chunk by chunk on the communication stream, while the
+        compute stream runs the expert GEMMs of the chunks that have arrived."""
+        from .p2p import PeerBuffers, copy_segments, view
+        ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
+        T, k = idx.shape
+        d = x.shape[1]
+        dev = x.device
+        rb = d * x.element_size()
+        bounds = chunk_bounds(T, self.n_chunks(T))
+        C = len(bounds)
+        comp = torch.cuda.current_stream(dev)
+        comm = self._stream(dev)
+        if self._bufs is None:
+            self._bufs = (PeerBuffers(self.group, me, ws, dev), PeerBuffers(self.group, me, ws, dev))
+        recv_buf, ret_buf = self._bufs
+
+        def mark(name):
+            if timer is not None:
+                timer(name)
+
+        plans, sends = [], []
+        for (a, b) in bounds:
+            p = self.k.dispatch_plan(idx[a:b], E)
+            plans.append(p)
+            sends.append(self.k.permute_rows(x[a:b], p["row_token"], p["offsets"], p["rows_cap"]))
+        counts = torch.stack([p["counts"] for p in plans])                 # [C, E]
+        G = torch.empty((ws, C, E), dtype=torch.int32, device=dev)          # [src, C, dst*El]
+        mark("counts_start")
+        # the count exchange also orders this step after every rank finished reading its
+        # buffers in the previous step (each rank joins it after its earlier work)
+        dist.all_gather_into_tensor(G.view(-1), counts.reshape(-1), group=self.group)
+        (Gh,) = self._to_host(G)
+        mark("counts_done")
+        Gh = Gh.reshape(ws, C, ws, El).astype(np.int64)
+        R = Gh.sum(3)                                   # [src, C, dst] rows src -> dst in chunk c
+        recv_c = R.sum(0)                               # [C, dst]
+        RO = np.cumsum(recv_c, 0) - recv_c              # chunk region start in dst's receive buffer
+        SO = np.cumsum(R, 0) - R                        # src offset inside dst's chunk region
+        send_c = R.sum(2)                               # [src, C]
+        SRO = np.cumsum(send_c, 1) - send_c             # chunk region start in src's return buffer
+        SD = np.cumsum(R, 2) - R                        # dst segment offset inside src's chunk region
+        recv_buf.ensure(int(max(recv_c.sum(0).max(), 1)) * rb)
+        ret_buf.ensure(int(max(send_c.sum(1).max(), 1)) * rb)
+        rc_me = G[:, :, me * El:(me + 1) * El]          # [src, C, El] received by me (device)
+        pos_dev = None
+        if capacity > 0:
+            pos = capacity_positions(np.ascontiguousarray(Gh[:, :, me, :].transpose(1, 0, 2)), capacity)
+            pos_dev = torch.from_numpy(pos).to(dev, non_blocking=True)
+
+        comm.wait_stream(comp)
+        ev_sent = []
+        for c in range(C):
+            sends[c].record_stream(comm)
+            base = sends[c].data_ptr()
+            copy_segments([(recv_buf.ptrs[r] + int(RO[c, r] + SO[me, c, r]) * rb, base + int(SD[me, c, r]) * rb,
+                            int(R[me, c, r]) * rb) for r in range(ws)], comm)
+            self._barrier(comm)
+            ev_sent.append(_record(comm))
+        recv_local = view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
+        ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
+        backs, ev_back, rows_total = [], [], 0
+        for c in range(C):
+            mark(f"wait_sent{c}_before")
+            _wait(comp, ev_sent[c])
+            mark(f"wait_sent{c}_after")
+            n_recv = int(recv_c[c, me])
+            rows = recv_local[int(RO[c, me]):int(RO[c, me]) + n_recv]
+            rg = self.k.ep_regroup_plan(rc_me[:, c, :].contiguous(), capacity, n_recv,
+                                        pos_base=None if pos_dev is None else pos_dev[c])
+            xe = self.k.permute_rows(rows, rg["row_src"], rg["offsets"], rg["rows_cap"])
+            mark(f"experts{c}_start")
+            y = experts(xe, rg["offsets"])
+            mark(f"experts{c}_end")
+            rows_total += rg["rows_cap"]
+            backs.append(self.k.gather_rows(y, rg["recv_dst"], n_recv))
+            ev_back.append(_record(comp))
+        self.last_rows = rows_total
+        ev_ret = []
+        for c in range(C):
+            _wait(comm, ev_back[c])
+            backs[c].record_stream(comm)
+            base = backs[c].data_ptr()
+            copy_segments([(ret_buf.ptrs[s] + int(SRO[s, c] + SD[s, c, me]) * rb, base + int(SO[s, c, me]) * rb,
+                            int(R[s, c, me]) * rb) for s in range(ws)], comm)
+            self._barrier(comm)
+            ev_ret.append(_record(comm))
+        out = torch.empty_like(x)
+        mark("combine_start")
+        for c, (a, b) in enumerate(bounds):
+            mark(f"wait_ret{c}_before")
+            _wait(comp, ev_ret[c])
+            mark(f"wait_ret{c}_after")
+            ret = ret_local[int(SRO[me, c]):int(SRO[me, c] + send_c[me, c])]
+            self.k.combine(ret, plans[c]["slot_row"], w[a:b], b - a, k,
+                           shared=None if shared is None else shared[a:b], out=out[a:b])
+        return out
+
+    def close(self):
+        """Collective: release the peer buffers of the p2p transport."""
+        if self._bufs is not None:
+            for b in self._bufs:
+                b.release()
+            self._bufs = None
 
     # ------------------------------------------------------------------ stage API
     def dispatch(self, x: torch.Tensor, idx: torch.Tensor, capacity: int = 0):

@@ -24,7 +24,7 @@ def _port():
     return p
 
 
-def _worker(rank, ws, port, cfg, out_dir):
+def _worker(rank, ws, port, cfg, transport, out_dir):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "tests" / "golden")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
                       NCCL_NVLS_ENABLE="0")
@@ -46,6 +46,8 @@ def _worker(rank, ws, port, cfg, out_dir):
     m = S.UltimateMoE(E, d, use_fp16=False, dtype=dt, top_k=k, expert_type="swiglu", d_ff=F,
                       capacity_factor=cf, num_shared_experts=1 if shared else 0, d_ff_shared=F,
                       use_nccl_opt=False, device=dev)
+    m.comm.transport = transport
+    m.comm.min_chunk_tokens = 64          # several chunks even at these small sizes
     El = E // ws
     sl = slice(rank * El, (rank + 1) * El)
     with torch.no_grad():
@@ -83,13 +85,14 @@ CASES = [(300, 256, 8, 2, 512, None, False), (257, 256, 16, 2, 256, 1.0, False),
          (200, 128, 32, 8, 128, None, True)]
 
 
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
 @pytest.mark.parametrize("cfg", CASES)
-def test_ep_layer_matches_oracle(tmp_path, cfg):
+def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs two or more GPUs")
     ws = 4 if n >= 4 and cfg[2] % 4 == 0 else 2
-    mp.spawn(_worker, args=(ws, _port(), cfg, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_worker, args=(ws, _port(), cfg, transport, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         err, same_bits, agree = np.load(tmp_path / f"r{r}.npy")
         assert agree > 0.99

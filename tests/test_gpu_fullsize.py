@@ -13,6 +13,7 @@ from util import max_rel_err
 pytestmark = pytest.mark.gpu
 
 
+@torch.no_grad()
 def _fp32_reference_tokens(x, gate, w1, w3, w2, k, tok, bias=None, shared=None):
     """Layer output of the tokens `tok`, everything in fp32 (torch, on the GPU)."""
     xs = x[tok].float()
