@@ -79,7 +79,7 @@ class _StageTimer:
                 names = [n for n, _ in events]
                 self.data["Router"].append(span("start", "router"))
                 self.data["Dispatch_Comm"].append(span("router", "counts_done"))
-                self.data["Expert_Compute"].append(sum(span(n, n.replace("_start", "_end")) for n in names
+                self.data["Expert_Compute"].append(sum(span(n, n[:-len("_start")] + "_end") for n in names
                                                        if n.startswith("experts") and n.endswith("_start")))
                 self.data["Combine_Comm"].append(span("combine_start", "end"))
                 exposed = span("counts_start", "counts_done") + sum(

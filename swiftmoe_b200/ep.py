@@ -92,6 +92,7 @@ class ExpertParallelExchange:
             raise ValueError("transport must be 'auto', 'p2p' or 'collective'")
         self.transport = transport
         self._bufs = None           # (receive, return) PeerBuffers of the p2p transport
+        self._cstreams = {}         # per-device copy streams, one per peer
         self._flag = None
 
     # ------------------------------------------------------------------ helpers
@@ -133,6 +134,8 @@ class ExpertParallelExchange:
         CUDA tensors use the peer-copy transport (``_forward_p2p``) unless
         ``transport="collective"``; CPU tensors (gloo) use all_to_all_single."""
         use_p2p = self.transport == "p2p" or (self.transport == "auto" and x.is_cuda)
+        if use_p2p and capacity <= 0:
+            return self._forward_p2p_local_first(x, idx, w, experts, shared, timer)
         if use_p2p:
             return self._forward_p2p(x, idx, w, capacity, experts, shared, timer)
         return self._forward_collective(x, idx, w, capacity, experts, shared, timer)
@@ -335,6 +338,119 @@ class ExpertParallelExchange:
             self.k.combine(ret, plans[c]["slot_row"], w[a:b], b - a, k,
                            shared=None if shared is None else shared[a:b], out=out[a:b])
         return out
+
+    def _copy_streams(self, dev, n: int):
+        lst = self._cstreams.get(dev.index)
+        if lst is None or len(lst) < n:
+            lst = self._cstreams[dev.index] = [torch.cuda.Stream(dev) for _ in range(max(n, 1))]
+        return lst[:n]
+
+    def _fan_out(self, segs, base: torch.cuda.Stream, keep: torch.Tensor):
+        """Issue one copy per destination, each on its own stream so several copy engines
+        work at once; `base` waits for all of them.  `keep` is the source tensor."""
+        from .p2p import copy_segments
+        segs = [sg for sg in segs if sg[2] > 0]
+        streams = self._copy_streams(base.device, len(segs))
+        start = _record(base)
+        done = []
+        for sg, st in zip(segs, streams):
+            st.wait_event(start)
+            keep.record_stream(st)
+            copy_segments([sg], st)
+            done.append(_record(st))
+        for e in done:
+            base.wait_event(e)
+
+    def _forward_p2p_local_first(self, x, idx, w, experts, shared=None, timer=None):
+        """Peer-copy exchange without a capacity limit.  The rows this rank routes to its
+        OWN experts are contiguous in its send buffer and need no exchange: their expert
+        GEMMs are queued before the host waits for the count matrix, so the count
+        exchange, the host's bookkeeping and the copies of every other rank's rows over
+        NVLink (one copy stream per peer) all run underneath them."""
+        from .p2p import PeerBuffers, copy_segments, view
+        ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
+        T, k = idx.shape
+        d = x.shape[1]
+        dev = x.device
+        rb = d * x.element_size()
+        comp = torch.cuda.current_stream(dev)
+        comm = self._stream(dev)
+        if self._bufs is None:
+            self._bufs = (PeerBuffers(self.group, me, ws, dev), PeerBuffers(self.group, me, ws, dev))
+        recv_buf, ret_buf = self._bufs
+
+        def mark(name):
+            if timer is not None:
+                timer(name)
+
+        plan = self.k.dispatch_plan(idx, E)
+        send = self.k.permute_rows(x, plan["row_token"], plan["offsets"], plan["rows_cap"])
+        # count exchange and its host copy on the communication stream; the host waits
+        # for these alone, not for the expert work queued on the compute stream below
+        G = torch.empty((ws, E), dtype=torch.int32, device=dev)
+        if self._host is None or self._host.numel() < ws * E:
+            self._host = torch.empty(ws * E, dtype=torch.int32, pin_memory=True)
+        mark("counts_start")
+        comm.wait_stream(comp)
+        with torch.cuda.stream(comm):
+            dist.all_gather_into_tensor(G.view(-1), plan["counts"], group=self.group)
+            self._host[:ws * E].copy_(G.view(-1), non_blocking=True)
+            ev_counts = _record(comm)
+        mark("counts_done")
+        self_offsets = plan["offsets"][me * El:(me + 1) * El + 1]
+        mark("experts_self_start")
+        y_self = experts(send, self_offsets)
+        mark("experts_self_end")
+        ev_counts.synchronize()
+        Gh = self._host[:ws * E].numpy().reshape(ws, ws, El).astype(np.int64)   # [src, dst, El]
+        R = Gh.sum(2)                                  # rows src -> dst
+        Rr = R.copy()
+        np.fill_diagonal(Rr, 0)                        # a rank's own rows are not copied
+        recv_tot = Rr.sum(0)                           # [dst]
+        SO = np.cumsum(Rr, 0) - Rr                     # src offset inside dst's receive buffer
+        SD = np.cumsum(R, 1) - R                       # dst segment offset inside src's send layout
+        send_tot = R.sum(1)
+        recv_buf.ensure(int(max(recv_tot.max(), 1)) * rb)
+        ret_buf.ensure(int(max(send_tot.max(), 1)) * rb)
+        # dispatch copies to every peer, then one all-reduce to order them before use
+        sbase = send.data_ptr()
+        self._fan_out([(recv_buf.ptrs[r], 0, 0) if r == me else
+                       (recv_buf.ptrs[r] + int(SO[me, r]) * rb, sbase + int(SD[me, r]) * rb, int(R[me, r]) * rb)
+                       for r in range(ws)], comm, send)
+        self._barrier(comm)
+        ev_sent = _record(comm)
+        # this rank's own rows: expert outputs go straight to the return buffer
+        ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
+        a0, n0 = int(SD[me, me]), int(R[me, me])
+        y_self.record_stream(comp)
+        copy_segments([(ret_local.data_ptr() + a0 * rb, y_self.data_ptr() + a0 * rb, n0 * rb)], comp)
+        # rows from the other ranks
+        mark("wait_sent0_before")
+        _wait(comp, ev_sent)
+        mark("wait_sent0_after")
+        n_recv = int(recv_tot[me])
+        rc = G[:, me * El:(me + 1) * El].clone()
+        rc[me].zero_()
+        recv_local = view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
+        rg = self.k.ep_regroup_plan(rc, 0, n_recv)
+        xe = self.k.permute_rows(recv_local[:n_recv], rg["row_src"], rg["offsets"], rg["rows_cap"])
+        mark("experts0_start")
+        y = experts(xe, rg["offsets"])
+        mark("experts0_end")
+        self.last_rows = n0 + rg["rows_cap"]
+        back = self.k.gather_rows(y, rg["recv_dst"], n_recv)
+        comm.wait_stream(comp)
+        bbase = back.data_ptr()
+        self._fan_out([(0, 0, 0) if s_ == me else
+                       (ret_buf.ptrs[s_] + int(SD[s_, me]) * rb, bbase + int(SO[s_, me]) * rb, int(R[s_, me]) * rb)
+                       for s_ in range(ws)], comm, back)
+        self._barrier(comm)
+        ev_ret = _record(comm)
+        mark("combine_start")
+        mark("wait_ret0_before")
+        _wait(comp, ev_ret)
+        mark("wait_ret0_after")
+        return self.k.combine(ret_local[:int(send_tot[me])], plan["slot_row"], w, T, k, shared=shared)
 
     def close(self):
         """Collective: release the peer buffers of the p2p transport."""
