@@ -13,9 +13,11 @@
 namespace smoe {
 
 // --------------------------------------------------------------------------- errors
-// Device-side error word.  A bounded wait that gives up stores its code here (first
-// writer wins) and every role of the kernel then leaves its loop; the host reads and
-// clears it with smoe_read_device_error().
+// Device-side error word for the host.  A bounded wait that gives up, or a dispatch
+// plan that meets an expert index outside [0, E), stores its code here (first writer
+// wins); the host reads and clears it with smoe_read_device_error().  Kernels never
+// read it: within a launch the roles of a CTA learn of a give-up through a word in
+// their own shared memory.
 __device__ int g_device_error = 0;
 
 enum DeviceErrorCode : int {
@@ -25,9 +27,6 @@ enum DeviceErrorCode : int {
 };
 
 __device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
-__device__ __forceinline__ bool device_error_set() {
-  return *reinterpret_cast<volatile int*>(&g_device_error) != 0;
-}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -138,8 +137,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed.  Gives up after
-// kWaitLimitNs (or as soon as another thread has flagged an error) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// kWaitLimitNs, or as soon as another thread of the same CTA has given up (*cta_abort,
+// a shared-memory word of this launch), and returns false.  A timeout also records
+// kErrWaitTimeout in the global error word for the host; that word is only reported,
+// never consulted, so an old error cannot make later launches skip work.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* cta_abort) {
 #pragma unroll 1
   for (int i = 0; i < 256; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -147,8 +149,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (device_error_set()) return false;
+    if (*cta_abort) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *cta_abort = 1;
       set_device_error(kErrWaitTimeout);
       return false;
     }

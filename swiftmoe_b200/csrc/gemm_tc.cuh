@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   unsigned char* sB = smem + STAGES * A_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);  // set when a wait gives up
   int* s_off = reinterpret_cast<int*>(s_tmem + 4);
   int* s_ts = s_off + (MAX_GROUPS + 1);
 
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t mma_done_bar = smem_u32(bars + 2 * STAGES + 4);
 
   if (threadIdx.x == 0) {
+    *s_abort = 0;
     // group boundaries, forced monotonic and inside [0, rows_cap] so that no tile can
     // read or write past the row buffers whatever the caller passed
     int prev = 0;
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
         const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
@@ -205,11 +207,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1)) break;
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, s_abort)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
           const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
@@ -235,7 +237,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
       const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
-      if (!mbar_wait(tfull_bar(acc), acc_phase)) break;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       const bool row_ok = r < t.rows_valid;
       OutT* crow = C + (int64_t)(t.row0 + (row_ok ? r : 0)) * ldc;
