@@ -76,7 +76,8 @@ def _worker(rank, ws, port, cfg, transport, out_dir):
         # only when routing agrees everywhere
         err = max_rel_err(out, refs[rank]) if all(s.all() for s in same) else 0.0
     np.save(os.path.join(out_dir, f"r{rank}.npy"),
-            np.array([err, float(np.array_equal(out, out2)), float(same[rank].mean())]))
+            np.array([err, float(np.array_equal(out, out2)), float(same[rank].mean()),
+                      float(kernels.read_device_error(dev))]))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -94,7 +95,8 @@ def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
     ws = 4 if n >= 4 and cfg[2] % 4 == 0 else 2
     mp.spawn(_worker, args=(ws, _port(), cfg, transport, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
-        err, same_bits, agree = np.load(tmp_path / f"r{r}.npy")
+        err, same_bits, agree, dev_err = np.load(tmp_path / f"r{r}.npy")
+        assert dev_err == 0.0
         assert agree > 0.99
         assert err <= 2e-2, (r, err)
         assert same_bits == 1.0
