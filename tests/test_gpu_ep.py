@@ -75,6 +75,10 @@ def _worker(rank, ws, port, cfg, transport, out_dir):
         # with a capacity, a near-tie routing flip on any rank can move the cut; compare
         # only when routing agrees everywhere
         err = max_rel_err(out, refs[rank]) if all(s.all() for s in same) else 0.0
+    diff_rows = np.nonzero(np.abs(out - out2).max(1) > 0)[0] if out.size else np.zeros(0, int)
+    if diff_rows.size:
+        print(f"rank {rank} ({transport}): {diff_rows.size} rows differ between calls, first "
+              f"{diff_rows[:8].tolist()}, max |diff| {np.abs(out - out2).max():.3e}", flush=True)
     np.save(os.path.join(out_dir, f"r{rank}.npy"),
             np.array([err, float(np.array_equal(out, out2)), float(same[rank].mean()),
                       float(kernels.read_device_error(dev))]))
