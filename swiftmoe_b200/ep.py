@@ -181,7 +181,11 @@ class ExpertParallelExchange:
 
         send_splits = [[int(v) for v in hc[:, c, :].sum(1)] for c in range(C)]
         recv_splits = [[int(v) for v in hr[:, c, :].sum(1)] for c in range(C)]
+        # every buffer another stream writes is allocated here, before that stream waits for
+        # the compute stream: a block allocated later could still be read by compute work
+        # queued earlier (the caching allocator only orders reuse within one stream)
         recv_rows = [torch.empty((max(sum(recv_splits[c]), 1), d), dtype=x.dtype, device=dev) for c in range(C)]
+        rets = [torch.empty((max(sum(send_splits[c]), 1), d), dtype=x.dtype, device=dev) for c in range(C)]
         ev_sent = []
         # dispatch all-to-alls on the communication stream
         if comm is not None:
@@ -211,7 +215,6 @@ class ExpertParallelExchange:
             states.append((rg, n_recv))
         self.last_rows = rows_total
         # return all-to-alls (communication stream) and combine (compute stream)
-        rets = [torch.empty((max(sum(send_splits[c]), 1), d), dtype=x.dtype, device=dev) for c in range(C)]
         ev_ret = []
         for c in range(C):
             _wait(comm, ev_back[c])
