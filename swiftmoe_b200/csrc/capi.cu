@@ -140,6 +140,29 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
   return SMOE_OK;
 }
 
+template <int EPI, typename OutT>
+int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
+                   const int32_t* offsets, int G, int64_t rows_cap, int N, int K, uint32_t idesc, cudaStream_t st) {
+  static SmemGrant done;
+  auto kern = tc::grouped_gemm_pair_kernel<EPI, OutT>;
+  SMOE_CK(ensure_smem(kern, tc::pair::SMEM_BYTES, &done));
+  const int grid = device_sms() & ~1;  // whole CTA pairs
+  kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, G, N,
+                                                        K, (int)rows_cap, idesc);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+// Which tensor-core kernel runs a grouped GEMM: CTA pairs (256-row tiles) when the groups
+// are large enough to fill them, single CTAs (128-row tiles) otherwise.  The environment
+// variable SMOE_GEMM_VARIANT=1sm|2sm forces one of them (for measurements).
+bool use_pair_kernel(int64_t rows_cap, int G) {
+  static const char* forced = getenv("SMOE_GEMM_VARIANT");
+  if (forced && strcmp(forced, "1sm") == 0) return false;
+  if (forced && strcmp(forced, "2sm") == 0) return true;
+  return rows_cap >= 512 * (int64_t)G;
+}
+
 int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
                       const int32_t* offsets, int G, int64_t rows_cap, int N, int K, cudaStream_t st) {
   if (!A || !B || !C || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
@@ -174,6 +197,18 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     if (!make_map_3d(&mb3, B3, dt, G, N, K)) return SMOE_ERR_CUDA;
   } else {
     mb3 = mb;
+  }
+  if (use_pair_kernel(rows_cap, G)) {
+    const uint32_t idesc2 = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::pair::BM, tc::BN);
+    if (epi == SMOE_EPI_SWIGLU)
+      return dtype == SMOE_BF16
+                 ? launch_tc_pair<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st)
+                 : launch_tc_pair<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
+    if (out_dtype == SMOE_F32)
+      return launch_tc_pair<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
+    return dtype == SMOE_BF16
+               ? launch_tc_pair<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st)
+               : launch_tc_pair<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
   }
   const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
   if (epi == SMOE_EPI_SWIGLU) {

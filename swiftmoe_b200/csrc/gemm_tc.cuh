@@ -51,6 +51,35 @@ struct TileCoord {
   int g, row0, rows_valid, nb;
 };
 
+template <int BM_, int GM_>
+__device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_off, int G, int NB);
+
+// Tile L -> (group, first row, valid rows, n-block).  Inside a group the tiles are
+// rasterised in bands of GM_ m-tiles, m fastest, so concurrently running CTAs share the
+// weight tiles of a few n-blocks and the rows of a few m-tiles.
+template <int BM_, int GM_>
+__device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_off, int G, int NB) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_ts[mid] <= L) lo = mid; else hi = mid - 1;
+  }
+  TileCoord t;
+  t.g = lo;
+  const int local = L - s_ts[lo];
+  const int rows = s_off[lo + 1] - s_off[lo];
+  const int mt_g = (rows + BM_ - 1) / BM_;
+  const int band = local / (GM_ * NB);
+  const int m_first = band * GM_;
+  const int gm = min(mt_g - m_first, GM_);
+  const int r = local - band * GM_ * NB;
+  const int mt = m_first + r % gm;
+  t.nb = r / gm;
+  t.row0 = s_off[lo] + mt * BM_;
+  t.rows_valid = min(BM_, s_off[lo + 1] - t.row0);
+  return t;
+}
+
 __device__ __forceinline__ TileCoord decode_tile(int L, const int* s_ts, const int* s_off, int G, int NB) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
@@ -97,6 +126,46 @@ template <typename H> struct Store16 {
       }
   }
 };
+
+// Drain one 128-row accumulator (this warp's 32 TMEM lanes) into rows of C: SwiGLU on
+// the [gate | up] halves, or a plain store of all BN columns.
+template <int EPI, typename OutT>
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool row_ok, int col0, int N) {
+  if constexpr (EPI == SMOE_EPI_SWIGLU) {
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t gv[32], uv[32];
+      tmem_ld32(tbase + c * 32, gv);
+      tmem_ld32(tbase + 128 + c * 32, uv);
+      tmem_ld_wait();
+      float h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float g = __uint_as_float(gv[j]);
+        const float u = __uint_as_float(uv[j]);
+        h[j] = g / (1.0f + __expf(-g)) * u;
+      }
+      if (row_ok) Store16<OutT>::cols32(crow, col0 + c * 32, N, h);
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld32(tbase + c * 32, v);
+      tmem_ld_wait();
+      if (row_ok) {
+        if constexpr (sizeof(OutT) == 4) {
+          Store<float>::cols32(reinterpret_cast<float*>(crow), col0 + c * 32, N, v);
+        } else {
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          Store16<OutT>::cols32(crow, col0 + c * 32, N, f);
+        }
+      }
+    }
+  }
+}
 
 // EPI: SMOE_EPI_STORE or SMOE_EPI_SWIGLU.  OutT: float, __nv_bfloat16 or __half.
 template <int EPI, typename OutT>
@@ -288,6 +357,207 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ============================================================================ CTA pairs
+// The same grouped GEMM on pairs of CTAs (a cluster of 2 on neighbouring SMs) issuing
+// tcgen05.mma.cta_group::2: one 256 x 256 tile per pair, M split across the two CTAs
+// (128 rows each, accumulated in each CTA's own TMEM) and the B operand split along N
+// (each CTA stages 128 of the 256 weight rows).  Per FLOP every SM moves a third less
+// data from L2 into shared memory than the single-CTA kernel, and the 32 KB stages
+// allow a 6-deep ring.  The even CTA issues the MMAs; each CTA's TMA loads count their
+// bytes on the even CTA's "full" barrier; the MMA thread's commits arrive on the
+// "empty" / "accumulator full" barriers of both CTAs; both CTAs' epilogue warps arrive
+// on the even CTA's "accumulator empty" barrier.
+namespace pair {
+constexpr int BM = 256;  // rows per pair tile
+constexpr int BMC = 128; // rows per CTA
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BMC * BK * 2;
+constexpr int B_BYTES = (BN / 2) * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
+constexpr int GM = 8;
+constexpr int NUM_BARS = 2 * STAGES + 5;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 2 * (MAX_GROUPS + 1) * 4;
+}  // namespace pair
+
+__device__ __forceinline__ void mbar_wait_drain_cluster(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (globaltimer_ns() - t0 > kDrainLimitNs) {
+      set_device_error(kErrWaitTimeout);
+      return;
+    }
+  }
+}
+
+template <int EPI, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
+                             const int32_t* __restrict__ offsets, int G, int N, int K, int rows_cap,
+                             uint32_t idesc) {
+  constexpr int BM = pair::BM, BMC = pair::BMC, STAGES = pair::STAGES, GM = pair::GM;
+  constexpr int A_BYTES = pair::A_BYTES, B_BYTES = pair::B_BYTES, NUM_BARS = pair::NUM_BARS;
+  constexpr int PAIR_STAGE_BYTES = pair::PAIR_STAGE_BYTES;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  int* s_off = reinterpret_cast<int*>(s_tmem + 4);
+  int* s_ts = s_off + (MAX_GROUPS + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs for the pair
+  const int pair_id = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int NB = (EPI == SMOE_EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
+  const int KB = (K + BK - 1) / BK;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+  const uint32_t mma_done_bar = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    *s_abort = 0;
+    int prev = 0;
+    for (int i = 0; i <= G; ++i) {
+      prev = min(max(offsets[i], prev), rows_cap);
+      s_off[i] = prev;
+    }
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // four epilogue warps in each CTA of the pair
+    }
+    mbar_init(mma_done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (EPI == SMOE_EPI_SWIGLU) tma_prefetch_desc(&tmB3);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(s_tmem), 2 * BN);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < G; ++g) {
+      s_ts[g] = acc;
+      acc += ((s_off[g + 1] - s_off[g] + BM - 1) / BM) * NB;
+    }
+    s_ts[G] = acc;
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total = s_ts[G];
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int L = pair_id; L < total && ok; L += npairs) {
+        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_off, G, NB);
+        const int a_row = t.row0 + (int)rank * BMC;
+        const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN + (int)rank * 128;
+        const void* bmap = (EPI == SMOE_EPI_SWIGLU && rank == 1) ? (const void*)&tmB3 : (const void*)&tmB;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR_STAGE_BYTES);
+          const uint32_t fb = mapa_shared(full_bar(stage), 0);
+          tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, a_row);
+          tma_load_3d_pair(smem_u32(sB + stage * B_BYTES), bmap, fb, kb * BK, n0, t.g);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every issued stage must have been consumed (its loads landed) before exit
+      for (int s = 0; s < STAGES; ++s) {
+        const int64_t cnt = issued / STAGES + (s < issued % STAGES ? 1 : 0);
+        if (cnt > 0) mbar_wait_drain_cluster(empty_bar(s), (uint32_t)((cnt - 1) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------- MMA issuer (even CTA)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int L = pair_id; L < total && ok; L += npairs) {
+        if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1, s_abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait_cluster(full_bar(stage), phase, s_abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit_pair(mapa_shared(empty_bar(stage), 0));
+          umma_commit_pair(mapa_shared(empty_bar(stage), 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(tfull_bar(acc), 0));
+        umma_commit_pair(mapa_shared(tfull_bar(acc), 1));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      umma_commit_pair(mapa_shared(mma_done_bar, 0));
+      mbar_wait_drain_cluster(mma_done_bar, 0);
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int L = pair_id; L < total; L += npairs) {
+      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_off, G, NB);
+      if (!mbar_wait_cluster(tfull_bar(acc), acc_phase, s_abort)) break;
+      tc_fence_after();
+      const int row_base = t.row0 + (int)rank * BMC;
+      const int rows_valid = min(BMC, t.rows_valid - (int)rank * BMC);
+      const bool row_ok = r < rows_valid;
+      OutT* crow = C + (int64_t)(row_ok ? row_base + r : 0) * ldc;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int col0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
+      epilogue_tile<EPI, OutT>(tbase, crow, row_ok, col0, N);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs into this CTA's TMEM are complete
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 
