@@ -224,9 +224,16 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
 }
 
 // ------------------------------------------------------------------ router
-enum RouterPath { kRouterSmall, kRouterGemm, kRouterGeneric };
+enum RouterPath { kRouterMma, kRouterSmall, kRouterGemm, kRouterGeneric };
+
+int router_mma_tiles(int E) { return E <= 8 ? 1 : (E <= 16 ? 2 : 4); }
+size_t router_mma_smem(int d, int E) {
+  const int nt = router_mma_tiles(E);
+  return (size_t)8 * nt * (d + 8) * 2 + (size_t)4 * 16 * 8 * nt * sizeof(float);
+}
 
 RouterPath router_path(int d, int E, int dtype) {
+  if (dtype != SMOE_F32 && E <= 32 && d % 32 == 0 && router_mma_smem(d, E) <= 200 * 1024) return kRouterMma;
   const size_t smem = (size_t)E * d * elt_size(dtype);
   if (E <= 32 && smem <= 200 * 1024) return kRouterSmall;
   if (dtype == SMOE_F32) return kRouterGemm;
@@ -267,6 +274,33 @@ int router_small_dispatch(const void* x, const void* wg, const float* bias, int 
   if (d % V == 0 && aligned16(x) && aligned16(wg))
     return router_small_dispatch_e<T, V>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
   return router_small_dispatch_e<T, 1>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+}
+
+template <typename T, int NT>
+int launch_router_mma(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
+                      float* w, float* logits, cudaStream_t st) {
+  static SmemGrant done;
+  auto kern = router_mma_kernel<T, NT>;
+  const int smem = (int)router_mma_smem(d, E);
+  SMOE_CK(ensure_smem(kern, smem, &done));
+  int per_sm = 1;
+  SMOE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
+  per_sm = std::max(per_sm, 1);
+  const int64_t tasks = cdiv(T_, 16);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(tasks, 4), (int64_t)device_sms() * per_sm));
+  kern<<<grid, 128, smem, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w, logits);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+template <typename T>
+int router_mma_dispatch(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
+                        float* w, float* logits, cudaStream_t st) {
+  switch (router_mma_tiles(E)) {
+    case 1: return launch_router_mma<T, 1>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+    case 2: return launch_router_mma<T, 2>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+    default: return launch_router_mma<T, 4>(x, wg, bias, T_, d, E, k, idx, w, logits, st);
+  }
 }
 
 // Generic fallback router kernel for shapes the other two paths do not take
@@ -321,7 +355,8 @@ int smoe_read_device_error(int* flag, smoe_stream_t stream) {
 
 size_t smoe_router_workspace_size(int T, int d, int E, int dtype) {
   if (T <= 0 || E <= 0 || elt_size(dtype) == 0) return 0;
-  if (router_path(d, E, dtype) == kRouterSmall) return 0;
+  const RouterPath p = router_path(d, E, dtype);
+  if (p == kRouterSmall || p == kRouterMma) return 0;
   return align_up((size_t)T * E * sizeof(float), 256) + 256;
 }
 
@@ -333,7 +368,12 @@ int smoe_router_fwd(const void* x, const void* wg, int dtype, const float* logit
     return SMOE_ERR_INVALID;
   if (T == 0) return SMOE_OK;
   if (!x || !wg || !idx || !w) return SMOE_ERR_INVALID;
-  const RouterPath path = router_path(d, E, dtype);
+  RouterPath path = router_path(d, E, dtype);
+  if (path == kRouterMma && (!aligned16(x) || !aligned16(wg))) path = kRouterSmall;
+  if (path == kRouterMma) {
+    return dtype == SMOE_F16 ? router_mma_dispatch<__half>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st)
+                             : router_mma_dispatch<__nv_bfloat16>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st);
+  }
   if (path == kRouterSmall) {
     switch (dtype) {
       case SMOE_F32: return router_small_dispatch<float>(x, wg, logit_bias, T, d, E, k, idx, w, logits_out, st);

@@ -170,3 +170,15 @@ def test_bf16_layer_vs_reference_bf16_output(M):
     same = (idx.cpu().numpy() == f["topk_idx"]).all(1)
     assert same.mean() > 0.95
     assert max_rel_err(out[same], f["out"][same]) <= 2e-2
+
+
+def test_bench_records_schema():
+    """Records carry every key of the reference driver's schema (+ the stage breakdown)."""
+    from swiftmoe_b200.bench_records import run_single_config
+    from test_host_logic import REFERENCE_RECORD_KEYS
+    r = run_single_config("ultimate", 16, 256, 300, device=torch.device("cuda", 0), enable_profiling=True,
+                          warmup=2, iterations=3)
+    assert REFERENCE_RECORD_KEYS <= set(r)
+    assert {"Router", "Dispatch_Comm", "Expert_Compute", "Combine_Comm"} <= set(r)
+    b = run_single_config("baseline", 16, 256, 300, device=torch.device("cuda", 0), warmup=2, iterations=3)
+    assert REFERENCE_RECORD_KEYS <= set(b) and b["throughput_tokens_per_sec"] > 0

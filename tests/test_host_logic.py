@@ -94,3 +94,16 @@ def test_product_does_not_import_oracle():
     for p in Path(swiftmoe_b200.__file__).parent.glob("*.py"):
         src = p.read_text()
         assert "import oracle" not in src and "from oracle" not in src, p
+
+
+REFERENCE_RECORD_KEYS = {  # experiments/benchmark_suite.py:134-152
+    "model_type", "world_size", "batch_size", "num_experts", "d_model", "use_triton", "use_nccl_opt",
+    "latency_mean_ms", "latency_std_ms", "latency_min_ms", "latency_max_ms", "latency_p50_ms",
+    "latency_p95_ms", "latency_p99_ms", "throughput_tokens_per_sec", "max_memory_gb"}
+
+
+def test_bench_records_grid_matches_reference():
+    from swiftmoe_b200.bench_records import reference_grid
+    grid = reference_grid()
+    assert {e for e, _ in grid} == {64, 128, 256}
+    assert {b for _, b in grid} == {512, 1024, 2048, 4096, 8192}
