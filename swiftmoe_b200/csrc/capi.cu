@@ -227,13 +227,9 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
 enum RouterPath { kRouterMma, kRouterSmall, kRouterGemm, kRouterGeneric };
 
 int router_mma_tiles(int E) { return E <= 8 ? 1 : (E <= 16 ? 2 : 4); }
-size_t router_mma_smem(int d, int E) {
-  const int nt = router_mma_tiles(E);
-  return (size_t)8 * nt * (d + 8) * 2 + (size_t)4 * 16 * 8 * nt * sizeof(float);
-}
 
 RouterPath router_path(int d, int E, int dtype) {
-  if (dtype != SMOE_F32 && E <= 32 && d % 32 == 0 && router_mma_smem(d, E) <= 200 * 1024) return kRouterMma;
+  if (dtype != SMOE_F32 && E <= 32 && d % 64 == 0) return kRouterMma;
   const size_t smem = (size_t)E * d * elt_size(dtype);
   if (E <= 32 && smem <= 200 * 1024) return kRouterSmall;
   if (dtype == SMOE_F32) return kRouterGemm;
@@ -279,16 +275,10 @@ int router_small_dispatch(const void* x, const void* wg, const float* bias, int 
 template <typename T, int NT>
 int launch_router_mma(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
                       float* w, float* logits, cudaStream_t st) {
-  static SmemGrant done;
-  auto kern = router_mma_kernel<T, NT>;
-  const int smem = (int)router_mma_smem(d, E);
-  SMOE_CK(ensure_smem(kern, smem, &done));
-  int per_sm = 1;
-  SMOE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
-  per_sm = std::max(per_sm, 1);
-  const int64_t tasks = cdiv(T_, 16);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(tasks, 4), (int64_t)device_sms() * per_sm));
-  kern<<<grid, 128, smem, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w, logits);
+  const int64_t blocks = cdiv(T_, 32);  // 32 tokens per block
+  if (blocks > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
+  router_mma_kernel<T, NT><<<(unsigned)blocks, 128, 0, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w,
+                                                              logits);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

@@ -110,111 +110,107 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
 }
 
 // Router for 16-bit x with E <= 32 on the warp-level tensor-core MMA
-// (mma.sync m16n8k16, fp32 accumulate).  A warp owns 16 tokens; per step of 32 columns
-// of x each lane loads two 16-byte chunks of x (its token rows g and g+8) and one of the
-// gate row per 8 experts from shared memory, and issues two MMAs per 8 experts.  The
-// reduction index k is permuted identically in both operands (lane quad q supplies
-// columns 8q..8q+7 of the step as its fragment pairs), which leaves the dot products
-// unchanged and lets every fragment be one contiguous 16-byte load.  The logits of the
-// 16 tokens then go through shared memory to one lane per token for top-k + softmax.
-// The router reads x once: it is bound by HBM bandwidth.
+// (mma.sync m16n8k16, fp32 accumulate).  A block owns 32 tokens: warps 0/1 take tokens
+// 0-15 and warps 2/3 tokens 16-31, each pair splitting the d columns in two halves.  Per
+// step of 32 columns a lane loads two 16-byte chunks of x (its token rows g and g+8) and,
+// per 8 experts, one 16-byte chunk of the gate (read through L1, where the whole gate
+// stays resident), and issues two MMAs per 8 experts; 8 steps are unrolled so 8 KB of x
+// per warp is in flight.  The reduction index is permuted identically in both operands
+// (lane quad q supplies columns 8q..8q+7 of the step as its fragment pairs), which leaves
+// each dot product unchanged and makes every fragment one contiguous 16-byte load.  The
+// two half sums meet in shared memory (added in a fixed order) and one lane per token
+// does top-k + softmax.  The router reads x once: it is bound by HBM bandwidth.
 template <typename T, int NT>  // NT: number of 8-expert column tiles (E <= 8 * NT)
 __global__ void __launch_bounds__(128) router_mma_kernel(const T* __restrict__ x, const T* __restrict__ wg,
                                                          const float* __restrict__ bias, int T_, int d, int E, int k,
                                                          int32_t* __restrict__ idx, float* __restrict__ w,
                                                          float* __restrict__ logits_out) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int ldg = d + 8;  // padded gate row (elements): rows fall on different banks
-  T* s_wg = reinterpret_cast<T*>(smem_raw);
-  float* s_lg = reinterpret_cast<float*>(smem_raw + (size_t)8 * NT * ldg * sizeof(T));  // [4 warps][16][8*NT]
-  for (int i = threadIdx.x; i < 8 * NT * (d / 8); i += blockDim.x) {
-    const int e = i / (d / 8), c = (i % (d / 8)) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (e < E) v = *reinterpret_cast<const uint4*>(wg + (size_t)e * d + c);
-    *reinterpret_cast<uint4*>(s_wg + (size_t)e * ldg + c) = v;
-  }
-  __syncthreads();
+  __shared__ float s_part[4][16][8 * NT];  // per warp: partial logits of its 16 tokens
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, q = lane & 3;
-  float* lg = s_lg + warp * 16 * 8 * NT;
-  const int ntasks = (T_ + 15) / 16;
-  for (int task = blockIdx.x * 4 + warp; task < ntasks; task += gridDim.x * 4) {
-    const int t0 = task * 16;
-    const int r0 = t0 + g, r1 = t0 + g + 8;
-    const T* x0 = x + (size_t)min(r0, T_ - 1) * d + q * 8;
-    const T* x1 = x + (size_t)min(r1, T_ - 1) * d + q * 8;
-    float acc[NT][4];
+  const int half = warp & 1;               // which half of the d columns
+  const int t0 = blockIdx.x * 32 + (warp >> 1) * 16;
+  const int r0 = min(t0 + g, T_ - 1), r1 = min(t0 + g + 8, T_ - 1);
+  const int dh = d / 2;                    // d % 64 == 0 on this path
+  const T* x0 = x + (size_t)r0 * d + half * dh + q * 8;
+  const T* x1 = x + (size_t)r1 * d + half * dh + q * 8;
+  const T* gq = wg + half * dh + q * 8;
+  float acc[NT][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+  for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[n][j] = 0.f;
-#pragma unroll 4
-    for (int kb = 0; kb < d; kb += 32) {
-      const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(x0 + kb));
-      const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(x1 + kb));
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const uint4 b = *reinterpret_cast<const uint4*>(s_wg + (size_t)(n * 8 + g) * ldg + kb + q * 8);
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-              : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-              : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
-        } else {
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-              : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-              : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
-        }
-      }
-    }
-    // D fragment: acc[n][0..1] = rows g, experts 8n+2q..+1; acc[n][2..3] = row g+8
-    __syncwarp();
+    for (int j = 0; j < 4; ++j) acc[n][j] = 0.f;
+#pragma unroll 8
+  for (int kb = 0; kb < dh; kb += 32) {
+    const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(x0 + kb));
+    const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(x1 + kb));
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-      lg[g * 8 * NT + n * 8 + 2 * q] = acc[n][0];
-      lg[g * 8 * NT + n * 8 + 2 * q + 1] = acc[n][1];
-      lg[(g + 8) * 8 * NT + n * 8 + 2 * q] = acc[n][2];
-      lg[(g + 8) * 8 * NT + n * 8 + 2 * q + 1] = acc[n][3];
-    }
-    __syncwarp();
-    if (lane < 16 && t0 + lane < T_) {
-      const int t = t0 + lane;
-      const float* row = lg + lane * 8 * NT;
-      if (logits_out != nullptr)
-        for (int e = 0; e < E; ++e) logits_out[(size_t)t * E + e] = row[e];
-      // top-k by repeated selection over the E logits (+ offsets), ties -> lower index
-      uint32_t taken = 0;
-      float first = 0.f, sum = 0.f;
-      for (int j = 0; j < k; ++j) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = 0; e < E; ++e) {
-          if (taken & (1u << e)) continue;
-          const float v = row[e] + (bias != nullptr ? bias[e] : 0.f);
-          if (ranks_before(v, e, bv, bi)) { bv = v; bi = e; }
-        }
-        taken |= 1u << bi;
-        if (j == 0) first = bv;
-        const float ex = expf(bv - first);
-        sum += ex;
-        idx[(size_t)t * k + j] = bi;
-        w[(size_t)t * k + j] = ex;
+      const int e = n * 8 + g;
+      uint4 b = make_uint4(0, 0, 0, 0);
+      if (e < E) b = __ldg(reinterpret_cast<const uint4*>(gq + (size_t)e * d + kb));
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
+            : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
+            : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
+      } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
+            : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
+            : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
       }
-      for (int j = 0; j < k; ++j) w[(size_t)t * k + j] /= sum;
     }
+  }
+  // D fragment: acc[n][0..1] = token g, experts 8n+2q..+1; acc[n][2..3] = token g+8
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    s_part[warp][g][n * 8 + 2 * q] = acc[n][0];
+    s_part[warp][g][n * 8 + 2 * q + 1] = acc[n][1];
+    s_part[warp][g + 8][n * 8 + 2 * q] = acc[n][2];
+    s_part[warp][g + 8][n * 8 + 2 * q + 1] = acc[n][3];
+  }
+  __syncthreads();
+  if (half == 0 && lane < 16 && t0 + lane < T_) {
+    const int t = t0 + lane;
+    float row[8 * NT];
+#pragma unroll
+    for (int e = 0; e < 8 * NT; ++e) row[e] = s_part[warp][lane][e] + s_part[warp + 1][lane][e];
+    if (logits_out != nullptr)
+      for (int e = 0; e < E; ++e) logits_out[(size_t)t * E + e] = row[e];
+    if (bias != nullptr)
+      for (int e = 0; e < E; ++e) row[e] += bias[e];
+    // top-k by repeated selection, ties -> lower index, NaN first
+    uint32_t taken = 0;
+    float first = 0.f, sum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int e = 0; e < 8 * NT; ++e) {
+        if (e >= E || (taken & (1u << e))) continue;
+        if (ranks_before(row[e], e, bv, bi)) { bv = row[e]; bi = e; }
+      }
+      taken |= 1u << bi;
+      if (j == 0) first = bv;
+      const float ex = expf(bv - first);
+      sum += ex;
+      idx[(size_t)t * k + j] = bi;
+      w[(size_t)t * k + j] = ex;
+    }
+    for (int j = 0; j < k; ++j) w[(size_t)t * k + j] /= sum;
   }
 }
 
