@@ -275,10 +275,18 @@ int router_small_dispatch(const void* x, const void* wg, const float* bias, int 
 template <typename T, int NT>
 int launch_router_mma(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
                       float* w, float* logits, cudaStream_t st) {
-  const int64_t blocks = cdiv(T_, 32);  // 32 tokens per block
+  if (d % 128 == 0) {  // four warps per 16 tokens
+    const int64_t blocks = cdiv(T_, 16);
+    if (blocks > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
+    router_mma_kernel<T, NT, 4><<<(unsigned)blocks, 128, 0, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx,
+                                                                   w, logits);
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
+  const int64_t blocks = cdiv(T_, 32);  // two warps per 16 tokens
   if (blocks > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
-  router_mma_kernel<T, NT><<<(unsigned)blocks, 128, 0, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w,
-                                                              logits);
+  router_mma_kernel<T, NT, 2><<<(unsigned)blocks, 128, 0, st>>>((const T*)x, (const T*)wg, bias, T_, d, E, k, idx, w,
+                                                                 logits);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

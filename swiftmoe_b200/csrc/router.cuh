@@ -109,69 +109,105 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
   }
 }
 
+// 16-byte loads kept in program order with the MMAs (volatile asm), so a whole batch of
+// loads is in flight before the first MMA that consumes it.  x is streamed (no L1
+// allocation); the small gate matrix is read through L1, where it stays resident.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_keep(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Two m16n8k16 MMAs (fp32 accumulate) over one 32-column step: fragment pairs .x/.y
+// then .z/.w of the 16-byte chunks (see router_mma_kernel for the column order).
+template <typename T>
+__device__ __forceinline__ void mma_step(float (&c)[4], const uint4& a0, const uint4& a1, const uint4& b) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
+  }
+}
+
 // Router for 16-bit x with E <= 32 on the warp-level tensor-core MMA
-// (mma.sync m16n8k16, fp32 accumulate).  A block owns 32 tokens: warps 0/1 take tokens
-// 0-15 and warps 2/3 tokens 16-31, each pair splitting the d columns in two halves.  Per
+// (mma.sync m16n8k16, fp32 accumulate).  KSPLIT warps of a block share 16 tokens, each
+// taking one slice of the d columns (4 slices when d % 128 == 0, else 2).  Per
 // step of 32 columns a lane loads two 16-byte chunks of x (its token rows g and g+8) and,
 // per 8 experts, one 16-byte chunk of the gate (read through L1, where the whole gate
 // stays resident), and issues two MMAs per 8 experts; 8 steps are unrolled so 8 KB of x
 // per warp is in flight.  The reduction index is permuted identically in both operands
 // (lane quad q supplies columns 8q..8q+7 of the step as its fragment pairs), which leaves
 // each dot product unchanged and makes every fragment one contiguous 16-byte load.  The
-// two half sums meet in shared memory (added in a fixed order) and one lane per token
-// does top-k + softmax.  The router reads x once: it is bound by HBM bandwidth.
-template <typename T, int NT>  // NT: number of 8-expert column tiles (E <= 8 * NT)
+// slice sums meet in shared memory (added in a fixed order) and one lane per token does
+// top-k + softmax.  The router reads x once: it is bound by HBM bandwidth.
+template <typename T, int NT, int KSPLIT>  // E <= 8 * NT; KSPLIT warps share 16 tokens
 __global__ void __launch_bounds__(128) router_mma_kernel(const T* __restrict__ x, const T* __restrict__ wg,
                                                          const float* __restrict__ bias, int T_, int d, int E, int k,
                                                          int32_t* __restrict__ idx, float* __restrict__ w,
                                                          float* __restrict__ logits_out) {
+  constexpr int GROUPS = 4 / KSPLIT;       // 16-token groups per block of 4 warps
   __shared__ float s_part[4][16][8 * NT];  // per warp: partial logits of its 16 tokens
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, q = lane & 3;
-  const int half = warp & 1;               // which half of the d columns
-  const int t0 = blockIdx.x * 32 + (warp >> 1) * 16;
+  const int part = warp % KSPLIT;          // which slice of the d columns
+  const int t0 = blockIdx.x * 16 * GROUPS + (warp / KSPLIT) * 16;
   const int r0 = min(t0 + g, T_ - 1), r1 = min(t0 + g + 8, T_ - 1);
-  const int dh = d / 2;                    // d % 64 == 0 on this path
-  const T* x0 = x + (size_t)r0 * d + half * dh + q * 8;
-  const T* x1 = x + (size_t)r1 * d + half * dh + q * 8;
-  const T* gq = wg + half * dh + q * 8;
+  const int dh = d / KSPLIT;               // a multiple of 32 on this path
+  const T* x0 = x + (size_t)r0 * d + part * dh + q * 8;
+  const T* x1 = x + (size_t)r1 * d + part * dh + q * 8;
+  const T* gq = wg + part * dh + q * 8;
   float acc[NT][4];
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[n][j] = 0.f;
-#pragma unroll 8
-  for (int kb = 0; kb < dh; kb += 32) {
+  // batches of UNR steps: all loads of a batch are issued before its MMAs, so a warp keeps
+  // UNR * 1 KB of x in flight
+  constexpr int UNR = 8;
+  int kb = 0;
+  for (; kb + 32 * UNR <= dh; kb += 32 * UNR) {
+    uint4 A0[UNR], A1[UNR], Bv[UNR][NT];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      A0[u] = ldg_stream(x0 + kb + 32 * u);
+      A1[u] = ldg_stream(x1 + kb + 32 * u);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int e = min(n * 8 + g, E - 1);  // rows >= E are multiplied by zero below
+        Bv[u][n] = ldg_keep(gq + (size_t)e * d + kb + 32 * u);
+        if (n * 8 + g >= E) Bv[u][n] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma_step<T>(acc[n], A0[u], A1[u], Bv[u][n]);
+  }
+  for (; kb < dh; kb += 32) {
     const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(x0 + kb));
     const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(x1 + kb));
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       const int e = n * 8 + g;
-      uint4 b = make_uint4(0, 0, 0, 0);
-      if (e < E) b = __ldg(reinterpret_cast<const uint4*>(gq + (size_t)e * d + kb));
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-            : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-            : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
-      } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-            : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(b.x), "r"(b.y));
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-            : "r"(a0.z), "r"(a1.z), "r"(a0.w), "r"(a1.w), "r"(b.z), "r"(b.w));
-      }
+      const uint4 b = e < E ? __ldg(reinterpret_cast<const uint4*>(gq + (size_t)e * d + kb)) : make_uint4(0, 0, 0, 0);
+      mma_step<T>(acc[n], a0, a1, b);
     }
   }
   // D fragment: acc[n][0..1] = token g, experts 8n+2q..+1; acc[n][2..3] = token g+8
@@ -183,11 +219,16 @@ __global__ void __launch_bounds__(128) router_mma_kernel(const T* __restrict__ x
     s_part[warp][g + 8][n * 8 + 2 * q + 1] = acc[n][3];
   }
   __syncthreads();
-  if (half == 0 && lane < 16 && t0 + lane < T_) {
+  if (part == 0 && lane < 16 && t0 + lane < T_) {
     const int t = t0 + lane;
     float row[8 * NT];
 #pragma unroll
-    for (int e = 0; e < 8 * NT; ++e) row[e] = s_part[warp][lane][e] + s_part[warp + 1][lane][e];
+    for (int e = 0; e < 8 * NT; ++e) {
+      float v = s_part[warp][lane][e];
+#pragma unroll
+      for (int p = 1; p < KSPLIT; ++p) v += s_part[warp + p][lane][e];  // fixed order
+      row[e] = v;
+    }
     if (logits_out != nullptr)
       for (int e = 0; e < E; ++e) logits_out[(size_t)t * E + e] = row[e];
     if (bias != nullptr)
