@@ -130,8 +130,10 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
 
 /* --------------------------------------------------------------------- expert GEMMs
  * Grouped GEMM over G groups of rows.  Group g owns rows [offsets[g], offsets[g+1]) of
- * A [rows_cap, K] and multiplies them by B_g^T where B is [G, N, K] (nn.Linear layout,
- * K contiguous).  offsets lives in device memory and is read by the kernel.
+ * A [rows_cap, K] -- or [offsets[g], ends[g]) when `ends` is not NULL -- and multiplies
+ * them by B_g^T where B is [G, N, K] (nn.Linear layout, K contiguous).  offsets / ends
+ * live in device memory and are read by the kernel; ranges are clamped to [0, rows_cap]
+ * and only the rows of a group's range are written.
  *   epilogue SMOE_EPI_STORE  : C[r, n] = acc                       (C is [rows_cap, N])
  *   epilogue SMOE_EPI_SWIGLU : C[r, n] = silu(A B1_g^T) * (A B3_g^T) (B3 = B2 arg, C [rows_cap, N])
  * bf16 / fp16 run on tcgen05 tensor cores (TMEM accumulators, TMA-fed shared memory,
@@ -142,8 +144,8 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
 #define SMOE_EPI_STORE 0
 #define SMOE_EPI_SWIGLU 1
 SMOE_API int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype,
-                      int out_dtype, int epilogue, const int32_t* offsets, int G,
-                      int64_t rows_cap, int N, int K, smoe_stream_t stream);
+                      int out_dtype, int epilogue, const int32_t* offsets, const int32_t* ends,
+                      int G, int64_t rows_cap, int N, int K, smoe_stream_t stream);
 
 /* dst[g, c, r] = src[g, r, c] for G matrices of [R, C] (weight relayout, e.g. the
  * reference's x@W expert_weights [E, d_in, d_out] -> nn.Linear layout [E, d_out, d_in]). */

@@ -225,12 +225,14 @@ class MoECore(nn.Module):
         L.check(lib.smoe_layer_fwd(C.byref(a), L.stream_handle(x.device)), "smoe_layer_fwd")
         return out
 
-    def _experts(self, xe: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    def _experts(self, xe: torch.Tensor, offsets: torch.Tensor, ends: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Expert outputs for the rows of local expert g: [offsets[g], offsets[g+1]), or
+        [offsets[g], ends[g]) when ``ends`` is given (other rows are left unwritten)."""
         if self.expert_type == "swiglu":
             w1, w3, w2 = self._swiglu()
-            h = K.grouped_gemm(xe, w1, offsets, B3=w3, epilogue=L.SMOE_EPI_SWIGLU)
-            return K.grouped_gemm(h, w2, offsets)
-        return K.grouped_gemm(xe, self._linear_kmajor(), offsets)
+            h = K.grouped_gemm(xe, w1, offsets, B3=w3, epilogue=L.SMOE_EPI_SWIGLU, ends=ends)
+            return K.grouped_gemm(h, w2, offsets, ends=ends)
+        return K.grouped_gemm(xe, self._linear_kmajor(), offsets, ends=ends)
 
     def _shared_out(self, x: torch.Tensor) -> Optional[torch.Tensor]:
         sh = self._shared()

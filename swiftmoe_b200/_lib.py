@@ -52,7 +52,7 @@ SIGNATURES = {
     "smoe_dispatch_plan_noalloc": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
     "smoe_permute_rows": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i64, _vp, _vp]),
     "smoe_combine": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
-    "smoe_grouped_gemm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32, _i64, _i32, _i32, _vp]),
+    "smoe_grouped_gemm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp]),
     "smoe_transpose_batched": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "smoe_gather_rows": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _vp]),
     "smoe_ep_regroup_workspace_size": (_sz, [_i32, _i32]),

@@ -130,11 +130,12 @@ __global__ void fill_two_kernel(int32_t* p, int32_t a, int32_t b) {
 // ------------------------------------------------------------------ grouped GEMM
 template <int EPI, typename OutT>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
-              const int32_t* offsets, int G, int64_t rows_cap, int N, int K, uint32_t idesc, cudaStream_t st) {
+              const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
+              cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
-  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, G, N,
+  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
                                                          K, (int)rows_cap, idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
@@ -142,12 +143,13 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
 
 template <int EPI, typename OutT>
 int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
-                   const int32_t* offsets, int G, int64_t rows_cap, int N, int K, uint32_t idesc, cudaStream_t st) {
+                   const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
+              cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::grouped_gemm_pair_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::pair::SMEM_BYTES, &done));
   const int grid = device_sms() & ~1;  // whole CTA pairs
-  kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, G, N,
+  kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
                                                         K, (int)rows_cap, idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
@@ -167,7 +169,8 @@ bool use_pair_kernel(int64_t rows_cap, int G) {
 }
 
 int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
-                      const int32_t* offsets, int G, int64_t rows_cap, int N, int K, cudaStream_t st) {
+                      const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
+                      cudaStream_t st) {
   if (!A || !B || !C || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
   if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU) return SMOE_ERR_INVALID;
   if (epi == SMOE_EPI_SWIGLU && !B3) return SMOE_ERR_INVALID;
@@ -179,10 +182,10 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, 32) : cdiv(N, simt::BN)));
     if (epi == SMOE_EPI_SWIGLU)
       simt::grouped_gemm_f32_kernel<SMOE_EPI_SWIGLU><<<grid, simt::THREADS, 0, st>>>(
-          (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, offsets, G, N, K, (int)rows_cap);
+          (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, offsets, ends, G, N, K, (int)rows_cap);
     else
       simt::grouped_gemm_f32_kernel<SMOE_EPI_STORE><<<grid, simt::THREADS, 0, st>>>(
-          (const float*)A, (const float*)B, nullptr, (float*)C, N, offsets, G, N, K, (int)rows_cap);
+          (const float*)A, (const float*)B, nullptr, (float*)C, N, offsets, ends, G, N, K, (int)rows_cap);
     SMOE_CK(cudaGetLastError());
     return SMOE_OK;
   }
@@ -205,22 +208,22 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     const uint32_t idesc2 = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::pair::BM, tc::BN);
     if (epi == SMOE_EPI_SWIGLU)
       return dtype == SMOE_BF16
-                 ? launch_tc_pair<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st)
-                 : launch_tc_pair<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
+                 ? launch_tc_pair<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st)
+                 : launch_tc_pair<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
     if (out_dtype == SMOE_F32)
-      return launch_tc_pair<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
+      return launch_tc_pair<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
     return dtype == SMOE_BF16
-               ? launch_tc_pair<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st)
-               : launch_tc_pair<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc2, st);
+               ? launch_tc_pair<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st)
+               : launch_tc_pair<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
   }
   const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
   if (epi == SMOE_EPI_SWIGLU) {
-    return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st)
-                              : launch_tc<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
+    return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st)
+                              : launch_tc<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
   }
-  if (out_dtype == SMOE_F32) return launch_tc<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
-  return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st)
-                            : launch_tc<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, G, rows_cap, N, K, idesc, st);
+  if (out_dtype == SMOE_F32) return launch_tc<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
+  return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st)
+                            : launch_tc<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
 }
 
 // ------------------------------------------------------------------ router
@@ -390,7 +393,7 @@ int smoe_router_fwd(const void* x, const void* wg, int dtype, const float* logit
   if (path == kRouterGemm) {
     fill_two_kernel<<<1, 1, 0, st>>>(offs, 0, T);
     SMOE_CK(cudaGetLastError());
-    const int rc = grouped_gemm_impl(x, wg, nullptr, logits, dtype, SMOE_F32, SMOE_EPI_STORE, offs, 1, T, E, d, st);
+    const int rc = grouped_gemm_impl(x, wg, nullptr, logits, dtype, SMOE_F32, SMOE_EPI_STORE, offs, nullptr, 1, T, E, d, st);
     if (rc != SMOE_OK) return rc;
   } else {
     const unsigned grid = (unsigned)cdiv(T, 8);
@@ -507,8 +510,10 @@ int smoe_combine(const void* y, int dtype, const int32_t* slot_row, const float*
 }
 
 int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epilogue,
-                      const int32_t* offsets, int G, int64_t rows_cap, int N, int K, smoe_stream_t stream) {
-  return grouped_gemm_impl(A, B, B3, C, dtype, out_dtype, epilogue, offsets, G, rows_cap, N, K, (cudaStream_t)stream);
+                      const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
+                      smoe_stream_t stream) {
+  return grouped_gemm_impl(A, B, B3, C, dtype, out_dtype, epilogue, offsets, ends, G, rows_cap, N, K,
+                           (cudaStream_t)stream);
 }
 
 int smoe_transpose_batched(const void* src, void* dst, int dtype, int G, int R, int C, smoe_stream_t stream) {
@@ -746,13 +751,13 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
   if (rc) return rc;
   if ((rc = mark(2))) return rc;
   if (a->expert_type == SMOE_EXPERT_SWIGLU) {
-    rc = grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, E, p.rows_cap, F, d, st);
+    rc = grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E, p.rows_cap, F, d, st);
     if (rc) return rc;
     if ((rc = mark(3))) return rc;
-    rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, E, p.rows_cap, d, F, st);
+    rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, F, st);
     if (rc) return rc;
   } else {
-    rc = grouped_gemm_impl(xrows, a->w_lin, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, E, p.rows_cap, d, d, st);
+    rc = grouped_gemm_impl(xrows, a->w_lin, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, d, st);
     if (rc) return rc;
     if ((rc = mark(3))) return rc;
   }
@@ -763,9 +768,9 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
     SMOE_CK(cudaGetLastError());
     void* hs = ws + p.off_hs;
     ys = ws + p.off_ys;
-    rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, hs, dt, dt, SMOE_EPI_SWIGLU, soff, 1, T, a->d_ff_shared, d, st);
+    rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, hs, dt, dt, SMOE_EPI_SWIGLU, soff, nullptr, 1, T, a->d_ff_shared, d, st);
     if (rc) return rc;
-    rc = grouped_gemm_impl(hs, a->sw2, nullptr, ys, dt, dt, SMOE_EPI_STORE, soff, 1, T, d, a->d_ff_shared, st);
+    rc = grouped_gemm_impl(hs, a->sw2, nullptr, ys, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, d, a->d_ff_shared, st);
     if (rc) return rc;
   }
   if ((rc = mark(4))) return rc;

@@ -3,7 +3,7 @@
 // max-abs tolerance rules out TF32 tensor cores.
 //
 // Same grouping contract as the tensor-core kernel: group g owns rows
-// [offsets[g], offsets[g+1]) of A [rows, K]; B is [G, N, K].  Block tile 64 x 64,
+// [offsets[g], ends ? ends[g] : offsets[g+1]) of A [rows, K]; B is [G, N, K].  Block tile 64 x 64,
 // K step 16, 256 threads with a 4 x 4 register tile each.  For the SwiGLU epilogue a
 // block computes 32 gate columns and the 32 matching up columns and stores
 // silu(gate) * up.
@@ -20,21 +20,21 @@ __global__ void __launch_bounds__(THREADS) grouped_gemm_f32_kernel(const float* 
                                                                    const float* __restrict__ B,
                                                                    const float* __restrict__ B3, float* __restrict__ C,
                                                                    int64_t ldc, const int32_t* __restrict__ offsets,
-                                                                   int G, int N, int K, int rows_cap) {
-  __shared__ int s_off[MAX_GROUPS + 1];
+                                                                   const int32_t* __restrict__ ends, int G, int N,
+                                                                   int K, int rows_cap) {
+  __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS];
   __shared__ int s_ts[MAX_GROUPS + 1];
   __shared__ float As[BK][BM + 4];
   __shared__ float Bs[BK][BN + 4];
-  if (threadIdx.x == 0) {
-    int prev = 0;  // monotonic and inside [0, rows_cap]
-    for (int i = 0; i <= G; ++i) {
-      prev = min(max(offsets[i], prev), rows_cap);
-      s_off[i] = prev;
-    }
+  if (threadIdx.x == 0) {  // row ranges clamped into [0, rows_cap]
     int acc = 0;
     for (int g = 0; g < G; ++g) {
+      const int b = min(max(offsets[g], 0), rows_cap);
+      const int f = min(max(ends != nullptr ? ends[g] : offsets[g + 1], b), rows_cap);
+      s_beg[g] = b;
+      s_fin[g] = f;
       s_ts[g] = acc;
-      acc += (s_off[g + 1] - s_off[g] + BM - 1) / BM;
+      acc += (f - b + BM - 1) / BM;
     }
     s_ts[G] = acc;
   }
@@ -47,8 +47,8 @@ __global__ void __launch_bounds__(THREADS) grouped_gemm_f32_kernel(const float* 
     if (s_ts[mid] <= mt) lo = mid; else hi = mid - 1;
   }
   const int g = lo;
-  const int row0 = s_off[g] + (mt - s_ts[g]) * BM;
-  const int row_end = s_off[g + 1];
+  const int row0 = s_beg[g] + (mt - s_ts[g]) * BM;
+  const int row_end = s_fin[g];
   // column layout of the block: STORE -> output columns n0 .. n0+63;
   // SWIGLU -> smem columns 0..31 = gate rows n0.., 32..63 = up rows n0..
   const int n0 = (EPI == SMOE_EPI_SWIGLU) ? blockIdx.y * 32 : blockIdx.y * BN;

@@ -33,7 +33,7 @@ constexpr int THREADS = 192;
 constexpr int MAX_GROUPS = 1024;
 constexpr int GM = 16;  // m-tiles per rasterisation band
 constexpr int NUM_BARS = 2 * STAGES + 5;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 2 * (MAX_GROUPS + 1) * 4;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 * (MAX_GROUPS + 1) * 4;
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 200 ms
 
 // Wait used while draining on the way out: ignores the error word, bounded by time.
@@ -51,14 +51,31 @@ struct TileCoord {
   int g, row0, rows_valid, nb;
 };
 
-template <int BM_, int GM_>
-__device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_off, int G, int NB);
+// Per-launch group table, built by one thread: group g covers rows
+// [s_beg[g], s_fin[g]) -- offsets[g] .. (ends ? ends[g] : offsets[g+1]) clamped into
+// [0, rows_cap] so that no tile can touch rows outside the buffers whatever the caller
+// passed -- and its tiles are numbered from s_ts[g]; s_ts[G] is the total.
+template <int BM_>
+__device__ __forceinline__ void build_group_table(const int32_t* offsets, const int32_t* ends, int G, int rows_cap,
+                                                  int NB, int* s_beg, int* s_fin, int* s_ts) {
+  int acc = 0;
+  for (int g = 0; g < G; ++g) {
+    const int b = min(max(offsets[g], 0), rows_cap);
+    const int f = min(max(ends != nullptr ? ends[g] : offsets[g + 1], b), rows_cap);
+    s_beg[g] = b;
+    s_fin[g] = f;
+    s_ts[g] = acc;
+    acc += ((f - b + BM_ - 1) / BM_) * NB;
+  }
+  s_ts[G] = acc;
+}
 
 // Tile L -> (group, first row, valid rows, n-block).  Inside a group the tiles are
 // rasterised in bands of GM_ m-tiles, m fastest, so concurrently running CTAs share the
 // weight tiles of a few n-blocks and the rows of a few m-tiles.
 template <int BM_, int GM_>
-__device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_off, int G, int NB) {
+__device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_beg, const int* s_fin, int G,
+                                                   int NB) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -67,7 +84,7 @@ __device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const
   TileCoord t;
   t.g = lo;
   const int local = L - s_ts[lo];
-  const int rows = s_off[lo + 1] - s_off[lo];
+  const int rows = s_fin[lo] - s_beg[lo];
   const int mt_g = (rows + BM_ - 1) / BM_;
   const int band = local / (GM_ * NB);
   const int m_first = band * GM_;
@@ -75,30 +92,8 @@ __device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const
   const int r = local - band * GM_ * NB;
   const int mt = m_first + r % gm;
   t.nb = r / gm;
-  t.row0 = s_off[lo] + mt * BM_;
-  t.rows_valid = min(BM_, s_off[lo + 1] - t.row0);
-  return t;
-}
-
-__device__ __forceinline__ TileCoord decode_tile(int L, const int* s_ts, const int* s_off, int G, int NB) {
-  int lo = 0, hi = G - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_ts[mid] <= L) lo = mid; else hi = mid - 1;
-  }
-  TileCoord t;
-  t.g = lo;
-  const int local = L - s_ts[lo];
-  const int rows = s_off[lo + 1] - s_off[lo];
-  const int mt_g = (rows + BM - 1) / BM;
-  const int band = local / (GM * NB);
-  const int m_first = band * GM;
-  const int gm = min(mt_g - m_first, GM);
-  const int r = local - band * GM * NB;
-  const int mt = m_first + r % gm;
-  t.nb = r / gm;
-  t.row0 = s_off[lo] + mt * BM;
-  t.rows_valid = min(BM, s_off[lo + 1] - t.row0);
+  t.row0 = s_beg[lo] + mt * BM_;
+  t.rows_valid = min(BM_, s_fin[lo] - t.row0);
   return t;
 }
 
@@ -172,8 +167,8 @@ template <int EPI, typename OutT>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
-                        const int32_t* __restrict__ offsets, int G, int N, int K, int rows_cap,
-                        uint32_t idesc) {
+                        const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
+                        int K, int rows_cap, uint32_t idesc) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -182,8 +177,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);  // set when a wait gives up
-  int* s_off = reinterpret_cast<int*>(s_tmem + 4);
-  int* s_ts = s_off + (MAX_GROUPS + 1);
+  int* s_beg = reinterpret_cast<int*>(s_tmem + 4);
+  int* s_fin = s_beg + (MAX_GROUPS + 1);
+  int* s_ts = s_fin + (MAX_GROUPS + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -198,13 +194,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    // group boundaries, forced monotonic and inside [0, rows_cap] so that no tile can
-    // read or write past the row buffers whatever the caller passed
-    int prev = 0;
-    for (int i = 0; i <= G; ++i) {
-      prev = min(max(offsets[i], prev), rows_cap);
-      s_off[i] = prev;
-    }
+    build_group_table<BM>(offsets, ends, G, rows_cap, NB, s_beg, s_fin, s_ts);
   }
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -222,15 +212,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (EPI == SMOE_EPI_SWIGLU) tma_prefetch_desc(&tmB3);
   }
   if (warp == 1) tmem_alloc(smem_u32(s_tmem), 2 * BN);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int g = 0; g < G; ++g) {
-      s_ts[g] = acc;
-      acc += ((s_off[g + 1] - s_off[g] + BM - 1) / BM) * NB;
-    }
-    s_ts[G] = acc;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -245,7 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
-        const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
+        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
         const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
@@ -305,7 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
-      const TileCoord t = decode_tile(L, s_ts, s_off, G, NB);
+      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
       if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       const bool row_ok = r < t.rows_valid;
@@ -380,7 +361,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
 constexpr int GM = 8;
 constexpr int NUM_BARS = 2 * STAGES + 5;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 2 * (MAX_GROUPS + 1) * 4;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 * (MAX_GROUPS + 1) * 4;
 }  // namespace pair
 
 __device__ __forceinline__ void mbar_wait_drain_cluster(uint32_t bar, uint32_t parity) {
@@ -397,8 +378,8 @@ template <int EPI, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
-                             const int32_t* __restrict__ offsets, int G, int N, int K, int rows_cap,
-                             uint32_t idesc) {
+                             const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
+                             int K, int rows_cap, uint32_t idesc) {
   constexpr int BM = pair::BM, BMC = pair::BMC, STAGES = pair::STAGES, GM = pair::GM;
   constexpr int A_BYTES = pair::A_BYTES, B_BYTES = pair::B_BYTES, NUM_BARS = pair::NUM_BARS;
   constexpr int PAIR_STAGE_BYTES = pair::PAIR_STAGE_BYTES;
@@ -410,8 +391,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  int* s_off = reinterpret_cast<int*>(s_tmem + 4);
-  int* s_ts = s_off + (MAX_GROUPS + 1);
+  int* s_beg = reinterpret_cast<int*>(s_tmem + 4);
+  int* s_fin = s_beg + (MAX_GROUPS + 1);
+  int* s_ts = s_fin + (MAX_GROUPS + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -429,11 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    int prev = 0;
-    for (int i = 0; i <= G; ++i) {
-      prev = min(max(offsets[i], prev), rows_cap);
-      s_off[i] = prev;
-    }
+    build_group_table<BM>(offsets, ends, G, rows_cap, NB, s_beg, s_fin, s_ts);
   }
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -451,15 +429,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (EPI == SMOE_EPI_SWIGLU) tma_prefetch_desc(&tmB3);
   }
   if (warp == 1) tmem_alloc_pair(smem_u32(s_tmem), 2 * BN);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int g = 0; g < G; ++g) {
-      s_ts[g] = acc;
-      acc += ((s_off[g + 1] - s_off[g] + BM - 1) / BM) * NB;
-    }
-    s_ts[G] = acc;
-  }
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
@@ -475,7 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int L = pair_id; L < total && ok; L += npairs) {
-        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_off, G, NB);
+        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
         const int a_row = t.row0 + (int)rank * BMC;
         const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN + (int)rank * 128;
         const void* bmap = (EPI == SMOE_EPI_SWIGLU && rank == 1) ? (const void*)&tmB3 : (const void*)&tmB;
@@ -535,7 +504,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = pair_id; L < total; L += npairs) {
-      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_off, G, NB);
+      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
       if (!mbar_wait_cluster(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       const int row_base = t.row0 + (int)rank * BMC;

@@ -366,10 +366,12 @@ class ExpertParallelExchange:
 
     def _forward_p2p_local_first(self, x, idx, w, experts, shared=None, timer=None):
         """Peer-copy exchange without a capacity limit.  The rows this rank routes to its
-        OWN experts are contiguous in its send buffer and need no exchange: their expert
-        GEMMs are queued before the host waits for the count matrix, so the count
-        exchange, the host's bookkeeping and the copies of every other rank's rows over
-        NVLink (one copy stream per peer) all run underneath them."""
+        OWN experts are contiguous in its send buffer and need no exchange.  The first
+        half of each local expert's rows is computed before the host waits for the count
+        matrix, so the count exchange, the host's bookkeeping and the copies of every
+        other rank's rows over NVLink (one copy stream per peer) run underneath it; the
+        second half is computed after the other ranks' rows, underneath the copies that
+        return their outputs."""
         from .p2p import PeerBuffers, copy_segments, view
         ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
         T, k = idx.shape
@@ -400,10 +402,12 @@ class ExpertParallelExchange:
             self._host[:ws * E].copy_(G.view(-1), non_blocking=True)
             ev_counts = _record(comm)
         mark("counts_done")
-        self_offsets = plan["offsets"][me * El:(me + 1) * El + 1]
-        mark("experts_self_start")
-        y_self = experts(send, self_offsets)
-        mark("experts_self_end")
+        offs = plan["offsets"][me * El:(me + 1) * El + 1]
+        starts, fins = offs[:-1], offs[1:]
+        mids = starts + (fins - starts) // 2                      # first / second half of each expert
+        mark("experts_selfA_start")
+        y_a = experts(send, starts, ends=mids)
+        mark("experts_selfA_end")
         ev_counts.synchronize()
         Gh = self._host[:ws * E].numpy().reshape(ws, ws, El).astype(np.int64)   # [src, dst, El]
         R = Gh.sum(2)                                  # rows src -> dst
@@ -422,11 +426,15 @@ class ExpertParallelExchange:
                        for r in range(ws)], comm, send)
         self._barrier(comm)
         ev_sent = _record(comm)
-        # this rank's own rows: expert outputs go straight to the return buffer
+        # this rank's own rows: expert outputs are copied into the return buffer, whose
+        # layout is the send layout (the same row numbers as in `send`)
         ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
-        a0, n0 = int(SD[me, me]), int(R[me, me])
-        y_self.record_stream(comp)
-        copy_segments([(ret_local.data_ptr() + a0 * rb, y_self.data_ptr() + a0 * rb, n0 * rb)], comp)
+        own = Gh[me, me, :]                                       # rows per local expert
+        a_e = int(SD[me, me]) + np.concatenate([[0], np.cumsum(own)[:-1]])
+        m_e = a_e + own // 2
+        rbase = ret_local.data_ptr()
+        copy_segments([(rbase + int(a) * rb, y_a.data_ptr() + int(a) * rb, int(m - a) * rb)
+                       for a, m in zip(a_e, m_e)], comp)
         # rows from the other ranks
         mark("wait_sent0_before")
         _wait(comp, ev_sent)
@@ -440,7 +448,7 @@ class ExpertParallelExchange:
         mark("experts0_start")
         y = experts(xe, rg["offsets"])
         mark("experts0_end")
-        self.last_rows = n0 + rg["rows_cap"]
+        self.last_rows = int(R[me, me]) + rg["rows_cap"]
         back = self.k.gather_rows(y, rg["recv_dst"], n_recv)
         comm.wait_stream(comp)
         bbase = back.data_ptr()
@@ -449,6 +457,13 @@ class ExpertParallelExchange:
                        for s_ in range(ws)], comm, back)
         self._barrier(comm)
         ev_ret = _record(comm)
+        # second half of the own rows, underneath the return copies
+        mark("experts_selfB_start")
+        y_b = experts(send, mids, ends=fins)
+        mark("experts_selfB_end")
+        f_e = a_e + own
+        copy_segments([(rbase + int(m) * rb, y_b.data_ptr() + int(m) * rb, int(f - m) * rb)
+                       for m, f in zip(m_e, f_e)], comp)
         mark("combine_start")
         mark("wait_ret0_before")
         _wait(comp, ev_ret)

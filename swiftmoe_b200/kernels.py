@@ -112,9 +112,10 @@ def combine(y: torch.Tensor, slot_row: torch.Tensor, w: torch.Tensor, T: int, k:
 
 def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, *, B3: Optional[torch.Tensor] = None,
                  epilogue: int = L.SMOE_EPI_STORE, out_dtype: Optional[torch.dtype] = None,
-                 out: Optional[torch.Tensor] = None):
-    """C[rows_cap, N] for groups defined by device offsets [G+1]; B is [G, N, K]."""
-    _need_cuda(A, B, B3, offsets)
+                 out: Optional[torch.Tensor] = None, ends: Optional[torch.Tensor] = None):
+    """C[rows_cap, N] for groups of rows [offsets[g], offsets[g+1]) -- or [offsets[g],
+    ends[g]) when ``ends`` is given -- of A; B is [G, N, K]."""
+    _need_cuda(A, B, B3, offsets, ends)
     rows_cap, K = A.shape
     G, N, K2 = B.shape
     if K2 != K:
@@ -123,7 +124,7 @@ def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, *, B3:
     if out is None:
         out = torch.empty((max(rows_cap, 1), N), dtype=od, device=A.device)
     L.check(L.load().smoe_grouped_gemm(L.ptr(A), L.ptr(B), L.ptr(B3), L.ptr(out), L.dtype_code(A.dtype),
-                                       L.dtype_code(od), epilogue, L.ptr(offsets), G, rows_cap, N, K,
+                                       L.dtype_code(od), epilogue, L.ptr(offsets), L.ptr(ends), G, rows_cap, N, K,
                                        L.stream_handle(A.device)), "smoe_grouped_gemm")
     return out
 

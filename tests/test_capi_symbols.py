@@ -51,7 +51,7 @@ def test_invalid_arguments_rejected_before_any_device_call(lib):
     # k > E, k > 32, bad dtype: rejected by validation, no CUDA call is made
     assert lib.smoe_router_fwd(None, None, 2, None, 10, 64, 4, 5, None, None, None, None, 0, None) == -1
     assert lib.smoe_topk_from_logits(None, 10, 64, 33, None, None, None) == -1
-    assert lib.smoe_grouped_gemm(None, None, None, None, 2, 2, 0, None, 1, 10, 8, 8, None) == -1
+    assert lib.smoe_grouped_gemm(None, None, None, None, 2, 2, 0, None, None, 1, 10, 8, 8, None) == -1
     assert lib.smoe_combine(None, 9, None, None, 1, 2, 8, None, None, None) == -1
     a = _lib.LayerArgs()
     a.tokens, a.d_model, a.num_experts, a.top_k, a.dtype = 10, 64, 8, 9, 2

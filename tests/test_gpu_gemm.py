@@ -106,3 +106,24 @@ def test_transpose_batched(K):
     assert torch.equal(K.transpose_batched(x), x.transpose(1, 2).contiguous())
     xb = x.bfloat16()
     assert torch.equal(K.transpose_batched(xb), xb.transpose(1, 2).contiguous())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_grouped_row_ranges(K, dtype):
+    """Groups given as explicit [start, end) row ranges (not contiguous): rows outside
+    every range are not written."""
+    sizes = [300, 170, 0, 500]
+    A, B, B3, offs, rows = make_groups(sizes, 256, 192, dtype, seed=9)
+    o = offs.tolist()
+    starts = torch.tensor([o[g] + (o[g + 1] - o[g]) // 3 for g in range(4)], dtype=torch.int32)
+    ends = torch.tensor([o[g + 1] - (o[g + 1] - o[g]) // 4 for g in range(4)], dtype=torch.int32)
+    sentinel = torch.full((rows, 192), 7.0, dtype=dtype, device="cuda")
+    out = K.grouped_gemm(A.cuda(), B.cuda(), starts.cuda(), ends=ends.cuda(), out=sentinel)
+    ref = ref_store(A, B, offs)
+    got = out.float().cpu()
+    inside = torch.zeros(rows, dtype=torch.bool)
+    for g in range(4):
+        inside[starts[g]:ends[g]] = True
+    assert (got[~inside] == 7.0).all()
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert max_abs_err(got[inside].numpy(), ref[inside].numpy()) <= tol * max(1.0, ref.abs().max().item())
