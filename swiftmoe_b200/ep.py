@@ -366,12 +366,12 @@ class ExpertParallelExchange:
 
     def _forward_p2p_local_first(self, x, idx, w, experts, shared=None, timer=None):
         """Peer-copy exchange without a capacity limit.  The rows this rank routes to its
-        OWN experts are contiguous in its send buffer and need no exchange.  The first
-        half of each local expert's rows is computed before the host waits for the count
-        matrix, so the count exchange, the host's bookkeeping and the copies of every
-        other rank's rows over NVLink (one copy stream per peer) run underneath it; the
-        second half is computed after the other ranks' rows, underneath the copies that
-        return their outputs."""
+        OWN experts are contiguous in its send buffer and need no exchange.  They are
+        computed before the host waits for the count matrix, so the count exchange, the
+        host's bookkeeping and the copies of every other rank's rows over NVLink (one copy
+        stream per peer) run underneath them.  From 4 ranks on, only the first half of
+        each local expert's rows goes first and the second half is computed after the
+        other ranks' rows, underneath the copies that return their outputs."""
         from .p2p import PeerBuffers, copy_segments, view
         ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
         T, k = idx.shape
@@ -404,7 +404,11 @@ class ExpertParallelExchange:
         mark("counts_done")
         offs = plan["offsets"][me * El:(me + 1) * El + 1]
         starts, fins = offs[:-1], offs[1:]
-        mids = starts + (fins - starts) // 2                      # first / second half of each expert
+        # With 2 ranks half of the rows are local and the local GEMMs alone hide the whole
+        # dispatch; splitting them would only add tail waves.  From 4 ranks on, the local
+        # rows are split in two halves around the remote rows.
+        split = ws >= 4
+        mids = starts + (fins - starts) // 2 if split else fins
         mark("experts_selfA_start")
         y_a = experts(send, starts, ends=mids)
         mark("experts_selfA_end")
@@ -431,7 +435,7 @@ class ExpertParallelExchange:
         ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
         own = Gh[me, me, :]                                       # rows per local expert
         a_e = int(SD[me, me]) + np.concatenate([[0], np.cumsum(own)[:-1]])
-        m_e = a_e + own // 2
+        m_e = a_e + (own // 2 if split else own)
         rbase = ret_local.data_ptr()
         copy_segments([(rbase + int(a) * rb, y_a.data_ptr() + int(a) * rb, int(m - a) * rb)
                        for a, m in zip(a_e, m_e)], comp)
@@ -457,13 +461,13 @@ class ExpertParallelExchange:
                        for s_ in range(ws)], comm, back)
         self._barrier(comm)
         ev_ret = _record(comm)
-        # second half of the own rows, underneath the return copies
-        mark("experts_selfB_start")
-        y_b = experts(send, mids, ends=fins)
-        mark("experts_selfB_end")
-        f_e = a_e + own
-        copy_segments([(rbase + int(m) * rb, y_b.data_ptr() + int(m) * rb, int(f - m) * rb)
-                       for m, f in zip(m_e, f_e)], comp)
+        if split:  # second half of the own rows, underneath the return copies
+            mark("experts_selfB_start")
+            y_b = experts(send, mids, ends=fins)
+            mark("experts_selfB_end")
+            f_e = a_e + own
+            copy_segments([(rbase + int(m) * rb, y_b.data_ptr() + int(m) * rb, int(f - m) * rb)
+                           for m, f in zip(m_e, f_e)], comp)
         mark("combine_start")
         mark("wait_ret0_before")
         _wait(comp, ev_ret)
