@@ -32,8 +32,26 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-layer fwd tokens/sec at 1/2/4/8 B200; exposed all-to-all ms; % of roofline"
-D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = 4096, 8, 2, 14336, 16384
-WORKLOAD = "mixtral-moe-layer-fwd: d_model 4096, 8 experts top-2 softmax, SwiGLU d_ff 14336, 16384 tok/GPU, bf16"
+# Workloads (tokens are per GPU).  "mixtral" is the default and the headline line; the
+# others are the remaining layer shapes of the benchmark configurations, measured with
+# the same harness.
+WORKLOADS = {
+    "mixtral": dict(d=4096, E=8, k=2, F=14336, T=16384, dtype="bf16", cf=None, shared=0, bias_std=0.0,
+                    name="mixtral-moe-layer-fwd: d_model 4096, 8 experts top-2 softmax, SwiGLU d_ff 14336, "
+                         "16384 tok/GPU, bf16"),
+    "ep-capacity": dict(d=4096, E=64, k=2, F=4096, T=8192, dtype="bf16", cf=1.25, shared=0, bias_std=0.0,
+                        name="ep-moe-layer-fwd: d_model 4096, 64 experts top-2, SwiGLU d_ff 4096, 8192 tok/GPU, "
+                             "capacity factor 1.25 (overflow dropped in index order), bf16"),
+    "fine-grained": dict(d=2048, E=128, k=8, F=1024, T=32768, dtype="bf16", cf=None, shared=1, bias_std=1.5,
+                         name="fine-grained-moe-layer-fwd: d_model 2048, 128 experts + 1 shared, top-8, SwiGLU "
+                              "d_ff 1024, 32768 tok/GPU, router offsets ~N(0,1.5), bf16"),
+    "cpu-runnable-fp32": dict(d=512, E=8, k=2, F=2048, T=4096, dtype="fp32", cf=None, shared=0, bias_std=0.0,
+                              name="small-moe-layer-fwd: d_model 512, 8 experts top-2, SwiGLU d_ff 2048, "
+                                   "4096 tok, fp32"),
+}
+W = WORKLOADS["mixtral"]
+D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = W["d"], W["E"], W["k"], W["F"], W["T"]
+WORKLOAD = W["name"]
 # dram__bytes_read.sum + dram__bytes_write.sum of one grouped SwiGLU (gate/up) GEMM launch,
 # from the ncu capture summarised in profiles/grouped_swiglu_gemm_mixtral.md (None until captured)
 GEMM1_DRAM_BYTES_PER_LAUNCH = None
@@ -45,7 +63,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="swiftmoe", choices=["swiftmoe", "reference"])
-    ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default: the workload's)")
+    ap.add_argument("--workload", default="mixtral", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ep-chunks", type=int, default=None, help="token chunks of the EP exchange")
@@ -197,6 +216,11 @@ def run_reference_arm(args):
 # --------------------------------------------------------------------- GPU arm
 def main():
     args = parse()
+    global D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD
+    wl = WORKLOADS[args.workload]
+    D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD = wl["d"], wl["E"], wl["k"], wl["F"], wl["name"]
+    if args.tokens is None:
+        args.tokens = wl["T"]
     if args.impl == "reference":
         run_reference_arm(args)
         return
@@ -218,9 +242,13 @@ def main():
 
     T = args.tokens
     torch.manual_seed(1234)
-    model = S.UltimateMoE(N_EXPERTS, D_MODEL, use_fp16=False, use_nccl_opt=False, dtype=torch.bfloat16,
+    cdtype = torch.float32 if wl["dtype"] == "fp32" else torch.bfloat16
+    model = S.UltimateMoE(N_EXPERTS, D_MODEL, use_fp16=False, use_nccl_opt=False, dtype=cdtype,
                           top_k=TOP_K, expert_type="swiglu", d_ff=D_FF, device=dev,
-                          enable_profiling=(ws > 1))
+                          enable_profiling=(ws > 1), capacity_factor=wl["cf"],
+                          num_shared_experts=wl["shared"], d_ff_shared=D_FF)
+    if wl["bias_std"]:
+        model.set_logit_bias(torch.randn(N_EXPERTS, generator=torch.Generator().manual_seed(2)) * wl["bias_std"])
     with torch.no_grad():
         g = torch.Generator(device=dev).manual_seed(7)   # identical gate on every rank
         model.gate_weight.copy_(torch.randn(model.gate_weight.shape, generator=g, device=dev) * 0.02)
@@ -229,7 +257,7 @@ def main():
             model.comm.chunks = args.ep_chunks
         if args.ep_transport:
             model.comm.transport = args.ep_transport
-    x = torch.randn((T, D_MODEL), device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(100 + rank))
+    x = torch.randn((T, D_MODEL), device=dev, dtype=cdtype, generator=torch.Generator(device=dev).manual_seed(100 + rank))
     out = torch.empty_like(x)
 
     def barrier():
@@ -282,21 +310,36 @@ def main():
         stage_ms = {k: v for k, v in s.items()}
         exposed = s.get("Exposed_A2A", 0.0)
     burst, sustained, hbm, src = peaks()
-    S_rows = T * TOP_K
+    # routed rows this rank computed (capacity drops included), from the plan / exchange
+    if ws == 1:
+        S_rows = T * TOP_K if wl["cf"] is None else None
+    else:
+        S_rows = model.comm.last_rows
+    if S_rows is None:  # one GPU with a capacity: kept rows = sum of the plan's kept counts
+        from swiftmoe_b200._core import capacity_rows
+        from swiftmoe_b200 import kernels as KK
+        cap = capacity_rows(wl["cf"], T, 1, TOP_K, N_EXPERTS)
+        idx_, _ = KK.router(x, model.gate_weight, TOP_K, model.logit_bias)
+        S_rows = int(torch.clamp(torch.bincount(idx_.flatten().long(), minlength=N_EXPERTS), max=cap).sum())
     if ws == 1:
         gemm1_ms = stage_ms["Expert_GEMM1"]
         flops = 2.0 * S_rows * D_MODEL * 2 * D_FF
-        kname = "grouped SwiGLU gate/up GEMM (tcgen05)"
+        kname = "grouped SwiGLU gate/up GEMM (tcgen05)" if cdtype != torch.float32 else \
+            "grouped SwiGLU gate/up GEMM (fp32 FFMA)"
     else:
         gemm1_ms = stage_ms["Expert_Compute"]
         flops = 6.0 * S_rows * D_MODEL * D_FF
-        kname = "expert FFN (both grouped GEMMs, tcgen05); rows assumed balanced (T*k per rank)"
+        kname = "expert FFN (both grouped GEMMs, tcgen05), routed rows of this rank"
+    if wl["shared"]:
+        flops_shared = 6.0 * T * D_MODEL * D_FF
+    else:
+        flops_shared = 0.0
     achieved = flops / (gemm1_ms / 1e3) / 1e12
     roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": sustained,
                 "peak_kind": f"bf16_tflops_sustained ({src})", "unit": "TFLOP/s", "frac": achieved / sustained,
-                "traffic": GEMM1_DRAM_BYTES_PER_LAUNCH, "algorithmic_flops_per_launch": flops,
-                "launch_ms": gemm1_ms}
-    layer_flops = 6.0 * S_rows * D_MODEL * D_FF + 2.0 * T * D_MODEL * N_EXPERTS
+                "traffic": GEMM1_DRAM_BYTES_PER_LAUNCH if args.workload == "mixtral" and ws == 1 else None,
+                "algorithmic_flops_per_launch": flops, "launch_ms": gemm1_ms}
+    layer_flops = 6.0 * S_rows * D_MODEL * D_FF + flops_shared + 2.0 * T * D_MODEL * N_EXPERTS
     layer_frac = layer_flops / (ms / 1e3) / 1e12 / sustained
 
     # end-to-end through the public API: every step copies its input from pinned host
@@ -356,7 +399,7 @@ def main():
 
     launches_per_step = 8 if ws == 1 else 12
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "mixtral":
         try:
             cpu, _, _ = cpu_reference(args.cpu_seconds)
         except Exception as ex:  # reported, never fatal
@@ -364,13 +407,16 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16",
+                "vs_baseline": None, "dtype": wl["dtype"],
                 "data": "synthetic: x ~ N(0,1), weights N(0,0.02), seeded",
                 "config": {"workload": WORKLOAD, "d_model": D_MODEL, "num_experts": N_EXPERTS, "top_k": TOP_K,
                            "d_ff": D_FF, "tokens_per_gpu": T, "parallelism": f"ep{ws}",
+                           "capacity_factor": wl["cf"], "shared_experts": wl["shared"],
                            "ep_exchange": None if ws == 1 else
                            f"{model.comm.transport} transport, {model.comm.n_chunks(T)} token chunks",
-                           "l2": "inputs larger than L2: x 128 MiB and 2.82 GB of expert weights read every step"},
+                           "l2": f"inputs larger than L2: x {x.numel() * x.element_size() / 2**20:.0f} MiB and "
+                                 f"{3 * model.exp_per_rank * D_FF * D_MODEL * x.element_size() / 1e9:.2f} GB of "
+                                 f"expert weights read every step"},
                 "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
                 "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,
                 "cpu_baseline": cpu, "clocks": clk.summary()}
