@@ -128,6 +128,20 @@ __global__ void fill_two_kernel(int32_t* p, int32_t a, int32_t b) {
 }
 
 // ------------------------------------------------------------------ grouped GEMM
+// Raster band height (m-tiles) of the tensor-core GEMMs.  The SwiGLU gate/up GEMM
+// (K = d_model, short rows) uses bands of 32 m-tiles: with the Mixtral shape that is a
+// whole expert, whose 32 MB of rows stay in L2 while every weight tile is read from DRAM
+// once.  The down GEMM (K = d_ff, 3.7 MB per row tile) keeps bands of 16.
+// SMOE_RASTER_BAND overrides both (measurements).
+int raster_band(int epi) {
+  static const char* forced = getenv("SMOE_RASTER_BAND");
+  if (forced) {
+    const int v = atoi(forced);
+    if (v > 0) return v;
+  }
+  return epi == SMOE_EPI_SWIGLU ? 32 : tc::GM_DEFAULT;
+}
+
 template <int EPI, typename OutT>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
               const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
@@ -136,7 +150,7 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
   kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
-                                                         K, (int)rows_cap, idesc);
+                                                         K, (int)rows_cap, raster_band(EPI), idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
@@ -150,7 +164,7 @@ int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   SMOE_CK(ensure_smem(kern, tc::pair::SMEM_BYTES, &done));
   const int grid = device_sms() & ~1;  // whole CTA pairs
   kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
-                                                        K, (int)rows_cap, idesc);
+                                                        K, (int)rows_cap, raster_band(EPI) / 2, idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

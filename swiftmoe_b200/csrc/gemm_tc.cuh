@@ -31,7 +31,7 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
 constexpr int MAX_GROUPS = 1024;
-constexpr int GM = 16;  // m-tiles per rasterisation band
+constexpr int GM_DEFAULT = 16;  // m-tiles per rasterisation band unless the launch asks otherwise
 constexpr int NUM_BARS = 2 * STAGES + 5;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 * (MAX_GROUPS + 1) * 4;
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 200 ms
@@ -72,10 +72,11 @@ __device__ __forceinline__ void build_group_table(const int32_t* offsets, const 
 
 // Tile L -> (group, first row, valid rows, n-block).  Inside a group the tiles are
 // rasterised in bands of GM_ m-tiles, m fastest, so concurrently running CTAs share the
-// weight tiles of a few n-blocks and the rows of a few m-tiles.
-template <int BM_, int GM_>
+// weight tiles of a few n-blocks and the rows of a few m-tiles.  A band as tall as the
+// group reads every weight tile from DRAM once, provided the group's rows fit in L2.
+template <int BM_>
 __device__ __forceinline__ TileCoord decode_tile_t(int L, const int* s_ts, const int* s_beg, const int* s_fin, int G,
-                                                   int NB) {
+                                                   int NB, int GM_) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
                         const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
-                        int K, int rows_cap, uint32_t idesc) {
+                        int K, int rows_cap, int gm, uint32_t idesc) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
-        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
+        const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
         const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
-      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
+      const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
       if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       const bool row_ok = r < t.rows_valid;
@@ -359,7 +360,6 @@ constexpr int A_BYTES = BMC * BK * 2;
 constexpr int B_BYTES = (BN / 2) * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
-constexpr int GM = 8;
 constexpr int NUM_BARS = 2 * STAGES + 5;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 * (MAX_GROUPS + 1) * 4;
 }  // namespace pair
@@ -379,8 +379,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
                              const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
-                             int K, int rows_cap, uint32_t idesc) {
-  constexpr int BM = pair::BM, BMC = pair::BMC, STAGES = pair::STAGES, GM = pair::GM;
+                             int K, int rows_cap, int gm, uint32_t idesc) {
+  constexpr int BM = pair::BM, BMC = pair::BMC, STAGES = pair::STAGES;
   constexpr int A_BYTES = pair::A_BYTES, B_BYTES = pair::B_BYTES, NUM_BARS = pair::NUM_BARS;
   constexpr int PAIR_STAGE_BYTES = pair::PAIR_STAGE_BYTES;
   extern __shared__ unsigned char smem_raw[];
@@ -444,7 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int L = pair_id; L < total && ok; L += npairs) {
-        const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
+        const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
         const int a_row = t.row0 + (int)rank * BMC;
         const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN + (int)rank * 128;
         const void* bmap = (EPI == SMOE_EPI_SWIGLU && rank == 1) ? (const void*)&tmB3 : (const void*)&tmB;
@@ -504,7 +504,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = pair_id; L < total; L += npairs) {
-      const TileCoord t = decode_tile_t<BM, GM>(L, s_ts, s_beg, s_fin, G, NB);
+      const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
       if (!mbar_wait_cluster(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       const int row_base = t.row0 + (int)rank * BMC;
