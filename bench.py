@@ -52,9 +52,10 @@ WORKLOADS = {
 W = WORKLOADS["mixtral"]
 D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = W["d"], W["E"], W["k"], W["F"], W["T"]
 WORKLOAD = W["name"]
-# dram__bytes_read.sum + dram__bytes_write.sum of one grouped SwiGLU (gate/up) GEMM launch,
-# from the ncu capture summarised in profiles/grouped_swiglu_gemm_mixtral.md (None until captured)
-GEMM1_DRAM_BYTES_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one grouped SwiGLU (gate/up) GEMM launch
+# of the default workload at full size (2.906 GB read + 0.929 GB written), from the ncu
+# capture summarised in profiles/grouped_gemm_mixtral_T16384_dram.md
+GEMM1_DRAM_BYTES_PER_LAUNCH = 3834612224
 
 
 def parse():
