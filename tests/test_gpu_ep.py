@@ -104,3 +104,41 @@ def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
         assert agree > 0.99
         assert err <= 2e-2, (r, err)
         assert same_bits == 1.0
+
+
+def _ref_fixture_worker(rank, ws, port, name, transport, out_dir):
+    sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "tests" / "golden")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
+                      NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    import fixtures as fx
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    import swiftmoe_b200 as S
+    f, p = fx.ult_linear(name)
+    E, d = f["E"], f["d"]
+    El = E // ws
+    m = S.UltimateMoE(E, d, use_fp16=False, use_nccl_opt=False).to(dev)
+    m.comm.transport = transport
+    with torch.no_grad():
+        m.gate_weight.copy_(torch.from_numpy(p.gate))
+        m.expert_weights.copy_(torch.from_numpy(p.expert_w[rank * El:(rank + 1) * El]))
+    out = m(torch.from_numpy(f["x"][rank]).to(dev)).cpu().numpy()
+    err = float(np.abs(out - f["out"][rank]).max())
+    np.save(os.path.join(out_dir, f"ref{rank}.npy"), np.array([err]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
+@pytest.mark.parametrize("name,ws", [("ult_linear_fp32_ws2_E8_d32_M23", 2), ("ult_linear_fp32_ws4_E8_d32_M17", 4)])
+def test_ep_matches_reference_ultimate_moe(tmp_path, name, ws, transport):
+    """fp32 UltimateMoE over `ws` GPUs against the reference's own UltimateMoE run with the
+    same world size (gloo, CPU): max-abs 1e-5 on every rank."""
+    if torch.cuda.device_count() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    mp.spawn(_ref_fixture_worker, args=(ws, _port(), name, transport, str(tmp_path)), nprocs=ws, join=True)
+    for r in range(ws):
+        assert float(np.load(tmp_path / f"ref{r}.npy")[0]) <= 1e-5
