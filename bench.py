@@ -148,6 +148,13 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- CPU arm
+def _host_threads():
+    """All host threads this process may run on.  torchrun sets OMP_NUM_THREADS=1 for its
+    workers, so the BLAS pool is raised back to the affinity mask before timing."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=len(os.sched_getaffinity(0)))
+
+
 def cpu_reference(tokens_budget_s: float, sample_tokens: int = 64, seed: int = 0):
     """Time the numpy restatement of the reference forward on this host's cores."""
     import numpy as np
@@ -163,15 +170,16 @@ def cpu_reference(tokens_budget_s: float, sample_tokens: int = 64, seed: int = 0
 
     p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
     x = rng.standard_normal((sample_tokens, d), dtype=np.float32)
-    O.moe_forward([x[:8]], p, k=TOP_K)  # warm BLAS
-    done, t0 = 0, time.perf_counter()
-    while True:
-        O.moe_forward([x], p, k=TOP_K)
-        done += sample_tokens
-        el = time.perf_counter() - t0
-        if el >= tokens_budget_s:
-            break
-    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    with _host_threads():
+        O.moe_forward([x[:8]], p, k=TOP_K)  # warm BLAS
+        done, t0 = 0, time.perf_counter()
+        while True:
+            O.moe_forward([x], p, k=TOP_K)
+            done += sample_tokens
+            el = time.perf_counter() - t0
+            if el >= tokens_budget_s:
+                break
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     return {"value": done / el, "unit": "tokens/s", "cores": int(threads), "kind": "port",
             "sample": f"{done} tokens in batches of {sample_tokens} through the full layer "
                       f"(numpy fp32, oracle/moe_oracle.py), {el:.1f} s"}, p, x
@@ -194,14 +202,15 @@ def run_reference_arm(args):
     p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
     sample = 64
     x = rng.standard_normal((sample, d), dtype=np.float32)
-    for _ in range(args.warmup):
-        O.moe_forward([x], p, k=TOP_K)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.moe_forward([x], p, k=TOP_K)
-    el = time.perf_counter() - t0
+    with _host_threads():
+        for _ in range(args.warmup):
+            O.moe_forward([x], p, k=TOP_K)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            O.moe_forward([x], p, k=TOP_K)
+        el = time.perf_counter() - t0
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     v = sample * args.steps / el
-    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
