@@ -70,6 +70,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ep-chunks", type=int, default=None, help="token chunks of the EP exchange")
     ap.add_argument("--ep-transport", default=None, choices=["p2p", "collective"])
+    ap.add_argument("--ep-schedule", default=None, choices=["local_first", "chunked"],
+                    help="overlap schedule of the p2p exchange")
+    ap.add_argument("--ep-return", default=None, choices=["fused", "copy"],
+                    help="local-first return: GEMM epilogue stores to the peers, or copies")
     return ap.parse_args()
 
 
@@ -224,6 +228,16 @@ def run_reference_arm(args):
 
 
 # --------------------------------------------------------------------- GPU arm
+def count_launches(fn):
+    """Kernels of libswiftmoe (namespace smoe) launched by fn(), from a CUPTI trace."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "smoe" in e.name)
+
+
 def main():
     args = parse()
     global D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD
@@ -267,6 +281,10 @@ def main():
             model.comm.chunks = args.ep_chunks
         if args.ep_transport:
             model.comm.transport = args.ep_transport
+        if args.ep_schedule:
+            model.comm.schedule = args.ep_schedule
+        if args.ep_return:
+            model.comm.return_mode = args.ep_return
     x = torch.randn((T, D_MODEL), device=dev, dtype=cdtype, generator=torch.Generator(device=dev).manual_seed(100 + rank))
     out = torch.empty_like(x)
 
@@ -407,7 +425,13 @@ def main():
            "mode": "UltimateMoE.forward; pinned host input/output copied every step, double-buffered "
                    "so copies of neighbouring steps overlap the forward"}
 
-    launches_per_step = 8 if ws == 1 else 12
+    # this library's kernels in one forward, counted from the CUDA activity trace of an
+    # untimed forward (every rank runs it: the forward holds collectives)
+    try:
+        launches_per_step, launches_src = count_launches(lambda: model(x)), "CUPTI trace of one forward"
+    except Exception as e:  # no activity trace on this host: the static count of the path
+        launches_per_step = 8 if ws == 1 else (16 if ws >= 4 else 14)
+        launches_src = f"static count (trace failed: {type(e).__name__})"
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "mixtral":
         try:
@@ -423,11 +447,16 @@ def main():
                            "d_ff": D_FF, "tokens_per_gpu": T, "parallelism": f"ep{ws}",
                            "capacity_factor": wl["cf"], "shared_experts": wl["shared"],
                            "ep_exchange": None if ws == 1 else
-                           f"{model.comm.transport} transport, {model.comm.n_chunks(T)} token chunks",
+                           f"{model.comm.transport} transport, " + (
+                               f"{model.comm.schedule} schedule, {model.comm.return_mode} return"
+                               if model.comm.schedule == "local_first"
+                               else f"{model.comm.n_chunks(T)} token chunks"),
                            "l2": f"inputs larger than L2: x {x.numel() * x.element_size() / 2**20:.0f} MiB and "
                                  f"{3 * model.exp_per_rank * D_FF * D_MODEL * x.element_size() / 1e9:.2f} GB of "
                                  f"expert weights read every step"},
-                "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+                "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+                "gpu_launches_per_step": launches_per_step, "gpu_launches_source": launches_src,
+                "roofline": roofline,
                 "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,
                 "cpu_baseline": cpu, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)

@@ -146,6 +146,17 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
 SMOE_API int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype,
                       int out_dtype, int epilogue, const int32_t* offsets, const int32_t* ends,
                       int G, int64_t rows_cap, int N, int K, smoe_stream_t stream);
+/* The same grouped GEMM with output row r written at the address row_ptrs[r] (device
+ * array of rows_cap addresses, 16-byte aligned; 0 skips the row) instead of C + r*N.
+ * The addresses may lie in another GPU's memory (IPC-opened peer buffers): the
+ * epilogue then stores the expert outputs straight into the source ranks' return
+ * buffers over NVLink, tile by tile while the GEMM runs, and fences them at system
+ * scope before the kernel exits.  Replaces the return all_to_all_single that follows
+ * the expert loop in models/ultimate_moe.py:152 (MoEAsyncCommHandler.combine_async). */
+SMOE_API int smoe_grouped_gemm_rows(const void* A, const void* B, const void* B3, const uint64_t* row_ptrs,
+                                    int dtype, int out_dtype, int epilogue, const int32_t* offsets,
+                                    const int32_t* ends, int G, int64_t rows_cap, int N, int K,
+                                    smoe_stream_t stream);
 
 /* dst[g, c, r] = src[g, r, c] for G matrices of [R, C] (weight relayout, e.g. the
  * reference's x@W expert_weights [E, d_in, d_out] -> nn.Linear layout [E, d_out, d_in]). */
@@ -178,6 +189,19 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
                                   const int32_t* pos_base, int64_t n_recv, int32_t* expert_counts,
                                   int32_t* expert_offsets, int32_t* row_src, int32_t* recv_dst,
                                   void* workspace, size_t workspace_bytes, smoe_stream_t stream);
+/* Return addresses of the expert-parallel combine.  The receive buffer holds n_src
+ * source segments: received row r with seg_table[s] <= r < seg_table[s+1] came from
+ * source s and goes back to row r - seg_table[s] of that source's return region, whose
+ * address is seg_table[n_src + 1 + s] (an int64 holding a device address, usually in
+ * the source GPU's memory; 16-byte aligned, as is row_bytes).  seg_table is a device
+ * array of 2 * n_src + 1 int64.  Writes row_ptrs[i] for the expert rows i < rows_cap
+ * (0 past expert_offsets[E_l]) for smoe_grouped_gemm_rows, and writes zero rows at the
+ * destinations of received rows the capacity dropped (recv_dst < 0), so the source's
+ * combine adds nothing for those slots.  Replaces, with the GEMM above, the return
+ * path of models/ultimate_moe.py:152,224-231.                                          */
+SMOE_API int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, int E_l,
+                                 const int32_t* recv_dst, int64_t n_recv, const int64_t* seg_table, int n_src,
+                                 int64_t row_bytes, uint64_t* row_ptrs, int64_t rows_cap, smoe_stream_t stream);
 
 /* Expert-parallel exchange buffers.  These are the only allocations of the library:
  * each rank allocates its receive / return buffers once (grown when a batch needs

@@ -225,14 +225,17 @@ class MoECore(nn.Module):
         L.check(lib.smoe_layer_fwd(C.byref(a), L.stream_handle(x.device)), "smoe_layer_fwd")
         return out
 
-    def _experts(self, xe: torch.Tensor, offsets: torch.Tensor, ends: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def _experts(self, xe: torch.Tensor, offsets: torch.Tensor, ends: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None, row_ptrs: Optional[torch.Tensor] = None):
         """Expert outputs for the rows of local expert g: [offsets[g], offsets[g+1]), or
-        [offsets[g], ends[g]) when ``ends`` is given (other rows are left unwritten)."""
+        [offsets[g], ends[g]) when ``ends`` is given (other rows are left unwritten).
+        The output rows go to ``out`` (same row numbers as ``xe``), or to the addresses in
+        ``row_ptrs`` (then None is returned)."""
         if self.expert_type == "swiglu":
             w1, w3, w2 = self._swiglu()
             h = K.grouped_gemm(xe, w1, offsets, B3=w3, epilogue=L.SMOE_EPI_SWIGLU, ends=ends)
-            return K.grouped_gemm(h, w2, offsets, ends=ends)
-        return K.grouped_gemm(xe, self._linear_kmajor(), offsets, ends=ends)
+            return K.grouped_gemm(h, w2, offsets, ends=ends, out=out, row_ptrs=row_ptrs)
+        return K.grouped_gemm(xe, self._linear_kmajor(), offsets, ends=ends, out=out, row_ptrs=row_ptrs)
 
     def _shared_out(self, x: torch.Tensor) -> Optional[torch.Tensor]:
         sh = self._shared()

@@ -144,12 +144,12 @@ int raster_band(int epi) {
 
 template <int EPI, typename OutT>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
-              const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
+              const uint64_t* row_ptrs, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
               cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
-  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
+  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
                                                          K, (int)rows_cap, raster_band(EPI), idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
@@ -157,13 +157,13 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
 
 template <int EPI, typename OutT>
 int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
-                   const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
+                   const uint64_t* row_ptrs, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
               cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::grouped_gemm_pair_kernel<EPI, OutT>;
   SMOE_CK(ensure_smem(kern, tc::pair::SMEM_BYTES, &done));
   const int grid = device_sms() & ~1;  // whole CTA pairs
-  kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, offsets, ends, G, N,
+  kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
                                                         K, (int)rows_cap, raster_band(EPI) / 2, idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
@@ -182,10 +182,13 @@ bool use_pair_kernel(int64_t rows_cap, int G) {
   return forced != nullptr && strcmp(forced, "2sm") == 0;
 }
 
+// C [rows_cap, N] (ldc = N), or, when row_ptrs is given, output row r at the address
+// row_ptrs[r] (null: row skipped) and C unused.
 int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
                       const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
-                      cudaStream_t st) {
-  if (!A || !B || !C || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
+                      cudaStream_t st, const uint64_t* row_ptrs = nullptr) {
+  if (row_ptrs) C = nullptr;
+  if (!A || !B || (!C && !row_ptrs) || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
   if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU) return SMOE_ERR_INVALID;
   if (epi == SMOE_EPI_SWIGLU && !B3) return SMOE_ERR_INVALID;
   if (elt_size(dtype) == 0 || elt_size(out_dtype) == 0) return SMOE_ERR_INVALID;
@@ -196,17 +199,18 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, 32) : cdiv(N, simt::BN)));
     if (epi == SMOE_EPI_SWIGLU)
       simt::grouped_gemm_f32_kernel<SMOE_EPI_SWIGLU><<<grid, simt::THREADS, 0, st>>>(
-          (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, offsets, ends, G, N, K, (int)rows_cap);
+          (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, row_ptrs, offsets, ends, G, N, K,
+          (int)rows_cap);
     else
       simt::grouped_gemm_f32_kernel<SMOE_EPI_STORE><<<grid, simt::THREADS, 0, st>>>(
-          (const float*)A, (const float*)B, nullptr, (float*)C, N, offsets, ends, G, N, K, (int)rows_cap);
+          (const float*)A, (const float*)B, nullptr, (float*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap);
     SMOE_CK(cudaGetLastError());
     return SMOE_OK;
   }
   // 16-bit inputs on tensor cores
   if (G > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
   if (K % 8 != 0 || N % 8 != 0) return SMOE_ERR_UNSUPPORTED;
-  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (B3 && !aligned16(B3))) return SMOE_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(B) || (C && !aligned16(C)) || (B3 && !aligned16(B3))) return SMOE_ERR_UNSUPPORTED;
   if (epi == SMOE_EPI_SWIGLU && out_dtype != dtype) return SMOE_ERR_UNSUPPORTED;
   if (out_dtype != SMOE_F32 && out_dtype != dtype) return SMOE_ERR_UNSUPPORTED;
   const CUtensorMapDataType dt = dtype == SMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -222,22 +226,22 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     const uint32_t idesc2 = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::pair::BM, tc::BN);
     if (epi == SMOE_EPI_SWIGLU)
       return dtype == SMOE_BF16
-                 ? launch_tc_pair<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st)
-                 : launch_tc_pair<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
+                 ? launch_tc_pair<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc2, st)
+                 : launch_tc_pair<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc2, st);
     if (out_dtype == SMOE_F32)
-      return launch_tc_pair<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
+      return launch_tc_pair<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc2, st);
     return dtype == SMOE_BF16
-               ? launch_tc_pair<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st)
-               : launch_tc_pair<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc2, st);
+               ? launch_tc_pair<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc2, st)
+               : launch_tc_pair<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc2, st);
   }
   const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
   if (epi == SMOE_EPI_SWIGLU) {
-    return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st)
-                              : launch_tc<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
+    return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_SWIGLU, __nv_bfloat16>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc, st)
+                              : launch_tc<SMOE_EPI_SWIGLU, __half>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc, st);
   }
-  if (out_dtype == SMOE_F32) return launch_tc<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
-  return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st)
-                            : launch_tc<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, offsets, ends, G, rows_cap, N, K, idesc, st);
+  if (out_dtype == SMOE_F32) return launch_tc<SMOE_EPI_STORE, float>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc, st);
+  return dtype == SMOE_BF16 ? launch_tc<SMOE_EPI_STORE, __nv_bfloat16>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc, st)
+                            : launch_tc<SMOE_EPI_STORE, __half>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc, st);
 }
 
 // ------------------------------------------------------------------ router
@@ -530,6 +534,15 @@ int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int
                            (cudaStream_t)stream);
 }
 
+int smoe_grouped_gemm_rows(const void* A, const void* B, const void* B3, const uint64_t* row_ptrs, int dtype,
+                           int out_dtype, int epilogue, const int32_t* offsets, const int32_t* ends, int G,
+                           int64_t rows_cap, int N, int K, smoe_stream_t stream) {
+  if (!row_ptrs) return SMOE_ERR_INVALID;
+  if (out_dtype != SMOE_F32 && (N * (int64_t)elt_size(out_dtype)) % 16 != 0) return SMOE_ERR_UNSUPPORTED;
+  return grouped_gemm_impl(A, B, B3, nullptr, dtype, out_dtype, epilogue, offsets, ends, G, rows_cap, N, K,
+                           (cudaStream_t)stream, row_ptrs);
+}
+
 int smoe_transpose_batched(const void* src, void* dst, int dtype, int G, int R, int C, smoe_stream_t stream) {
   const int es = elt_size(dtype);
   if (es == 0 || G < 0 || R < 0 || C < 0) return SMOE_ERR_INVALID;
@@ -589,6 +602,22 @@ int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capaci
                                                  capacity, n_recv, row_src, recv_dst);
     SMOE_CK(cudaGetLastError());
   }
+  return SMOE_OK;
+}
+
+int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, int E_l, const int32_t* recv_dst,
+                        int64_t n_recv, const int64_t* seg_table, int n_src, int64_t row_bytes, uint64_t* row_ptrs,
+                        int64_t rows_cap, smoe_stream_t stream) {
+  if (E_l < 1 || n_src < 1 || n_recv < 0 || rows_cap < 0 || row_bytes <= 0 || row_bytes % 16 != 0)
+    return SMOE_ERR_INVALID;
+  if (!expert_offsets || !seg_table || (rows_cap > 0 && (!row_src || !row_ptrs)) || (n_recv > 0 && !recv_dst))
+    return SMOE_ERR_INVALID;
+  if (rows_cap == 0 && n_recv == 0) return SMOE_OK;
+  const int64_t work = std::max<int64_t>(rows_cap, n_recv * 32);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)device_sms() * 8));
+  ep_return_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(row_src, expert_offsets, E_l, recv_dst, n_recv,
+                                                                seg_table, n_src, row_bytes, row_ptrs, rows_cap);
+  SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
 

@@ -23,7 +23,8 @@ __device__ int g_device_error = 0;
 enum DeviceErrorCode : int {
   kErrNone = 0,
   kErrWaitTimeout = 1,   // an mbarrier wait exceeded its time limit
-  kErrBadExpertIndex = 2 // an expert index outside [0, E) reached the dispatch plan
+  kErrBadExpertIndex = 2, // an expert index outside [0, E) reached the dispatch plan
+  kErrBadRowAddress = 3   // a row address of the expert-parallel return was not 16-byte aligned
 };
 
 __device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }

@@ -377,6 +377,55 @@ __global__ void __launch_bounds__(256) ep_regroup_rows_kernel(const int32_t* __r
   }
 }
 
+// Expert-parallel return addresses.  seg[0..nsrc] are the first received row of each
+// source segment (seg[nsrc] = n_recv); seg[nsrc+1+s] is the address of source s's
+// return region.  Received row r goes back to row r - seg[s] of it.
+__device__ __forceinline__ uint64_t ep_return_addr(int64_t r, const int64_t* __restrict__ seg, int nsrc,
+                                                   int64_t row_bytes) {
+  int lo = 0, hi = nsrc - 1;  // last segment whose start <= r
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (seg[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  return (uint64_t)seg[nsrc + 1 + lo] + (uint64_t)((r - seg[lo]) * row_bytes);
+}
+
+// row_ptrs[i] for every expert row i < rows_cap (0 past the kept rows), and zero rows,
+// one warp per row, at the return addresses of received rows the capacity dropped.
+__global__ void __launch_bounds__(256) ep_return_rows_kernel(const int32_t* __restrict__ row_src,
+                                                             const int32_t* __restrict__ offsets, int El,
+                                                             const int32_t* __restrict__ recv_dst, int64_t n_recv,
+                                                             const int64_t* __restrict__ seg, int nsrc,
+                                                             int64_t row_bytes, uint64_t* __restrict__ row_ptrs,
+                                                             int64_t rows_cap) {
+  const int64_t kept = offsets[El];
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < rows_cap; i += nth) {
+    const int64_t r = i < kept ? row_src[i] : -1;
+    uint64_t p = (r >= 0 && r < n_recv) ? ep_return_addr(r, seg, nsrc, row_bytes) : 0;
+    if (p & 15) {
+      set_device_error(kErrBadRowAddress);
+      p = 0;
+    }
+    row_ptrs[i] = p;
+  }
+  const int lane = threadIdx.x & 31;
+  bool wrote = false;
+  for (int64_t r = tid >> 5; r < n_recv; r += nth >> 5) {
+    if (recv_dst[r] >= 0) continue;
+    const uint64_t p = ep_return_addr(r, seg, nsrc, row_bytes);
+    if (p & 15) {
+      if (lane == 0) set_device_error(kErrBadRowAddress);
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(p);
+    for (int64_t j = lane; j < row_bytes / 16; j += 32) dst[j] = make_uint4(0u, 0u, 0u, 0u);
+    wrote = true;
+  }
+  if (wrote) __threadfence_system();  // rows in another GPU's memory: visible before exit
+}
+
 // dst[g][c][r] = src[g][r][c]; 32x32 tiles through shared memory.
 template <typename T>
 __global__ void __launch_bounds__(256) transpose_batched_kernel(const T* __restrict__ src, T* __restrict__ dst, int R,

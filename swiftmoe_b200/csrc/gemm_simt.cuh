@@ -19,7 +19,8 @@ template <int EPI>
 __global__ void __launch_bounds__(THREADS) grouped_gemm_f32_kernel(const float* __restrict__ A,
                                                                    const float* __restrict__ B,
                                                                    const float* __restrict__ B3, float* __restrict__ C,
-                                                                   int64_t ldc, const int32_t* __restrict__ offsets,
+                                                                   int64_t ldc, const uint64_t* __restrict__ row_ptrs,
+                                                                   const int32_t* __restrict__ offsets,
                                                                    const int32_t* __restrict__ ends, int G, int N,
                                                                    int K, int rows_cap) {
   __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS];
@@ -111,7 +112,8 @@ __global__ void __launch_bounds__(THREADS) grouped_gemm_f32_kernel(const float* 
   for (int i = 0; i < 4; ++i) {
     const int row = row0 + ty * 4 + i;
     if (row >= row_end) continue;
-    float* crow = C + (int64_t)row * ldc;
+    float* crow = row_ptrs ? reinterpret_cast<float*>(row_ptrs[row]) : C + (int64_t)row * ldc;
+    if (crow == nullptr) continue;
     if (EPI == SMOE_EPI_SWIGLU) {
       // columns tx and tx+16 are gate; tx+32, tx+48 the matching up columns
 #pragma unroll
@@ -130,6 +132,7 @@ __global__ void __launch_bounds__(THREADS) grouped_gemm_f32_kernel(const float* 
       }
     }
   }
+  if (row_ptrs) __threadfence_system();  // rows in another GPU's memory: visible before exit
 }
 
 }  // namespace simt

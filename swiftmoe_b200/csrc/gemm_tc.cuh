@@ -123,6 +123,18 @@ template <typename H> struct Store16 {
   }
 };
 
+// Destination of one accumulator row: C + row * ldc, or the address held in row_ptrs
+// (for the expert-parallel return, a row of another GPU's buffer); a null address
+// skips the row.
+template <typename OutT>
+__device__ __forceinline__ OutT* out_row(OutT* C, int64_t ldc, const uint64_t* row_ptrs, int row, bool& row_ok) {
+  if (!row_ok) return C;
+  if (row_ptrs == nullptr) return C + (int64_t)row * ldc;
+  const uint64_t p = row_ptrs[row];
+  row_ok = p != 0;
+  return reinterpret_cast<OutT*>(p);
+}
+
 // Drain one 128-row accumulator (this warp's 32 TMEM lanes) into rows of C: SwiGLU on
 // the [gate | up] halves, or a plain store of all BN columns.
 template <int EPI, typename OutT>
@@ -167,7 +179,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool r
 template <int EPI, typename OutT>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
+                        const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                         const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
                         int K, int rows_cap, int gm, uint32_t idesc) {
   extern __shared__ unsigned char smem_raw[];
@@ -290,49 +302,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
       if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
-      const bool row_ok = r < t.rows_valid;
-      OutT* crow = C + (int64_t)(t.row0 + (row_ok ? r : 0)) * ldc;
+      bool row_ok = r < t.rows_valid;
+      OutT* crow = out_row(C, ldc, row_ptrs, t.row0 + r, row_ok);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr (EPI == SMOE_EPI_SWIGLU) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t gv[32], uv[32];
-          tmem_ld32(tbase + c * 32, gv);
-          tmem_ld32(tbase + 128 + c * 32, uv);
-          tmem_ld_wait();
-          float h[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float g = __uint_as_float(gv[j]);
-            const float u = __uint_as_float(uv[j]);
-            h[j] = g / (1.0f + __expf(-g)) * u;
-          }
-          if (row_ok) Store16<OutT>::cols32(crow, t.nb * 128 + c * 32, N, h);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c * 32, v);
-          tmem_ld_wait();
-          if (row_ok) {
-            if constexpr (sizeof(OutT) == 4) {
-              Store<float>::cols32(reinterpret_cast<float*>(crow), t.nb * BN + c * 32, N, v);
-            } else {
-              float f[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-              Store16<OutT>::cols32(crow, t.nb * BN + c * 32, N, f);
-            }
-          }
-        }
-      }
+      const int col0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
+      epilogue_tile<EPI, OutT>(tbase, crow, row_ok, col0, N);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (row_ptrs) __threadfence_system();  // rows in another GPU's memory: visible before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -377,7 +358,7 @@ __device__ __forceinline__ void mbar_wait_drain_cluster(uint32_t bar, uint32_t p
 template <int EPI, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc,
+                             const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                              const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
                              int K, int rows_cap, int gm, uint32_t idesc) {
   constexpr int BM = pair::BM, BMC = pair::BMC, STAGES = pair::STAGES;
@@ -509,8 +490,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row_base = t.row0 + (int)rank * BMC;
       const int rows_valid = min(BMC, t.rows_valid - (int)rank * BMC);
-      const bool row_ok = r < rows_valid;
-      OutT* crow = C + (int64_t)(row_ok ? row_base + r : 0) * ldc;
+      bool row_ok = r < rows_valid;
+      OutT* crow = out_row(C, ldc, row_ptrs, row_base + r, row_ok);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
       epilogue_tile<EPI, OutT>(tbase, crow, row_ok, col0, N);
@@ -520,6 +501,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (row_ptrs) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();

@@ -16,9 +16,13 @@ from the reference:
   and the weights are applied by the sender's combine;
 * ONE device-to-host copy of the count matrix per forward (the reference makes four:
   ``.item()``, two ``.tolist()`` and the per-expert ``.cpu()`` at :130,136-137,231);
-* the batch travels in token chunks on a communication stream: the dispatch
-  all-to-all of chunk c+1 and the return all-to-all of chunk c-1 run while the expert
-  GEMMs of chunk c run on the compute stream;
+* on CUDA devices rows move by device-to-device copies into the peers' buffers (copy
+  engines over NVLink, CUDA IPC), and the GEMMs of the rows a rank routes to its own
+  experts run while the other ranks' rows are in flight ("local first"); the
+  alternative schedules send the batch in token chunks on a communication stream, the
+  dispatch of chunk c+1 and the return of chunk c-1 running while the expert GEMMs of
+  chunk c run on the compute stream (``schedule="chunked"``, and the collective
+  transport);
 * the capacity cut (extension) happens on the receiver in (source rank, token, slot)
   order over the whole batch, and dropped rows travel back as zeros so the sender's
   combine needs no mask.
@@ -67,10 +71,17 @@ def capacity_positions(recv_counts: np.ndarray, capacity: int):
     return (src_start[None] + chunk_start).astype(np.int32)
 
 
+def kept_rows(rows_per_expert: np.ndarray, capacity: int) -> int:
+    """Rows an expert computes after the capacity cut (all of them without a capacity)."""
+    r = np.asarray(rows_per_expert, dtype=np.int64)
+    return int(np.minimum(r, capacity).sum() if capacity > 0 else r.sum())
+
+
 class ExpertParallelExchange:
     def __init__(self, num_experts: int, world_size: int, rank: int, d_model: int,
                  group: Optional[dist.ProcessGroup] = None, kernels=None, chunks: int = 4,
-                 min_chunk_tokens: int = 2048, transport: str = "auto"):
+                 min_chunk_tokens: int = 2048, transport: str = "auto", schedule: str = "local_first",
+                 runtime=None):
         if num_experts % world_size:
             raise ValueError("num_experts must be divisible by the world size")
         self.num_experts = num_experts
@@ -92,7 +103,16 @@ class ExpertParallelExchange:
             raise ValueError("transport must be 'auto', 'p2p' or 'collective'")
         self.transport = transport
         self._bufs = None           # (receive, return) PeerBuffers of the p2p transport
-        self._cstreams = {}         # per-device copy streams, one per peer
+        if schedule not in ("local_first", "chunked"):
+            raise ValueError("schedule must be 'local_first' or 'chunked'")
+        self.schedule = schedule    # p2p transport: local-first or chunk-by-chunk overlap
+        # local-first return of the other ranks' rows: "fused" = the expert GEMM stores
+        # them into the source ranks' buffers; "copy" = gather + device-to-device copies
+        self.return_mode = "fused"
+        if runtime is None:
+            from .p2p import CudaRuntime
+            runtime = CudaRuntime()
+        self.rt = runtime           # streams, events, peer buffers and copies (p2p transport)
         self._flag = None
 
     # ------------------------------------------------------------------ helpers
@@ -134,8 +154,8 @@ class ExpertParallelExchange:
         CUDA tensors use the peer-copy transport (``_forward_p2p``) unless
         ``transport="collective"``; CPU tensors (gloo) use all_to_all_single."""
         use_p2p = self.transport == "p2p" or (self.transport == "auto" and x.is_cuda)
-        if use_p2p and capacity <= 0:
-            return self._forward_p2p_local_first(x, idx, w, experts, shared, timer)
+        if use_p2p and self.schedule == "local_first":
+            return self._forward_p2p_local_first(x, idx, w, capacity, experts, shared, timer)
         if use_p2p:
             return self._forward_p2p(x, idx, w, capacity, experts, shared, timer)
         return self._forward_collective(x, idx, w, capacity, experts, shared, timer)
@@ -197,7 +217,6 @@ class ExpertParallelExchange:
                 ev_sent.append(_record(comm))
         # expert compute per chunk as its rows arrive (compute stream)
         backs, states, ev_back = [], [], []
-        rows_total = 0
         for c in range(C):
             mark(f"wait_sent{c}_before")
             _wait(comp, ev_sent[c])
@@ -209,11 +228,10 @@ class ExpertParallelExchange:
             mark(f"experts{c}_start")
             y = experts(xe, rg["offsets"])
             mark(f"experts{c}_end")
-            rows_total += rg["rows_cap"]
             backs.append(self.k.gather_rows(y, rg["recv_dst"], n_recv))
             ev_back.append(_record(comp))
             states.append((rg, n_recv))
-        self.last_rows = rows_total
+        self.last_rows = kept_rows(hr.sum((0, 1)), capacity)
         # return all-to-alls (communication stream) and combine (compute stream)
         ev_ret = []
         for c in range(C):
@@ -234,20 +252,27 @@ class ExpertParallelExchange:
 
 
     # ------------------------------------------------------------------ peer copies
-    def _barrier(self, stream):
+    def _barrier(self, stream, dev):
         """Orders this rank's copies issued on `stream` before every rank's next work on
         its own `stream`: a one-int all-reduce, which on each rank starts only after that
         rank's earlier copies completed."""
-        if self._flag is None or self._flag.device != stream.device:
-            self._flag = torch.zeros(1, dtype=torch.int32, device=stream.device)
-        with torch.cuda.stream(stream):
+        if self._flag is None or self._flag.device != dev:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        with self.rt.on(stream):
             dist.all_reduce(self._flag, group=self.group)
 
+    def _peer_buffers(self, dev):
+        if self._bufs is None:
+            self._bufs = (self.rt.buffers(self.group, self.rank, self.world_size, dev),
+                          self.rt.buffers(self.group, self.rank, self.world_size, dev))
+        return self._bufs
+
     def _forward_p2p(self, x, idx, w, capacity, experts, shared=None, timer=None):
-        """Rows travel by device-to-device copies into the peers' receive / return buffers
-        (copy engines over NVLink), chunk by chunk on the communication stream, while the
-        compute stream runs the expert GEMMs of the chunks that have arrived."""
-        from .p2p import PeerBuffers, copy_segments, view
+        """Chunked schedule: rows travel by device-to-device copies into the peers'
+        receive / return buffers (copy engines over NVLink), chunk by chunk on the
+        communication stream, while the compute stream runs the expert GEMMs of the
+        chunks that have arrived."""
+        rt = self.rt
         ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
         T, k = idx.shape
         d = x.shape[1]
@@ -255,11 +280,8 @@ class ExpertParallelExchange:
         rb = d * x.element_size()
         bounds = chunk_bounds(T, self.n_chunks(T))
         C = len(bounds)
-        comp = torch.cuda.current_stream(dev)
-        comm = self._stream(dev)
-        if self._bufs is None:
-            self._bufs = (PeerBuffers(self.group, me, ws, dev), PeerBuffers(self.group, me, ws, dev))
-        recv_buf, ret_buf = self._bufs
+        comp, comm = rt.compute(dev), rt.comm(dev)
+        recv_buf, ret_buf = self._peer_buffers(dev)
 
         def mark(name):
             if timer is not None:
@@ -294,21 +316,21 @@ class ExpertParallelExchange:
             pos = capacity_positions(np.ascontiguousarray(Gh[:, :, me, :].transpose(1, 0, 2)), capacity)
             pos_dev = torch.from_numpy(pos).to(dev, non_blocking=True)
 
-        comm.wait_stream(comp)
+        rt.join(comm, comp)
         ev_sent = []
         for c in range(C):
-            sends[c].record_stream(comm)
+            rt.keep(sends[c], comm)
             base = sends[c].data_ptr()
-            copy_segments([(recv_buf.ptrs[r] + int(RO[c, r] + SO[me, c, r]) * rb, base + int(SD[me, c, r]) * rb,
-                            int(R[me, c, r]) * rb) for r in range(ws)], comm)
-            self._barrier(comm)
-            ev_sent.append(_record(comm))
-        recv_local = view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
-        ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
-        backs, ev_back, rows_total = [], [], 0
+            rt.copy([(recv_buf.ptrs[r] + int(RO[c, r] + SO[me, c, r]) * rb, base + int(SD[me, c, r]) * rb,
+                      int(R[me, c, r]) * rb) for r in range(ws)], comm)
+            self._barrier(comm, dev)
+            ev_sent.append(rt.record(comm))
+        recv_local = rt.view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
+        ret_local = rt.view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
+        backs, ev_back = [], []
         for c in range(C):
             mark(f"wait_sent{c}_before")
-            _wait(comp, ev_sent[c])
+            rt.wait(comp, ev_sent[c])
             mark(f"wait_sent{c}_after")
             n_recv = int(recv_c[c, me])
             rows = recv_local[int(RO[c, me]):int(RO[c, me]) + n_recv]
@@ -318,71 +340,72 @@ class ExpertParallelExchange:
             mark(f"experts{c}_start")
             y = experts(xe, rg["offsets"])
             mark(f"experts{c}_end")
-            rows_total += rg["rows_cap"]
             backs.append(self.k.gather_rows(y, rg["recv_dst"], n_recv))
-            ev_back.append(_record(comp))
-        self.last_rows = rows_total
+            ev_back.append(rt.record(comp))
+        self.last_rows = kept_rows(Gh[:, :, me, :].sum((0, 1)), capacity)
         ev_ret = []
         for c in range(C):
-            _wait(comm, ev_back[c])
-            backs[c].record_stream(comm)
+            rt.wait(comm, ev_back[c])
+            rt.keep(backs[c], comm)
             base = backs[c].data_ptr()
-            copy_segments([(ret_buf.ptrs[s] + int(SRO[s, c] + SD[s, c, me]) * rb, base + int(SO[s, c, me]) * rb,
-                            int(R[s, c, me]) * rb) for s in range(ws)], comm)
-            self._barrier(comm)
-            ev_ret.append(_record(comm))
+            rt.copy([(ret_buf.ptrs[s] + int(SRO[s, c] + SD[s, c, me]) * rb, base + int(SO[s, c, me]) * rb,
+                      int(R[s, c, me]) * rb) for s in range(ws)], comm)
+            self._barrier(comm, dev)
+            ev_ret.append(rt.record(comm))
         out = torch.empty_like(x)
         mark("combine_start")
         for c, (a, b) in enumerate(bounds):
             mark(f"wait_ret{c}_before")
-            _wait(comp, ev_ret[c])
+            rt.wait(comp, ev_ret[c])
             mark(f"wait_ret{c}_after")
             ret = ret_local[int(SRO[me, c]):int(SRO[me, c] + send_c[me, c])]
             self.k.combine(ret, plans[c]["slot_row"], w[a:b], b - a, k,
                            shared=None if shared is None else shared[a:b], out=out[a:b])
         return out
 
-    def _copy_streams(self, dev, n: int):
-        lst = self._cstreams.get(dev.index)
-        if lst is None or len(lst) < n:
-            lst = self._cstreams[dev.index] = [torch.cuda.Stream(dev) for _ in range(max(n, 1))]
-        return lst[:n]
-
-    def _fan_out(self, segs, base: torch.cuda.Stream, keep: torch.Tensor):
+    def _fan_out(self, segs, base, keep: torch.Tensor, dev):
         """Issue one copy per destination, each on its own stream so several copy engines
         work at once; `base` waits for all of them.  `keep` is the source tensor."""
-        from .p2p import copy_segments
+        rt = self.rt
         segs = [sg for sg in segs if sg[2] > 0]
-        streams = self._copy_streams(base.device, len(segs))
-        start = _record(base)
+        streams = rt.copy_streams(dev, len(segs))
+        start = rt.record(base)
         done = []
         for sg, st in zip(segs, streams):
-            st.wait_event(start)
-            keep.record_stream(st)
-            copy_segments([sg], st)
-            done.append(_record(st))
+            rt.wait(st, start)
+            rt.keep(keep, st)
+            rt.copy([sg], st)
+            done.append(rt.record(st))
         for e in done:
-            base.wait_event(e)
+            rt.wait(base, e)
 
-    def _forward_p2p_local_first(self, x, idx, w, experts, shared=None, timer=None):
-        """Peer-copy exchange without a capacity limit.  The rows this rank routes to its
-        OWN experts are contiguous in its send buffer and need no exchange.  They are
-        computed before the host waits for the count matrix, so the count exchange, the
-        host's bookkeeping and the copies of every other rank's rows over NVLink (one copy
-        stream per peer) run underneath them.  From 4 ranks on, only the first half of
-        each local expert's rows goes first and the second half is computed after the
-        other ranks' rows, underneath the copies that return their outputs."""
-        from .p2p import PeerBuffers, copy_segments, view
+    def _forward_p2p_local_first(self, x, idx, w, capacity, experts, shared=None, timer=None):
+        """Local-first schedule.  The rows this rank routes to its OWN experts are
+        contiguous in its send buffer and need no exchange.  They are computed before the
+        host waits for the count matrix, so the count exchange, the host's bookkeeping and
+        the copies of every other rank's rows over NVLink (one copy stream per peer) run
+        underneath them.  From 4 ranks on, only the first half of each local expert's
+        rows goes first and the second half is computed after the other ranks' rows,
+        straight into the return buffer, while the other ranks finish their returns.
+
+        The outputs of the other ranks' rows go back without a separate pass: the expert
+        GEMM's epilogue stores each row at its address in the source rank's return
+        buffer (``return_mode="fused"``; addresses from ``ep_return_rows``), so the
+        return traffic crosses NVLink tile by tile while the GEMM runs.
+        ``return_mode="copy"`` gathers them and copies them back with the copy engines.
+
+        With a capacity, a rank's own rows for expert e follow the rows of every lower
+        rank in e's (source rank, token, slot) order, so how many of them are kept is
+        known only from the count matrix: the first half is computed speculatively, and
+        rows past the cut travel back as zeros like the dropped rows of other ranks."""
+        rt = self.rt
         ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
         T, k = idx.shape
         d = x.shape[1]
         dev = x.device
         rb = d * x.element_size()
-        comp = torch.cuda.current_stream(dev)
-        comm = self._stream(dev)
-        if self._bufs is None:
-            self._bufs = (PeerBuffers(self.group, me, ws, dev), PeerBuffers(self.group, me, ws, dev))
-        recv_buf, ret_buf = self._bufs
+        comp, comm = rt.compute(dev), rt.comm(dev)
+        recv_buf, ret_buf = self._peer_buffers(dev)
 
         def mark(name):
             if timer is not None:
@@ -394,13 +417,13 @@ class ExpertParallelExchange:
         # for these alone, not for the expert work queued on the compute stream below
         G = torch.empty((ws, E), dtype=torch.int32, device=dev)
         if self._host is None or self._host.numel() < ws * E:
-            self._host = torch.empty(ws * E, dtype=torch.int32, pin_memory=True)
+            self._host = rt.host_buffer(ws * E, torch.int32)
         mark("counts_start")
-        comm.wait_stream(comp)
-        with torch.cuda.stream(comm):
+        rt.join(comm, comp)
+        with rt.on(comm):
             dist.all_gather_into_tensor(G.view(-1), plan["counts"], group=self.group)
             self._host[:ws * E].copy_(G.view(-1), non_blocking=True)
-            ev_counts = _record(comm)
+            ev_counts = rt.record(comm)
         mark("counts_done")
         offs = plan["offsets"][me * El:(me + 1) * El + 1]
         starts, fins = offs[:-1], offs[1:]
@@ -412,7 +435,8 @@ class ExpertParallelExchange:
         mark("experts_selfA_start")
         y_a = experts(send, starts, ends=mids)
         mark("experts_selfA_end")
-        ev_counts.synchronize()
+        ev_a = rt.record(comp)
+        rt.host_wait(ev_counts)
         Gh = self._host[:ws * E].numpy().reshape(ws, ws, El).astype(np.int64)   # [src, dst, El]
         R = Gh.sum(2)                                  # rows src -> dst
         Rr = R.copy()
@@ -427,50 +451,74 @@ class ExpertParallelExchange:
         sbase = send.data_ptr()
         self._fan_out([(recv_buf.ptrs[r], 0, 0) if r == me else
                        (recv_buf.ptrs[r] + int(SO[me, r]) * rb, sbase + int(SD[me, r]) * rb, int(R[me, r]) * rb)
-                       for r in range(ws)], comm, send)
-        self._barrier(comm)
-        ev_sent = _record(comm)
-        # this rank's own rows: expert outputs are copied into the return buffer, whose
-        # layout is the send layout (the same row numbers as in `send`)
-        ret_local = view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
+                       for r in range(ws)], comm, send, dev)
+        self._barrier(comm, dev)
+        ev_sent = rt.record(comm)
+        # this rank's own rows of the first pass are copied (communication stream, once
+        # the GEMMs are done) into the return buffer, whose layout is the send layout
+        # (the same row numbers as in `send`); rows past the capacity cut become zeros
+        ret_local = rt.view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
         own = Gh[me, me, :]                                       # rows per local expert
+        keep = np.clip(capacity - Gh[:me, me, :].sum(0), 0, own) if capacity > 0 else own
         a_e = int(SD[me, me]) + np.concatenate([[0], np.cumsum(own)[:-1]])
-        m_e = a_e + (own // 2 if split else own)
+        h_e = own // 2 if split else own                          # rows of the first pass
         rbase = ret_local.data_ptr()
-        copy_segments([(rbase + int(a) * rb, y_a.data_ptr() + int(a) * rb, int(m - a) * rb)
-                       for a, m in zip(a_e, m_e)], comp)
+        rt.wait(comm, ev_a)
+        rt.keep(y_a, comm)
+        rt.copy([(rbase + int(a) * rb, y_a.data_ptr() + int(a) * rb, int(min(h, kp)) * rb)
+                 for a, h, kp in zip(a_e, h_e, keep)], comm)
+        with rt.on(comm):
+            for a, kp, o in zip(a_e, keep, own):
+                if kp < o:
+                    ret_local[int(a + kp):int(a + o)].zero_()
         # rows from the other ranks
         mark("wait_sent0_before")
-        _wait(comp, ev_sent)
+        rt.wait(comp, ev_sent)
         mark("wait_sent0_after")
         n_recv = int(recv_tot[me])
         rc = G[:, me * El:(me + 1) * El].clone()
+        pos = torch.cumsum(rc, 0, dtype=torch.int32) - rc if capacity > 0 else None
         rc[me].zero_()
-        recv_local = view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
-        rg = self.k.ep_regroup_plan(rc, 0, n_recv)
+        recv_local = rt.view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
+        rg = self.k.ep_regroup_plan(rc, capacity, n_recv, pos_base=pos)
         xe = self.k.permute_rows(recv_local[:n_recv], rg["row_src"], rg["offsets"], rg["rows_cap"])
-        mark("experts0_start")
-        y = experts(xe, rg["offsets"])
-        mark("experts0_end")
-        self.last_rows = int(R[me, me]) + rg["rows_cap"]
-        back = self.k.gather_rows(y, rg["recv_dst"], n_recv)
-        comm.wait_stream(comp)
-        bbase = back.data_ptr()
-        self._fan_out([(0, 0, 0) if s_ == me else
-                       (ret_buf.ptrs[s_] + int(SD[s_, me]) * rb, bbase + int(SO[s_, me]) * rb, int(R[s_, me]) * rb)
-                       for s_ in range(ws)], comm, back)
-        self._barrier(comm)
-        ev_ret = _record(comm)
-        if split:  # second half of the own rows, underneath the return copies
+        self.last_rows = kept_rows(Gh[:, me, :].sum(0), capacity)
+        if self.return_mode == "fused" and rb % 16 == 0:
+            # the expert GEMM's epilogue stores every output row straight into its source
+            # rank's return buffer (peer memory over NVLink) while the GEMM runs
+            seg = np.zeros(2 * ws + 1, np.int64)
+            seg[:ws] = SO[:, me]
+            seg[ws] = n_recv
+            seg[ws + 1:] = [0 if s_ == me else ret_buf.ptrs[s_] + int(SD[s_, me]) * rb for s_ in range(ws)]
+            seg_dev = torch.from_numpy(seg).to(dev, non_blocking=True)
+            row_ptrs = self.k.ep_return_rows(rg["row_src"], rg["offsets"], rg["recv_dst"], n_recv, seg_dev, rb,
+                                             rg["rows_cap"])
+            mark("experts0_start")
+            experts(xe, rg["offsets"], row_ptrs=row_ptrs)
+            mark("experts0_end")
+            rt.join(comm, comp)
+        else:
+            mark("experts0_start")
+            y = experts(xe, rg["offsets"])
+            mark("experts0_end")
+            back = self.k.gather_rows(y, rg["recv_dst"], n_recv)
+            rt.join(comm, comp)
+            bbase = back.data_ptr()
+            self._fan_out([(0, 0, 0) if s_ == me else
+                           (ret_buf.ptrs[s_] + int(SD[s_, me]) * rb, bbase + int(SO[s_, me]) * rb, int(R[s_, me]) * rb)
+                           for s_ in range(ws)], comm, back, dev)
+        self._barrier(comm, dev)
+        ev_ret = rt.record(comm)
+        if split:  # second half of the kept own rows, straight into the return buffer
+            ends_b = fins
+            if capacity > 0:
+                ends_b = torch.maximum(mids, torch.minimum(fins, starts + torch.clamp(capacity - pos[me], min=0)))
             mark("experts_selfB_start")
-            y_b = experts(send, mids, ends=fins)
+            experts(send, mids, ends=ends_b, out=ret_local)
             mark("experts_selfB_end")
-            f_e = a_e + own
-            copy_segments([(rbase + int(m) * rb, y_b.data_ptr() + int(m) * rb, int(f - m) * rb)
-                           for m, f in zip(m_e, f_e)], comp)
         mark("combine_start")
         mark("wait_ret0_before")
-        _wait(comp, ev_ret)
+        rt.wait(comp, ev_ret)
         mark("wait_ret0_after")
         return self.k.combine(ret_local[:int(send_tot[me])], plan["slot_row"], w, T, k, shared=shared)
 

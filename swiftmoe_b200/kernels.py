@@ -112,15 +112,26 @@ def combine(y: torch.Tensor, slot_row: torch.Tensor, w: torch.Tensor, T: int, k:
 
 def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, *, B3: Optional[torch.Tensor] = None,
                  epilogue: int = L.SMOE_EPI_STORE, out_dtype: Optional[torch.dtype] = None,
-                 out: Optional[torch.Tensor] = None, ends: Optional[torch.Tensor] = None):
+                 out: Optional[torch.Tensor] = None, ends: Optional[torch.Tensor] = None,
+                 row_ptrs: Optional[torch.Tensor] = None):
     """C[rows_cap, N] for groups of rows [offsets[g], offsets[g+1]) -- or [offsets[g],
-    ends[g]) when ``ends`` is given -- of A; B is [G, N, K]."""
-    _need_cuda(A, B, B3, offsets, ends)
+    ends[g]) when ``ends`` is given -- of A; B is [G, N, K].
+
+    ``row_ptrs`` (int64 [rows_cap] device addresses, see ``ep_return_rows``): output row
+    r is stored at row_ptrs[r] instead (possibly another GPU's memory); returns None."""
+    _need_cuda(A, B, B3, offsets, ends, row_ptrs)
     rows_cap, K = A.shape
     G, N, K2 = B.shape
     if K2 != K:
         raise L.SwiftMoEError("K mismatch")
     od = out_dtype or A.dtype
+    if row_ptrs is not None:
+        if row_ptrs.dtype != torch.int64 or row_ptrs.numel() < rows_cap:
+            raise L.SwiftMoEError("row_ptrs must be int64 with one address per row of A")
+        L.check(L.load().smoe_grouped_gemm_rows(L.ptr(A), L.ptr(B), L.ptr(B3), L.ptr(row_ptrs), L.dtype_code(A.dtype),
+                                                L.dtype_code(od), epilogue, L.ptr(offsets), L.ptr(ends), G, rows_cap,
+                                                N, K, L.stream_handle(A.device)), "smoe_grouped_gemm_rows")
+        return None
     if out is None:
         out = torch.empty((max(rows_cap, 1), N), dtype=od, device=A.device)
     L.check(L.load().smoe_grouped_gemm(L.ptr(A), L.ptr(B), L.ptr(B3), L.ptr(out), L.dtype_code(A.dtype),
@@ -160,6 +171,22 @@ def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int, pos_b
                                      L.ptr(row_src), L.ptr(recv_dst), L.ptr(wsb), wsb.numel(), L.stream_handle(dev)),
             "smoe_ep_regroup_plan")
     return dict(counts=counts, offsets=offsets, row_src=row_src, recv_dst=recv_dst, rows_cap=rows_cap)
+
+
+def ep_return_rows(row_src: torch.Tensor, offsets: torch.Tensor, recv_dst: torch.Tensor, n_recv: int,
+                   seg_table: torch.Tensor, row_bytes: int, rows_cap: int) -> torch.Tensor:
+    """Return address of every expert row (int64 [rows_cap]) for ``grouped_gemm(row_ptrs=)``;
+    zero rows at the return addresses of dropped received rows.  seg_table: int64
+    [2 * n_src + 1] device tensor: source segment starts (n_src + 1, last = n_recv), then
+    the address of each source's return region."""
+    _need_cuda(row_src, offsets, recv_dst, seg_table)
+    El = offsets.numel() - 1
+    n_src = (seg_table.numel() - 1) // 2
+    row_ptrs = torch.empty(max(rows_cap, 1), dtype=torch.int64, device=row_src.device)
+    L.check(L.load().smoe_ep_return_rows(L.ptr(row_src), L.ptr(offsets), El, L.ptr(recv_dst), n_recv,
+                                         L.ptr(seg_table), n_src, row_bytes, L.ptr(row_ptrs), rows_cap,
+                                         L.stream_handle(row_src.device)), "smoe_ep_return_rows")
+    return row_ptrs
 
 
 def read_device_error(device) -> int:

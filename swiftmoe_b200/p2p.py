@@ -91,3 +91,71 @@ def copy_segments(segs, stream: torch.cuda.Stream) -> None:
     src = (C.c_void_p * n)(*[s[1] for s in segs])
     nb = (C.c_size_t * n)(*[s[2] for s in segs])
     L.check(L.load().smoe_copy_segments(dst, src, nb, n, stream.cuda_stream), "smoe_copy_segments")
+
+
+class CudaRuntime:
+    """Streams, events, peer buffers and copies of the peer-copy transport on CUDA
+    devices.  The exchange schedules in ep.py only talk to the device through this
+    object, so a host implementation of the same methods can run them on CPU ranks."""
+
+    def __init__(self):
+        self._comm = {}
+        self._copy = {}
+
+    @staticmethod
+    def compute(dev):
+        return torch.cuda.current_stream(dev)
+
+    def comm(self, dev):
+        s = self._comm.get(dev.index)
+        if s is None:
+            s = self._comm[dev.index] = torch.cuda.Stream(dev)
+        return s
+
+    def copy_streams(self, dev, n: int):
+        lst = self._copy.get(dev.index)
+        if lst is None or len(lst) < n:
+            lst = self._copy[dev.index] = [torch.cuda.Stream(dev) for _ in range(max(n, 1))]
+        return lst[:n]
+
+    @staticmethod
+    def on(s):
+        return torch.cuda.stream(s)
+
+    @staticmethod
+    def record(s):
+        e = torch.cuda.Event()
+        e.record(s)
+        return e
+
+    @staticmethod
+    def wait(s, ev):
+        s.wait_event(ev)
+
+    @staticmethod
+    def join(s, other):
+        s.wait_stream(other)
+
+    @staticmethod
+    def host_wait(ev):
+        ev.synchronize()
+
+    @staticmethod
+    def keep(t: torch.Tensor, s):
+        t.record_stream(s)
+
+    @staticmethod
+    def host_buffer(n: int, dtype: torch.dtype) -> torch.Tensor:
+        return torch.empty(n, dtype=dtype, pin_memory=True)
+
+    @staticmethod
+    def buffers(group, rank: int, world_size: int, dev: torch.device) -> PeerBuffers:
+        return PeerBuffers(group, rank, world_size, dev)
+
+    @staticmethod
+    def view(ptr: int, shape, dtype: torch.dtype, dev: torch.device) -> torch.Tensor:
+        return view(ptr, shape, dtype, dev)
+
+    @staticmethod
+    def copy(segs, s) -> None:
+        copy_segments(segs, s)

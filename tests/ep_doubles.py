@@ -1,6 +1,8 @@
 """CPU test double of the swiftmoe_b200.kernels operations used by the expert-parallel
 exchange, so that its collective choreography runs on gloo ranks without a GPU.
 Each function follows the contract of the C-ABI entry point of the same name."""
+import ctypes
+
 import numpy as np
 import torch
 
@@ -84,3 +86,26 @@ def combine(y, slot_row, w, T, k, shared=None, out=None):
         out.copy_(res)
         return out
     return res
+
+
+def ep_return_rows(row_src, offsets, recv_dst, n_recv, seg_table, row_bytes, rows_cap):
+    seg = seg_table.numpy().astype(np.int64)
+    nsrc = (seg.size - 1) // 2
+    starts, base = seg[:nsrc + 1], seg[nsrc + 1:]
+
+    def addr(r):
+        s = int(np.searchsorted(starts[:nsrc], r, side="right")) - 1
+        return int(base[s]) + (r - int(starts[s])) * row_bytes
+
+    kept = int(offsets.numpy()[-1])
+    rs = row_src.numpy()
+    ptrs = np.zeros(max(rows_cap, 1), np.int64)
+    for i in range(min(kept, rows_cap)):
+        r = int(rs[i])
+        if 0 <= r < n_recv:
+            ptrs[i] = addr(r)
+    rd = recv_dst.numpy()
+    for r in range(n_recv):
+        if rd[r] < 0:
+            ctypes.memset(addr(r), 0, row_bytes)
+    return torch.from_numpy(ptrs)

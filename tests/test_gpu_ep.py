@@ -46,7 +46,9 @@ def _worker(rank, ws, port, cfg, transport, out_dir):
     m = S.UltimateMoE(E, d, use_fp16=False, dtype=dt, top_k=k, expert_type="swiglu", d_ff=F,
                       capacity_factor=cf, num_shared_experts=1 if shared else 0, d_ff_shared=F,
                       use_nccl_opt=False, device=dev)
-    m.comm.transport = transport
+    tr, _, sched = transport.partition("-")
+    tr, _, ret = tr.partition("+")
+    m.comm.transport, m.comm.schedule, m.comm.return_mode = tr, sched or "local_first", ret or "fused"
     m.comm.min_chunk_tokens = 64          # several chunks even at these small sizes
     El = E // ws
     sl = slice(rank * El, (rank + 1) * El)
@@ -90,7 +92,7 @@ CASES = [(300, 256, 8, 2, 512, None, False), (257, 256, 16, 2, 256, 1.0, False),
          (200, 128, 32, 8, 128, None, True)]
 
 
-@pytest.mark.parametrize("transport", ["p2p", "collective"])
+@pytest.mark.parametrize("transport", ["p2p", "p2p+copy", "p2p-chunked", "collective"])
 @pytest.mark.parametrize("cfg", CASES)
 def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
     n = torch.cuda.device_count()

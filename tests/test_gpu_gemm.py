@@ -127,3 +127,45 @@ def test_grouped_row_ranges(K, dtype):
     assert (got[~inside] == 7.0).all()
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     assert max_abs_err(got[inside].numpy(), ref[inside].numpy()) <= tol * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("cap", [0, 40])
+def test_grouped_gemm_row_addresses(K, dtype, cap):
+    """The fused expert-parallel return on one GPU: ep_return_rows turns a receive layout
+    (3 source segments x 3 local experts) into one address per expert row, inside a
+    buffer where the source regions lie in reverse order; the GEMM with row addresses
+    must store exactly the rows of the plain GEMM there, bit for bit, and the rows the
+    capacity dropped must become zeros.  Rows outside every region keep their sentinel."""
+    ws, El, Kd, N = 3, 3, 256, 192
+    rc = torch.tensor([[30, 0, 55], [17, 41, 9], [0, 23, 61]], dtype=torch.int32)
+    n_recv = int(rc.sum())
+    g = torch.Generator().manual_seed(5)
+    xr = torch.randn((n_recv, Kd), generator=g).to(dtype).cuda()
+    B = (torch.randn((El, N, Kd), generator=g) * 0.05).to(dtype).cuda()
+    rg = K.ep_regroup_plan(rc.cuda(), cap, n_recv)
+    xe = K.permute_rows(xr, rg["row_src"], rg["offsets"], rg["rows_cap"])
+    y = K.grouped_gemm(xe, B, rg["offsets"])
+    per_src = rc.sum(1).tolist()
+    starts = np.concatenate([[0], np.cumsum(per_src)]).astype(np.int64)
+    pad = 5                                           # rows between regions, never written
+    region, at = {}, pad                              # first row of each source region
+    for s in reversed(range(ws)):
+        region[s] = at
+        at += per_src[s] + pad
+    buf = torch.full((at, N), 7.0, dtype=dtype, device="cuda")
+    rb = N * buf.element_size()
+    seg = np.concatenate([starts, [buf.data_ptr() + int(region[s]) * rb for s in range(ws)]]).astype(np.int64)
+    row_ptrs = K.ep_return_rows(rg["row_src"], rg["offsets"], rg["recv_dst"], n_recv,
+                                torch.from_numpy(seg).cuda(), rb, rg["rows_cap"])
+    assert K.grouped_gemm(xe, B, rg["offsets"], row_ptrs=row_ptrs) is None
+    got, yc, rd = buf.cpu(), y.cpu(), rg["recv_dst"].cpu().tolist()
+    written = torch.zeros(at, dtype=torch.bool)
+    for s in range(ws):
+        for r in range(int(starts[s]), int(starts[s + 1])):
+            row = int(region[s]) + r - int(starts[s])
+            written[row] = True
+            want = yc[rd[r]] if rd[r] >= 0 else torch.zeros(N, dtype=dtype)
+            assert torch.equal(got[row], want), (s, r)
+    assert (got[~written] == 7.0).all()
+    assert K.read_device_error("cuda") == 0
