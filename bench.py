@@ -228,6 +228,35 @@ def run_reference_arm(args):
 
 
 # --------------------------------------------------------------------- GPU arm
+def _cpulist(text: str):
+    cpus = set()
+    for part in text.strip().split(","):
+        if part:
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+    return cpus
+
+
+def bind_near_gpu(index: int):
+    """Run this process on the host CPUs of the GPU's NUMA node (PCI local_cpulist), so
+    the pinned host buffers of the end-to-end leg are allocated in that node's memory.
+    Returns (the CPUs bound, the previous mask), or None if the topology is unknown."""
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(index)
+        path = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/local_cpulist"
+        with open(path) as f:
+            local = _cpulist(f.read())
+        before = os.sched_getaffinity(0)
+        sel = local & before
+        if not sel or sel == before:
+            return None
+        os.sched_setaffinity(0, sel)
+        return sel, before
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def count_launches(fn):
     """Kernels of libswiftmoe (namespace smoe) launched by fn(), from a CUPTI trace."""
     import torch
@@ -258,6 +287,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    binding = bind_near_gpu(local)
     if ws > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
@@ -333,10 +363,12 @@ def main():
             st["Combine_Comm"].append(e.elapsed(4, 5))
         stage_ms = {k: statistics.mean(v) for k, v in st.items()}
         exposed = 0.0
+        spans = None
     else:
         s = model.get_profile_summary()
         stage_ms = {k: v for k, v in s.items()}
         exposed = s.get("Exposed_A2A", 0.0)
+        spans = {k: round(v, 4) for k, v in model.get_profile_spans().items()}
     burst, sustained, hbm, src = peaks()
     # routed rows this rank computed (capacity drops included), from the plan / exchange
     if ws == 1:
@@ -435,6 +467,8 @@ def main():
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "mixtral":
         try:
+            if binding is not None:     # the CPU baseline uses every host thread again
+                os.sched_setaffinity(0, binding[1])
             cpu, _, _ = cpu_reference(args.cpu_seconds)
         except Exception as ex:  # reported, never fatal
             cpu = {"value": None, "error": repr(ex)}
@@ -446,6 +480,8 @@ def main():
                 "config": {"workload": WORKLOAD, "d_model": D_MODEL, "num_experts": N_EXPERTS, "top_k": TOP_K,
                            "d_ff": D_FF, "tokens_per_gpu": T, "parallelism": f"ep{ws}",
                            "capacity_factor": wl["cf"], "shared_experts": wl["shared"],
+                           "host_cpus": None if binding is None else
+                           f"{len(binding[0])} CPUs of the GPU's NUMA node (of {len(binding[1])})",
                            "ep_exchange": None if ws == 1 else
                            f"{model.comm.transport} transport, " + (
                                f"{model.comm.schedule} schedule, {model.comm.return_mode} return"
@@ -458,6 +494,7 @@ def main():
                 "gpu_launches_per_step": launches_per_step, "gpu_launches_source": launches_src,
                 "roofline": roofline,
                 "layer_tensor_frac": layer_frac, "stage_ms": stage_ms, "exposed_a2a_ms": exposed,
+                "rank0_timeline_ms": spans,
                 "cpu_baseline": cpu, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     clk.stop()

@@ -53,6 +53,7 @@ class _StageTimer:
         self.pending: List[tuple] = []
         self.data: Dict[str, List[float]] = {s: [] for s in STAGES}
         self.data["Exposed_A2A"] = []
+        self.spans: Dict[str, List[float]] = {}   # expert-parallel forward: mark -> next mark
 
     def mark(self, device) -> torch.cuda.Event:
         ev = torch.cuda.Event(enable_timing=True)
@@ -85,6 +86,8 @@ class _StageTimer:
                 exposed = span("counts_start", "counts_done") + sum(
                     span(n, n.replace("_before", "_after")) for n in names if n.endswith("_before"))
                 self.data["Exposed_A2A"].append(exposed)
+                for (a, ea), (b, eb) in zip(events[:-1], events[1:]):
+                    self.spans.setdefault(f"{a}>{b}", []).append(ea.elapsed_time(eb))
                 continue
             if kind == "lib":
                 spans = [(0, 1), (1, 2), (2, 4), (4, 5)]
@@ -288,11 +291,18 @@ class MoECore(nn.Module):
             out[k_] = float(sum(v) / len(v)) if v else 0.0
         return out
 
+    def get_profile_spans(self) -> Dict[str, float]:
+        """Expert-parallel forwards: mean milliseconds between consecutive stage marks on
+        the compute stream (keys "mark>next_mark"), in timeline order."""
+        self._timer.flush()
+        return {k_: float(sum(v) / len(v)) for k_, v in self._timer.spans.items() if v}
+
     def reset_profiling(self):
         """models/ultimate_moe.py:354-357."""
         self._timer.flush()
         for v in self._timer.data.values():
             v.clear()
+        self._timer.spans.clear()
 
     @property
     def profile_data(self):

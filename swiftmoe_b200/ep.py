@@ -97,6 +97,7 @@ class ExpertParallelExchange:
             kernels = _k
         self.k = kernels
         self._host = None
+        self._seg_host = None       # return-address table of the fused return (pinned)
         self._comm_stream = {}
         self.last_rows = 0          # expert rows computed by this rank in the last forward
         if transport not in ("auto", "p2p", "collective"):
@@ -486,11 +487,16 @@ class ExpertParallelExchange:
         if self.return_mode == "fused" and rb % 16 == 0:
             # the expert GEMM's epilogue stores every output row straight into its source
             # rank's return buffer (peer memory over NVLink) while the GEMM runs
-            seg = np.zeros(2 * ws + 1, np.int64)
+            # the pinned table is rewritten only after this step's count exchange, which
+            # follows every use of it by the previous step's compute stream
+            if self._seg_host is None or self._seg_host.numel() != 2 * ws + 1:
+                self._seg_host = rt.host_buffer(2 * ws + 1, torch.int64)
+            seg = self._seg_host.numpy()
             seg[:ws] = SO[:, me]
             seg[ws] = n_recv
             seg[ws + 1:] = [0 if s_ == me else ret_buf.ptrs[s_] + int(SD[s_, me]) * rb for s_ in range(ws)]
-            seg_dev = torch.from_numpy(seg).to(dev, non_blocking=True)
+            seg_dev = torch.empty(2 * ws + 1, dtype=torch.int64, device=dev)
+            seg_dev.copy_(self._seg_host, non_blocking=True)
             row_ptrs = self.k.ep_return_rows(rg["row_src"], rg["offsets"], rg["recv_dst"], n_recv, seg_dev, rb,
                                              rg["rows_cap"])
             mark("experts0_start")
