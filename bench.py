@@ -74,6 +74,8 @@ def parse():
                     help="overlap schedule of the p2p exchange")
     ap.add_argument("--ep-return", default=None, choices=["fused", "copy"],
                     help="local-first return: GEMM epilogue stores to the peers, or copies")
+    ap.add_argument("--ep-split-min-ws", type=int, default=None,
+                    help="local first: split the own rows in two halves from this world size on")
     return ap.parse_args()
 
 
@@ -315,6 +317,8 @@ def main():
             model.comm.schedule = args.ep_schedule
         if args.ep_return:
             model.comm.return_mode = args.ep_return
+        if args.ep_split_min_ws:
+            model.comm.split_min_ws = args.ep_split_min_ws
     x = torch.randn((T, D_MODEL), device=dev, dtype=cdtype, generator=torch.Generator(device=dev).manual_seed(100 + rank))
     out = torch.empty_like(x)
 

@@ -197,8 +197,10 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
  * array of 2 * n_src + 1 int64.  Writes row_ptrs[i] for the expert rows i < rows_cap
  * (0 past expert_offsets[E_l]) for smoe_grouped_gemm_rows, and writes zero rows at the
  * destinations of received rows the capacity dropped (recv_dst < 0), so the source's
- * combine adds nothing for those slots.  Replaces, with the GEMM above, the return
- * path of models/ultimate_moe.py:152,224-231.                                          */
+ * combine adds nothing for those slots.  row_src NULL: expert row i is received row i
+ * (the senders placed their rows in expert-major order; rows_cap <= n_recv); recv_dst
+ * NULL: nothing was dropped.  Replaces, with the GEMM above, the return path of
+ * models/ultimate_moe.py:152,224-231.                                                 */
 SMOE_API int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, int E_l,
                                  const int32_t* recv_dst, int64_t n_recv, const int64_t* seg_table, int n_src,
                                  int64_t row_bytes, uint64_t* row_ptrs, int64_t rows_cap, smoe_stream_t stream);

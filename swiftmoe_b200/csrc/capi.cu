@@ -148,8 +148,9 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
               cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
-  SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
-  kern<<<device_sms(), tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
+  constexpr int smem = EPI == tc::EPI_ROWS ? tc::SMEM_BYTES_ROWS : tc::SMEM_BYTES;
+  SMOE_CK(ensure_smem(kern, smem, &done));
+  kern<<<device_sms(), tc::THREADS, smem, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
                                                          K, (int)rows_cap, raster_band(EPI), idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
@@ -221,6 +222,14 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     if (!make_map_3d(&mb3, B3, dt, G, N, K)) return SMOE_ERR_CUDA;
   } else {
     mb3 = mb;
+  }
+  if (row_ptrs && epi == SMOE_EPI_STORE && out_dtype == dtype) {  // rows staged, 128-byte stores
+    const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
+    return dtype == SMOE_BF16
+               ? launch_tc<tc::EPI_ROWS, __nv_bfloat16>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K,
+                                                        idesc, st)
+               : launch_tc<tc::EPI_ROWS, __half>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, K, idesc,
+                                                 st);
   }
   if (use_pair_kernel(rows_cap, G)) {
     const uint32_t idesc2 = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::pair::BM, tc::BN);
@@ -610,10 +619,10 @@ int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, i
                         int64_t rows_cap, smoe_stream_t stream) {
   if (E_l < 1 || n_src < 1 || n_recv < 0 || rows_cap < 0 || row_bytes <= 0 || row_bytes % 16 != 0)
     return SMOE_ERR_INVALID;
-  if (!expert_offsets || !seg_table || (rows_cap > 0 && (!row_src || !row_ptrs)) || (n_recv > 0 && !recv_dst))
-    return SMOE_ERR_INVALID;
+  if (!expert_offsets || !seg_table || (rows_cap > 0 && !row_ptrs)) return SMOE_ERR_INVALID;
+  if (!row_src && rows_cap > n_recv) return SMOE_ERR_INVALID;
   if (rows_cap == 0 && n_recv == 0) return SMOE_OK;
-  const int64_t work = std::max<int64_t>(rows_cap, n_recv * 32);
+  const int64_t work = std::max<int64_t>(rows_cap, recv_dst ? n_recv * 32 : 0);
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)device_sms() * 8));
   ep_return_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(row_src, expert_offsets, E_l, recv_dst, n_recv,
                                                                 seg_table, n_src, row_bytes, row_ptrs, rows_cap);

@@ -392,6 +392,7 @@ __device__ __forceinline__ uint64_t ep_return_addr(int64_t r, const int64_t* __r
 
 // row_ptrs[i] for every expert row i < rows_cap (0 past the kept rows), and zero rows,
 // one warp per row, at the return addresses of received rows the capacity dropped.
+// row_src NULL: expert row i is received row i; recv_dst NULL: nothing was dropped.
 __global__ void __launch_bounds__(256) ep_return_rows_kernel(const int32_t* __restrict__ row_src,
                                                              const int32_t* __restrict__ offsets, int El,
                                                              const int32_t* __restrict__ recv_dst, int64_t n_recv,
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(256) ep_return_rows_kernel(const int32_t* __re
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = tid; i < rows_cap; i += nth) {
-    const int64_t r = i < kept ? row_src[i] : -1;
+    const int64_t r = i < kept ? (row_src != nullptr ? (int64_t)row_src[i] : i) : -1;
     uint64_t p = (r >= 0 && r < n_recv) ? ep_return_addr(r, seg, nsrc, row_bytes) : 0;
     if (p & 15) {
       set_device_error(kErrBadRowAddress);
@@ -410,6 +411,7 @@ __global__ void __launch_bounds__(256) ep_return_rows_kernel(const int32_t* __re
     }
     row_ptrs[i] = p;
   }
+  if (recv_dst == nullptr) return;  // nothing dropped
   const int lane = threadIdx.x & 31;
   bool wrote = false;
   for (int64_t r = tid >> 5; r < n_recv; r += nth >> 5) {

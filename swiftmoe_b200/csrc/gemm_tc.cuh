@@ -34,6 +34,12 @@ constexpr int MAX_GROUPS = 1024;
 constexpr int GM_DEFAULT = 16;  // m-tiles per rasterisation band unless the launch asks otherwise
 constexpr int NUM_BARS = 2 * STAGES + 5;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 * (MAX_GROUPS + 1) * 4;
+// Internal epilogue kind (not in the C ABI): store 16-bit rows at per-row addresses,
+// staged through shared memory so that every warp store writes 128 contiguous bytes
+// of 4 rows (expert-parallel return into other GPUs' buffers).
+constexpr int EPI_ROWS = 2;
+constexpr int ROWS_STAGE_BYTES = 32 * 128;  // per epilogue warp: 32 rows x 64 16-bit columns
+constexpr int SMEM_BYTES_ROWS = SMEM_BYTES + 16 + 4 * ROWS_STAGE_BYTES;
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 200 ms
 
 // Wait used while draining on the way out: ignores the error word, bounded by time.
@@ -135,6 +141,45 @@ __device__ __forceinline__ OutT* out_row(OutT* C, int64_t ldc, const uint64_t* r
   return reinterpret_cast<OutT*>(p);
 }
 
+// EPI_ROWS: drain this warp's 32 accumulator rows, 64 columns at a time.  Each thread
+// holds one row (tcgen05.ld 32x32b); the 128-byte row pieces go through a
+// 4 KB shared-memory stage (16-byte chunks XOR-swizzled by row, conflict-free both
+// ways) and leave as warp stores of 4 rows x 128 contiguous bytes.  row_addr: this
+// thread's row address (0 = skip the row); the other rows' addresses come by shuffle.
+template <typename OutT>
+__device__ __forceinline__ void epilogue_rows(uint32_t tbase, uint64_t row_addr, int col0, int N,
+                                              unsigned char* stage, int lane) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    uint32_t v0[32], v1[32];
+    tmem_ld32(tbase + c * 64, v0);
+    tmem_ld32(tbase + c * 64 + 32, v1);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* v = j < 4 ? v0 : v1;
+      const int b = (j & 3) * 8;
+      uint4 u;
+      u.x = pack2<OutT>(__uint_as_float(v[b + 0]), __uint_as_float(v[b + 1]));
+      u.y = pack2<OutT>(__uint_as_float(v[b + 2]), __uint_as_float(v[b + 3]));
+      u.z = pack2<OutT>(__uint_as_float(v[b + 4]), __uint_as_float(v[b + 5]));
+      u.w = pack2<OutT>(__uint_as_float(v[b + 6]), __uint_as_float(v[b + 7]));
+      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+    }
+    __syncwarp();
+    const int j = lane & 7;
+    const int col = col0 + c * 64 + j * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = i * 4 + (lane >> 3);
+      const uint64_t dst = __shfl_sync(0xffffffffu, row_addr, row);
+      const uint4 u = *reinterpret_cast<const uint4*>(stage + row * 128 + ((j ^ (row & 7)) << 4));
+      if (dst != 0 && col < N) *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(dst) + col) = u;
+    }
+    __syncwarp();
+  }
+}
+
 // Drain one 128-row accumulator (this warp's 32 TMEM lanes) into rows of C: SwiGLU on
 // the [gate | up] halves, or a plain store of all BN columns.
 template <int EPI, typename OutT>
@@ -193,6 +238,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   int* s_beg = reinterpret_cast<int*>(s_tmem + 4);
   int* s_fin = s_beg + (MAX_GROUPS + 1);
   int* s_ts = s_fin + (MAX_GROUPS + 1);
+  // EPI_ROWS only (its launches request SMEM_BYTES_ROWS): the epilogue warps' stages
+  unsigned char* s_stage =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_ts + MAX_GROUPS + 1) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -303,10 +351,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
       bool row_ok = r < t.rows_valid;
-      OutT* crow = out_row(C, ldc, row_ptrs, t.row0 + r, row_ok);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
-      epilogue_tile<EPI, OutT>(tbase, crow, row_ok, col0, N);
+      if constexpr (EPI == EPI_ROWS) {
+        const uint64_t addr = row_ok ? row_ptrs[t.row0 + r] : 0;
+        epilogue_rows<OutT>(tbase, addr, col0, N, s_stage + q * ROWS_STAGE_BYTES, lane);
+      } else {
+        OutT* crow = out_row(C, ldc, row_ptrs, t.row0 + r, row_ok);
+        epilogue_tile<EPI, OutT>(tbase, crow, row_ok, col0, N);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));

@@ -110,6 +110,8 @@ class ExpertParallelExchange:
         # local-first return of the other ranks' rows: "fused" = the expert GEMM stores
         # them into the source ranks' buffers; "copy" = gather + device-to-device copies
         self.return_mode = "fused"
+        # from this many ranks on, the own rows are computed in two halves (local first)
+        self.split_min_ws = 4
         if runtime is None:
             from .p2p import CudaRuntime
             runtime = CudaRuntime()
@@ -364,18 +366,20 @@ class ExpertParallelExchange:
                            shared=None if shared is None else shared[a:b], out=out[a:b])
         return out
 
-    def _fan_out(self, segs, base, keep: torch.Tensor, dev):
-        """Issue one copy per destination, each on its own stream so several copy engines
-        work at once; `base` waits for all of them.  `keep` is the source tensor."""
+    def _fan_out(self, groups, base, keep: torch.Tensor, dev):
+        """Issue each group of copies (a list of (dst, src, bytes)) on its own stream, so
+        several copy engines work at once -- one group per peer; `base` waits for all of
+        them.  `keep` is the source tensor."""
         rt = self.rt
-        segs = [sg for sg in segs if sg[2] > 0]
-        streams = rt.copy_streams(dev, len(segs))
+        groups = [[sg for sg in g if sg[2] > 0] for g in groups]
+        groups = [g for g in groups if g]
+        streams = rt.copy_streams(dev, len(groups))
         start = rt.record(base)
         done = []
-        for sg, st in zip(segs, streams):
+        for g, st in zip(groups, streams):
             rt.wait(st, start)
             rt.keep(keep, st)
-            rt.copy([sg], st)
+            rt.copy(g, st)
             done.append(rt.record(st))
         for e in done:
             rt.wait(base, e)
@@ -385,20 +389,26 @@ class ExpertParallelExchange:
         contiguous in its send buffer and need no exchange.  They are computed before the
         host waits for the count matrix, so the count exchange, the host's bookkeeping and
         the copies of every other rank's rows over NVLink (one copy stream per peer) run
-        underneath them.  From 4 ranks on, only the first half of each local expert's
-        rows goes first and the second half is computed after the other ranks' rows,
-        straight into the return buffer, while the other ranks finish their returns.
+        underneath them.  From ``split_min_ws`` ranks on, only the first half of each
+        local expert's rows goes first and the second half is computed after the other
+        ranks' rows, straight into the return buffer, while the other ranks finish their
+        returns.
+
+        The sender places its rows directly in the receiver's expert-major layout (one
+        copy per destination expert: local expert, then source rank, then token order),
+        so the receiver's GEMM reads its receive buffer as it is -- no regrouping pass.
+        With a capacity the sender knows from the count matrix which prefix of each
+        segment the receiver keeps, sends only that prefix and zeroes the return rows
+        of the rest; a rank's own rows for expert e follow the rows of every lower rank
+        in e's (source rank, token, slot) order, so the first half of them is computed
+        speculatively and the rows past the cut are zeroed the same way.
 
         The outputs of the other ranks' rows go back without a separate pass: the expert
         GEMM's epilogue stores each row at its address in the source rank's return
         buffer (``return_mode="fused"``; addresses from ``ep_return_rows``), so the
         return traffic crosses NVLink tile by tile while the GEMM runs.
-        ``return_mode="copy"`` gathers them and copies them back with the copy engines.
-
-        With a capacity, a rank's own rows for expert e follow the rows of every lower
-        rank in e's (source rank, token, slot) order, so how many of them are kept is
-        known only from the count matrix: the first half is computed speculatively, and
-        rows past the cut travel back as zeros like the dropped rows of other ranks."""
+        ``return_mode="copy"`` computes them locally and copies them back per segment
+        with the copy engines."""
         rt = self.rt
         ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
         T, k = idx.shape
@@ -428,10 +438,7 @@ class ExpertParallelExchange:
         mark("counts_done")
         offs = plan["offsets"][me * El:(me + 1) * El + 1]
         starts, fins = offs[:-1], offs[1:]
-        # With 2 ranks half of the rows are local and the local GEMMs alone hide the whole
-        # dispatch; splitting them would only add tail waves.  From 4 ranks on, the local
-        # rows are split in two halves around the remote rows.
-        split = ws >= 4
+        split = ws >= self.split_min_ws
         mids = starts + (fins - starts) // 2 if split else fins
         mark("experts_selfA_start")
         y_a = experts(send, starts, ends=mids)
@@ -439,86 +446,101 @@ class ExpertParallelExchange:
         ev_a = rt.record(comp)
         rt.host_wait(ev_counts)
         Gh = self._host[:ws * E].numpy().reshape(ws, ws, El).astype(np.int64)   # [src, dst, El]
-        R = Gh.sum(2)                                  # rows src -> dst
-        Rr = R.copy()
-        np.fill_diagonal(Rr, 0)                        # a rank's own rows are not copied
-        recv_tot = Rr.sum(0)                           # [dst]
-        SO = np.cumsum(Rr, 0) - Rr                     # src offset inside dst's receive buffer
-        SD = np.cumsum(R, 1) - R                       # dst segment offset inside src's send layout
+        R = Gh.sum(2)                                  # slots src -> dst
+        SD = np.cumsum(R, 1) - R                       # dst segment start in src's send / return layout
+        W = np.cumsum(Gh, 2) - Gh                      # expert start inside the (src -> dst) segment
+        if capacity > 0:                               # kept prefix of each (src, dst, expert) segment
+            Kp = np.clip(capacity - (np.cumsum(Gh, 0) - Gh), 0, Gh)
+        else:
+            Kp = Gh
+        Kr = Kp.copy()
+        Kr[np.arange(ws), np.arange(ws), :] = 0        # a rank's own rows are not copied
+        per_exp = Kr.sum(0)                            # [dst, El] rows each receiver gets per expert
+        EO = np.cumsum(per_exp, 1) - per_exp           # expert region start in dst's receive buffer
+        SO = np.cumsum(Kr, 0) - Kr                     # src offset inside that expert region
+        recv_tot = per_exp.sum(1)
         send_tot = R.sum(1)
         recv_buf.ensure(int(max(recv_tot.max(), 1)) * rb)
         ret_buf.ensure(int(max(send_tot.max(), 1)) * rb)
-        # dispatch copies to every peer, then one all-reduce to order them before use
+        # dispatch: one copy per (peer, expert) segment into the peer's expert-major
+        # layout, one stream per peer, then one all-reduce to order them before use
         sbase = send.data_ptr()
-        self._fan_out([(recv_buf.ptrs[r], 0, 0) if r == me else
-                       (recv_buf.ptrs[r] + int(SO[me, r]) * rb, sbase + int(SD[me, r]) * rb, int(R[me, r]) * rb)
-                       for r in range(ws)], comm, send, dev)
+        self._fan_out([[(recv_buf.ptrs[r] + int(EO[r, le] + SO[me, r, le]) * rb,
+                         sbase + int(SD[me, r] + W[me, r, le]) * rb, int(Kr[me, r, le]) * rb) for le in range(El)]
+                       for r in range(ws) if r != me], comm, send, dev)
         self._barrier(comm, dev)
         ev_sent = rt.record(comm)
-        # this rank's own rows of the first pass are copied (communication stream, once
-        # the GEMMs are done) into the return buffer, whose layout is the send layout
-        # (the same row numbers as in `send`); rows past the capacity cut become zeros
+        # own rows of the first pass: copied (communication stream, once the GEMMs are
+        # done) into the return buffer, whose layout is the send layout; every slot the
+        # capacity dropped -- own or sent -- becomes a zero row there
         ret_local = rt.view(ret_buf.local, (ret_buf.bytes // rb, d), x.dtype, dev)
-        own = Gh[me, me, :]                                       # rows per local expert
-        keep = np.clip(capacity - Gh[:me, me, :].sum(0), 0, own) if capacity > 0 else own
-        a_e = int(SD[me, me]) + np.concatenate([[0], np.cumsum(own)[:-1]])
-        h_e = own // 2 if split else own                          # rows of the first pass
+        own, keep = Gh[me, me, :], Kp[me, me, :]
+        a_e = SD[me, me] + W[me, me, :]
+        h_e = own // 2 if split else own               # rows of the first pass
         rbase = ret_local.data_ptr()
         rt.wait(comm, ev_a)
         rt.keep(y_a, comm)
         rt.copy([(rbase + int(a) * rb, y_a.data_ptr() + int(a) * rb, int(min(h, kp)) * rb)
                  for a, h, kp in zip(a_e, h_e, keep)], comm)
-        with rt.on(comm):
-            for a, kp, o in zip(a_e, keep, own):
-                if kp < o:
-                    ret_local[int(a + kp):int(a + o)].zero_()
-        # rows from the other ranks
+        if capacity > 0:
+            with rt.on(comm):
+                for r in range(ws):
+                    for le in np.nonzero(Kp[me, r] < Gh[me, r])[0]:
+                        a = int(SD[me, r] + W[me, r, le])
+                        ret_local[a + int(Kp[me, r, le]):a + int(Gh[me, r, le])].zero_()
+        # the other ranks' rows, already grouped by local expert
         mark("wait_sent0_before")
         rt.wait(comp, ev_sent)
         mark("wait_sent0_after")
         n_recv = int(recv_tot[me])
-        rc = G[:, me * El:(me + 1) * El].clone()
-        pos = torch.cumsum(rc, 0, dtype=torch.int32) - rc if capacity > 0 else None
-        rc[me].zero_()
         recv_local = rt.view(recv_buf.local, (recv_buf.bytes // rb, d), x.dtype, dev)
-        rg = self.k.ep_regroup_plan(rc, capacity, n_recv, pos_base=pos)
-        xe = self.k.permute_rows(recv_local[:n_recv], rg["row_src"], rg["offsets"], rg["rows_cap"])
-        self.last_rows = kept_rows(Gh[:, me, :].sum(0), capacity)
+        xe = recv_local[:n_recv]
+        # one pinned table per step: expert offsets of the receive buffer, then the return
+        # segments (local expert, source) -- starts, end, addresses in the sources' buffers.
+        # It is rewritten only after this step's count exchange, which follows every use
+        # of it by the previous step's compute stream.
+        nseg = El * ws
+        n_tab = 2 * nseg + 1 + El + 1 + El
+        if self._seg_host is None or self._seg_host.numel() != n_tab:
+            self._seg_host = rt.host_buffer(n_tab, torch.int64)
+        tab = self._seg_host.numpy()
+        seg_start = (EO[me][:, None] + SO[:, me, :].T).reshape(-1)          # (le, src) order
+        seg_addr = [0 if s_ == me else ret_buf.ptrs[s_] + int(SD[s_, me] + W[s_, me, le]) * rb
+                    for le in range(El) for s_ in range(ws)]
+        tab[:nseg] = seg_start
+        tab[nseg] = n_recv
+        tab[nseg + 1:2 * nseg + 1] = seg_addr
+        tab[2 * nseg + 1:2 * nseg + 1 + El] = EO[me]
+        tab[2 * nseg + 1 + El] = n_recv
+        tab[2 * nseg + 2 + El:] = keep                                       # own rows kept
+        tab_dev = torch.empty(n_tab, dtype=torch.int64, device=dev)
+        tab_dev.copy_(self._seg_host, non_blocking=True)
+        x_offs = tab_dev[2 * nseg + 1:2 * nseg + 2 + El].to(torch.int32)
+        self.last_rows = int(Kp[:, me, :].sum())
         if self.return_mode == "fused" and rb % 16 == 0:
             # the expert GEMM's epilogue stores every output row straight into its source
             # rank's return buffer (peer memory over NVLink) while the GEMM runs
-            # the pinned table is rewritten only after this step's count exchange, which
-            # follows every use of it by the previous step's compute stream
-            if self._seg_host is None or self._seg_host.numel() != 2 * ws + 1:
-                self._seg_host = rt.host_buffer(2 * ws + 1, torch.int64)
-            seg = self._seg_host.numpy()
-            seg[:ws] = SO[:, me]
-            seg[ws] = n_recv
-            seg[ws + 1:] = [0 if s_ == me else ret_buf.ptrs[s_] + int(SD[s_, me]) * rb for s_ in range(ws)]
-            seg_dev = torch.empty(2 * ws + 1, dtype=torch.int64, device=dev)
-            seg_dev.copy_(self._seg_host, non_blocking=True)
-            row_ptrs = self.k.ep_return_rows(rg["row_src"], rg["offsets"], rg["recv_dst"], n_recv, seg_dev, rb,
-                                             rg["rows_cap"])
+            row_ptrs = self.k.ep_return_rows(None, x_offs, None, n_recv, tab_dev[:2 * nseg + 1], rb, n_recv)
             mark("experts0_start")
-            experts(xe, rg["offsets"], row_ptrs=row_ptrs)
+            experts(xe, x_offs, row_ptrs=row_ptrs)
             mark("experts0_end")
             rt.join(comm, comp)
         else:
             mark("experts0_start")
-            y = experts(xe, rg["offsets"])
+            y = experts(xe, x_offs)
             mark("experts0_end")
-            back = self.k.gather_rows(y, rg["recv_dst"], n_recv)
             rt.join(comm, comp)
-            bbase = back.data_ptr()
-            self._fan_out([(0, 0, 0) if s_ == me else
-                           (ret_buf.ptrs[s_] + int(SD[s_, me]) * rb, bbase + int(SO[s_, me]) * rb, int(R[s_, me]) * rb)
-                           for s_ in range(ws)], comm, back, dev)
+            ybase = y.data_ptr()
+            self._fan_out([[(seg_addr[le * ws + s_], ybase + int(seg_start[le * ws + s_]) * rb,
+                             int(Kr[s_, me, le]) * rb) for le in range(El)]
+                           for s_ in range(ws) if s_ != me], comm, y, dev)
         self._barrier(comm, dev)
         ev_ret = rt.record(comm)
         if split:  # second half of the kept own rows, straight into the return buffer
             ends_b = fins
             if capacity > 0:
-                ends_b = torch.maximum(mids, torch.minimum(fins, starts + torch.clamp(capacity - pos[me], min=0)))
+                kd = tab_dev[2 * nseg + 2 + El:].to(torch.int32)
+                ends_b = torch.maximum(mids, torch.minimum(fins, starts + kd))
             mark("experts_selfB_start")
             experts(send, mids, ends=ends_b, out=ret_local)
             mark("experts_selfB_end")

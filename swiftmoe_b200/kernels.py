@@ -176,16 +176,18 @@ def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int, pos_b
 def ep_return_rows(row_src: torch.Tensor, offsets: torch.Tensor, recv_dst: torch.Tensor, n_recv: int,
                    seg_table: torch.Tensor, row_bytes: int, rows_cap: int) -> torch.Tensor:
     """Return address of every expert row (int64 [rows_cap]) for ``grouped_gemm(row_ptrs=)``;
-    zero rows at the return addresses of dropped received rows.  seg_table: int64
+    zero rows at the return addresses of dropped received rows.  row_src None: expert
+    row i is received row i; recv_dst None: nothing dropped.  seg_table: int64
     [2 * n_src + 1] device tensor: source segment starts (n_src + 1, last = n_recv), then
     the address of each source's return region."""
     _need_cuda(row_src, offsets, recv_dst, seg_table)
     El = offsets.numel() - 1
+    dev = offsets.device
     n_src = (seg_table.numel() - 1) // 2
-    row_ptrs = torch.empty(max(rows_cap, 1), dtype=torch.int64, device=row_src.device)
+    row_ptrs = torch.empty(max(rows_cap, 1), dtype=torch.int64, device=dev)
     L.check(L.load().smoe_ep_return_rows(L.ptr(row_src), L.ptr(offsets), El, L.ptr(recv_dst), n_recv,
                                          L.ptr(seg_table), n_src, row_bytes, L.ptr(row_ptrs), rows_cap,
-                                         L.stream_handle(row_src.device)), "smoe_ep_return_rows")
+                                         L.stream_handle(dev)), "smoe_ep_return_rows")
     return row_ptrs
 
 

@@ -98,14 +98,15 @@ def ep_return_rows(row_src, offsets, recv_dst, n_recv, seg_table, row_bytes, row
         return int(base[s]) + (r - int(starts[s])) * row_bytes
 
     kept = int(offsets.numpy()[-1])
-    rs = row_src.numpy()
+    rs = row_src.numpy() if row_src is not None else np.arange(max(rows_cap, 1))
     ptrs = np.zeros(max(rows_cap, 1), np.int64)
     for i in range(min(kept, rows_cap)):
         r = int(rs[i])
         if 0 <= r < n_recv:
             ptrs[i] = addr(r)
-    rd = recv_dst.numpy()
-    for r in range(n_recv):
-        if rd[r] < 0:
-            ctypes.memset(addr(r), 0, row_bytes)
+    if recv_dst is not None:
+        rd = recv_dst.numpy()
+        for r in range(n_recv):
+            if rd[r] < 0:
+                ctypes.memset(addr(r), 0, row_bytes)
     return torch.from_numpy(ptrs)

@@ -47,8 +47,11 @@ def _worker(rank, ws, port, cfg, transport, out_dir):
                       capacity_factor=cf, num_shared_experts=1 if shared else 0, d_ff_shared=F,
                       use_nccl_opt=False, device=dev)
     tr, _, sched = transport.partition("-")
-    tr, _, ret = tr.partition("+")
-    m.comm.transport, m.comm.schedule, m.comm.return_mode = tr, sched or "local_first", ret or "fused"
+    tr, *opts = tr.split("+")
+    m.comm.transport, m.comm.schedule = tr, sched or "local_first"
+    m.comm.return_mode = "copy" if "copy" in opts else "fused"
+    if "split" in opts:                   # own rows in two halves even with 2 ranks
+        m.comm.split_min_ws = 2
     m.comm.min_chunk_tokens = 64          # several chunks even at these small sizes
     El = E // ws
     sl = slice(rank * El, (rank + 1) * El)
@@ -92,7 +95,7 @@ CASES = [(300, 256, 8, 2, 512, None, False), (257, 256, 16, 2, 256, 1.0, False),
          (200, 128, 32, 8, 128, None, True)]
 
 
-@pytest.mark.parametrize("transport", ["p2p", "p2p+copy", "p2p-chunked", "collective"])
+@pytest.mark.parametrize("transport", ["p2p", "p2p+copy", "p2p+split", "p2p-chunked", "collective"])
 @pytest.mark.parametrize("cfg", CASES)
 def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
     n = torch.cuda.device_count()

@@ -129,7 +129,7 @@ def test_grouped_row_ranges(K, dtype):
     assert max_abs_err(got[inside].numpy(), ref[inside].numpy()) <= tol * max(1.0, ref.abs().max().item())
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("cap", [0, 40])
 def test_grouped_gemm_row_addresses(K, dtype, cap):
     """The fused expert-parallel return on one GPU: ep_return_rows turns a receive layout
