@@ -1,7 +1,6 @@
 """Expert-parallel exchange on world-size 2 and 4 gloo CPU ranks (kernels replaced by a
 numpy double), against the oracle's multi-rank forward, including capacity drops."""
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -13,15 +12,12 @@ import torch.multiprocessing as mp
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rdzv(tmp_path):
+    """File rendezvous for the spawned ranks (no TCP port that another process can take)."""
+    return str(tmp_path / "rendezvous")
 
 
-def _worker(rank, ws, port, E, d, T, k, cap_factor, chunks, result_dir):
+def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, chunks, result_dir):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     import torch.distributed as dist
@@ -29,9 +25,7 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, chunks, result_dir):
     from oracle import moe_oracle as O
     from swiftmoe_b200._core import capacity_rows
     from swiftmoe_b200.ep import ExpertParallelExchange
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    dist.init_process_group("gloo", init_method=f"file://{rdzv}", rank=rank, world_size=ws)
     rng = np.random.default_rng(0)
     gate = (rng.standard_normal((E, d)) * 0.3).astype(np.float32)
     W = (rng.standard_normal((E, d, d)) * 0.1).astype(np.float32)   # nn.Linear [out, in]
@@ -67,6 +61,6 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, chunks, result_dir):
                                                (4, 16, 2, 0.5, 2), (2, 4, 2, 0.7, 5)])
 def test_ep_exchange_matches_oracle(tmp_path, ws, E, k, cf, chunks):
     T, d = 23, 12
-    mp.spawn(_worker, args=(ws, _port(), E, d, T, k, cf, chunks, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, T, k, cf, chunks, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         assert float(np.load(tmp_path / f"err{r}.npy")[0]) <= 1e-5

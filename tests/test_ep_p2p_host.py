@@ -6,7 +6,7 @@ split of the own rows, the capacity cut of the own rows, the return addresses of
 fused return) is checked against the oracle's multi-rank forward without a GPU."""
 import ctypes
 import os
-import socket
+import zlib
 import sys
 from pathlib import Path
 
@@ -18,15 +18,12 @@ import torch.multiprocessing as mp
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rdzv(tmp_path):
+    """File rendezvous for the spawned ranks (no TCP port that another process can take)."""
+    return str(tmp_path / "rendezvous")
 
 
-def _worker(rank, ws, port, E, d, T, k, cap_factor, schedule, with_shared, result_dir):
+def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, result_dir):
     schedule, _, return_mode = schedule.partition("+")
     sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
     import torch.distributed as dist
@@ -35,9 +32,7 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, schedule, with_shared, resul
     from oracle import moe_oracle as O
     from swiftmoe_b200._core import capacity_rows
     from swiftmoe_b200.ep import ExpertParallelExchange
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    dist.init_process_group("gloo", init_method=f"file://{rdzv}", rank=rank, world_size=ws)
     rng = np.random.default_rng(0)
     gate = (rng.standard_normal((E, d)) * 0.3).astype(np.float32)
     W = (rng.standard_normal((E, d, d)) * 0.1).astype(np.float32)   # nn.Linear [out, in]
@@ -45,7 +40,7 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, schedule, with_shared, resul
     x = xs[rank]
     idx, w, _ = O.route(x, gate, k)
     ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=3, min_chunk_tokens=1,
-                                transport="p2p", schedule=schedule, runtime=HostRuntime(f"smoet{port}"))
+                                transport="p2p", schedule=schedule, runtime=HostRuntime(f"smoet{zlib.crc32(rdzv.encode()):08x}"))
     ex.return_mode = return_mode or "fused"
     cap = capacity_rows(cap_factor, T, ws, k, E)
     El = E // ws
@@ -98,7 +93,7 @@ def _worker(rank, ws, port, E, d, T, k, cap_factor, schedule, with_shared, resul
     (2, 8, 2, 1.0, "chunked", False), (4, 8, 2, 0.5, "chunked", True)])
 def test_p2p_schedules_match_oracle(tmp_path, ws, E, k, cf, schedule, shared):
     T, d = 23, 12
-    mp.spawn(_worker, args=(ws, _port(), E, d, T, k, cf, schedule, shared, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, T, k, cf, schedule, shared, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         err, same, rows_diff = np.load(tmp_path / f"err{r}.npy")
         assert err <= 1e-5, (r, err)

@@ -3,7 +3,6 @@ the oracle's multi-rank forward (experts split in contiguous blocks, capacity cu
 (source rank, token, slot) order).  Skipped on machines with fewer than two GPUs."""
 import datetime
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -16,25 +15,22 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rdzv(tmp_path):
+    """File rendezvous for the spawned ranks (no TCP port that another process can take)."""
+    return str(tmp_path / "rendezvous")
 
 
-def _worker(rank, ws, port, cfg, transport, out_dir):
+def _worker(rank, ws, rdzv, cfg, transport, out_dir):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "tests" / "golden")]
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
-                      NCCL_NVLS_ENABLE="0")
+    os.environ.update(LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     import synth
     from oracle import moe_oracle as O
     from util import max_rel_err, rounded
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method=f"file://{rdzv}", rank=rank, world_size=ws,
+                            timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     T, d, E, k, F, cf, shared = cfg
     dt = torch.bfloat16
@@ -102,7 +98,7 @@ def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
     if n < 2:
         pytest.skip("needs two or more GPUs")
     ws = 4 if n >= 4 and cfg[2] % 4 == 0 else 2
-    mp.spawn(_worker, args=(ws, _port(), cfg, transport, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_worker, args=(ws, _rdzv(tmp_path), cfg, transport, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         err, same_bits, agree, dev_err = np.load(tmp_path / f"r{r}.npy")
         assert dev_err == 0.0
@@ -111,15 +107,15 @@ def test_ep_layer_matches_oracle(tmp_path, cfg, transport):
         assert same_bits == 1.0
 
 
-def _ref_fixture_worker(rank, ws, port, name, transport, out_dir):
+def _ref_fixture_worker(rank, ws, rdzv, name, transport, out_dir):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "tests" / "golden")]
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
-                      NCCL_NVLS_ENABLE="0")
+    os.environ.update(LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     import fixtures as fx
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method=f"file://{rdzv}", rank=rank, world_size=ws,
+                            timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     import swiftmoe_b200 as S
     f, p = fx.ult_linear(name)
@@ -144,6 +140,6 @@ def test_ep_matches_reference_ultimate_moe(tmp_path, name, ws, transport):
     same world size (gloo, CPU): max-abs 1e-5 on every rank."""
     if torch.cuda.device_count() < ws:
         pytest.skip(f"needs {ws} GPUs")
-    mp.spawn(_ref_fixture_worker, args=(ws, _port(), name, transport, str(tmp_path)), nprocs=ws, join=True)
+    mp.spawn(_ref_fixture_worker, args=(ws, _rdzv(tmp_path), name, transport, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         assert float(np.load(tmp_path / f"ref{r}.npy")[0]) <= 1e-5
