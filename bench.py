@@ -74,6 +74,8 @@ def parse():
                     help="overlap schedule of the p2p exchange")
     ap.add_argument("--ep-return", default=None, choices=["fused", "copy"],
                     help="local-first return: GEMM epilogue stores to the peers, or copies")
+    ap.add_argument("--ep-dedup", default=None, choices=["auto", "on", "off"],
+                    help="local first: send each token once per destination rank")
     ap.add_argument("--ep-split-min-ws", type=int, default=None,
                     help="local first: split the own rows in two halves from this world size on")
     return ap.parse_args()
@@ -319,6 +321,8 @@ def main():
             model.comm.return_mode = args.ep_return
         if args.ep_split_min_ws:
             model.comm.split_min_ws = args.ep_split_min_ws
+        if args.ep_dedup:
+            model.comm.dedup = args.ep_dedup
     x = torch.randn((T, D_MODEL), device=dev, dtype=cdtype, generator=torch.Generator(device=dev).manual_seed(100 + rank))
     out = torch.empty_like(x)
 
@@ -488,7 +492,8 @@ def main():
                            f"{len(binding[0])} CPUs of the GPU's NUMA node (of {len(binding[1])})",
                            "ep_exchange": None if ws == 1 else
                            f"{model.comm.transport} transport, " + (
-                               f"{model.comm.schedule} schedule, {model.comm.return_mode} return"
+                               f"{model.comm.schedule} schedule, {model.comm.return_mode} return, "
+                               f"token dedup {model.comm.dedup}"
                                if model.comm.schedule == "local_first"
                                else f"{model.comm.n_chunks(T)} token chunks"),
                            "l2": f"inputs larger than L2: x {x.numel() * x.element_size() / 2**20:.0f} MiB and "

@@ -81,6 +81,7 @@ SMOE_API int smoe_topk_from_logits(const float* logits, int T, int E, int k, int
  *   expert_offsets[E+1] : start row of each expert's segment (exclusive scan of the kept
  *                         counts, each rounded up to row_align); [E] = total rows
  *   slot_row  [T*k]     : destination row of every slot, -1 when dropped by capacity
+ *                         or skipped (an idx entry of -1 marks a slot to skip)
  *   row_token [rows_cap]: source token of every row, -1 for alignment padding
  * capacity <= 0 means unlimited; otherwise at most `capacity` rows per expert are kept,
  * the lowest (token, slot) indices winning.  rows_cap must be >= smoe_plan_rows_cap().
@@ -201,6 +202,28 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
  * (the senders placed their rows in expert-major order; rows_cap <= n_recv); recv_dst
  * NULL: nothing was dropped.  Replaces, with the GEMM above, the return path of
  * models/ultimate_moe.py:152,224-231.                                                 */
+/* Expert-parallel token dedup (top-k with several experts per rank).  A token whose
+ * slots go to several experts of one rank is sent to that rank once:
+ *   smoe_ep_dedup_ranks: ridx[T, k] = destination rank of each slot in this rank's
+ *     rotated order ((e / E_l - rank + ws) % ws; this rank first) for the first slot of
+ *     the token bound for that rank, -1 for its later slots to the same rank.  A
+ *     smoe_dispatch_plan over ridx with ws experts (-1 = skipped slot) lays out the sent
+ *     rows: one per (token, rank), grouped by rotated rank, token order.
+ *   smoe_ep_dedup_meta: for each sent row p (= slot_row of a first slot): meta_e[p, j] =
+ *     the local expert of slot j if it goes to the row's rank, else -1, and
+ *     meta_w[p, j] its gate weight (0 else), in slot order; own_e [T, k] holds the same
+ *     for this rank's own rows (rows [0, own_count[0]), own_count = the plan's
+ *     counts[0], device) and -1 in rows [own_count[0], T).
+ * The receiver plans over meta_e (local experts, -1 skipped), runs the experts and
+ * returns ONE weighted partial sum per received row (smoe_combine over meta_w); the
+ * sender adds the partial sums of its token's ranks.  Replaces the per-(token, slot)
+ * replication of models/ultimate_moe.py:123 (`repeat_interleave`) and its payload
+ * all_to_all_single (:139-141).                                                       */
+SMOE_API int smoe_ep_dedup_ranks(const int32_t* idx, int64_t T, int k, int E_l, int ws, int rank, int32_t* ridx,
+                                 smoe_stream_t stream);
+SMOE_API int smoe_ep_dedup_meta(const int32_t* idx, const float* w, const int32_t* ridx, const int32_t* slot_row,
+                                const int32_t* own_count, int64_t T, int k, int E_l, int ws, int32_t* meta_e,
+                                float* meta_w, int32_t* own_e, smoe_stream_t stream);
 SMOE_API int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, int E_l,
                                  const int32_t* recv_dst, int64_t n_recv, const int64_t* seg_table, int n_src,
                                  int64_t row_bytes, uint64_t* row_ptrs, int64_t rows_cap, smoe_stream_t stream);

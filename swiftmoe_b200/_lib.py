@@ -59,6 +59,8 @@ SIGNATURES = {
     "smoe_ep_regroup_workspace_size": (_sz, [_i32, _i32]),
     "smoe_ep_regroup_plan": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "smoe_ep_return_rows": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp]),
+    "smoe_ep_dedup_ranks": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "smoe_ep_dedup_meta": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "smoe_ep_buffer_create": (_i32, [_sz, C.POINTER(_vp), _vp]),
     "smoe_ep_buffer_destroy": (_i32, [_vp]),
     "smoe_ep_peer_open": (_i32, [_vp, C.POINTER(_vp)]),

@@ -614,6 +614,30 @@ int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, int capaci
   return SMOE_OK;
 }
 
+int smoe_ep_dedup_ranks(const int32_t* idx, int64_t T, int k, int E_l, int ws, int rank, int32_t* ridx,
+                        smoe_stream_t stream) {
+  if (T < 0 || k < 1 || E_l < 1 || ws < 1 || rank < 0 || rank >= ws) return SMOE_ERR_INVALID;
+  if (T == 0) return SMOE_OK;
+  if (!idx || !ridx) return SMOE_ERR_INVALID;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T, 256), (int64_t)device_sms() * 8);
+  ep_dedup_ranks_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, T, k, E_l, ws, rank, ridx);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_ep_dedup_meta(const int32_t* idx, const float* w, const int32_t* ridx, const int32_t* slot_row,
+                       const int32_t* own_count, int64_t T, int k, int E_l, int ws, int32_t* meta_e, float* meta_w,
+                       int32_t* own_e, smoe_stream_t stream) {
+  if (T < 0 || k < 1 || E_l < 1 || ws < 1) return SMOE_ERR_INVALID;
+  if (T == 0) return SMOE_OK;
+  if (!idx || !w || !ridx || !slot_row || !own_count || !meta_e || !meta_w || !own_e) return SMOE_ERR_INVALID;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T * k, 256), (int64_t)device_sms() * 8);
+  ep_dedup_meta_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, w, ridx, slot_row, own_count, T, k, E_l, ws,
+                                                               meta_e, meta_w, own_e);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
 int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, int E_l, const int32_t* recv_dst,
                         int64_t n_recv, const int64_t* seg_table, int n_src, int64_t row_bytes, uint64_t* row_ptrs,
                         int64_t rows_cap, smoe_stream_t stream) {

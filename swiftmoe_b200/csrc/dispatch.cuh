@@ -28,7 +28,7 @@ __device__ __forceinline__ void plan_warp_counts(const int32_t* __restrict__ idx
     int e = -1;
     if (s < n_slots) {
       e = idx[s];
-      if (e < 0 || e >= E) {
+      if (e != -1 && (e < 0 || e >= E)) {  // -1 marks a slot to skip
         set_device_error(kErrBadExpertIndex);
         e = -1;
       }
@@ -426,6 +426,69 @@ __global__ void __launch_bounds__(256) ep_return_rows_kernel(const int32_t* __re
     wrote = true;
   }
   if (wrote) __threadfence_system();  // rows in another GPU's memory: visible before exit
+}
+
+// Expert-parallel token dedup.  A token whose k slots go to several experts of one rank
+// travels to that rank once.  ridx[t][j] = the destination rank of slot j in this rank's
+// rotated order ((e / El - me + ws) % ws, so this rank's own rows come first) for the
+// first slot of token t bound for that rank, -1 for its later slots to the same rank;
+// a dispatch plan over ridx with ws "experts" then lays out one row per (token, rank).
+__global__ void __launch_bounds__(256) ep_dedup_ranks_kernel(const int32_t* __restrict__ idx, int64_t T, int k,
+                                                             int El, int ws, int me, int32_t* __restrict__ ridx) {
+  const int E = El * ws;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < T; t += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t* it = idx + t * k;
+    for (int j = 0; j < k; ++j) {
+      const int e = it[j];
+      if (e < 0 || e >= E) {
+        set_device_error(kErrBadExpertIndex);
+        ridx[t * k + j] = -1;
+        continue;
+      }
+      const int r = e / El;
+      bool first = true;
+      for (int jj = 0; jj < j; ++jj) {
+        const int e2 = it[jj];
+        if (e2 >= 0 && e2 < E && e2 / El == r) first = false;
+      }
+      ridx[t * k + j] = first ? (r - me + ws) % ws : -1;
+    }
+  }
+}
+
+// Per sent (token, rank) row p = slot_row[t][j] of a first slot j: the local expert
+// (-1 if the slot goes elsewhere) and the gate weight of each of the token's k slots, in
+// slot order, for the receiver's expansion and its weighted partial sum.  own_e holds
+// the same for this rank's own rows (rows [0, own_count[0]) of the rotated send layout)
+// and -1 in rows [own_count[0], T), so that a plan over own_e [T, k] covers exactly them.
+__global__ void __launch_bounds__(256) ep_dedup_meta_kernel(const int32_t* __restrict__ idx,
+                                                            const float* __restrict__ w,
+                                                            const int32_t* __restrict__ ridx,
+                                                            const int32_t* __restrict__ slot_row,
+                                                            const int32_t* __restrict__ own_count, int64_t T,
+                                                            int k, int El, int ws, int32_t* __restrict__ meta_e,
+                                                            float* __restrict__ meta_w, int32_t* __restrict__ own_e) {
+  const int E = El * ws;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = tid; t < T; t += nth) {
+    const int32_t* it = idx + t * k;
+    for (int j = 0; j < k; ++j) {
+      const int rr = ridx[t * k + j];
+      const int64_t p = slot_row[t * k + j];
+      if (rr < 0 || p < 0) continue;
+      const int r = it[j] / El;
+      for (int jj = 0; jj < k; ++jj) {
+        const int e2 = it[jj];
+        const bool same = e2 >= 0 && e2 < E && e2 / El == r;
+        meta_e[p * k + jj] = same ? e2 % El : -1;
+        meta_w[p * k + jj] = same ? w[t * k + jj] : 0.0f;
+        if (rr == 0) own_e[p * k + jj] = same ? e2 % El : -1;
+      }
+    }
+  }
+  const int64_t own = own_count[0];
+  for (int64_t i = own * k + tid; i < T * k; i += nth) own_e[i] = -1;
 }
 
 // dst[g][c][r] = src[g][r][c]; 32x32 tiles through shared memory.

@@ -191,6 +191,33 @@ def ep_return_rows(row_src: torch.Tensor, offsets: torch.Tensor, recv_dst: torch
     return row_ptrs
 
 
+def ep_dedup_ranks(idx: torch.Tensor, El: int, ws: int, rank: int) -> torch.Tensor:
+    """ridx [T, k] int32: rotated destination rank of the first slot of each token bound
+    for a rank, -1 for its later slots to the same rank (see smoe_ep_dedup_ranks)."""
+    _need_cuda(idx)
+    T, k = idx.shape
+    ridx = torch.empty((T, k), dtype=torch.int32, device=idx.device)
+    L.check(L.load().smoe_ep_dedup_ranks(L.ptr(idx), T, k, El, ws, rank, L.ptr(ridx),
+                                         L.stream_handle(idx.device)), "smoe_ep_dedup_ranks")
+    return ridx
+
+
+def ep_dedup_meta(idx: torch.Tensor, w: torch.Tensor, ridx: torch.Tensor, slot_row: torch.Tensor,
+                  own_count: torch.Tensor, El: int, ws: int, rows_cap: int):
+    """(meta_e [rows_cap, k] int32, meta_w [rows_cap, k] fp32, own_e [T, k] int32) of the
+    sent rows (see smoe_ep_dedup_meta); own_count: device int32, this rank's row count."""
+    _need_cuda(idx, w, ridx, slot_row, own_count)
+    T, k = idx.shape
+    dev = idx.device
+    meta_e = torch.empty((max(rows_cap, 1), k), dtype=torch.int32, device=dev)
+    meta_w = torch.empty((max(rows_cap, 1), k), dtype=torch.float32, device=dev)
+    own_e = torch.empty((max(T, 1), k), dtype=torch.int32, device=dev)
+    L.check(L.load().smoe_ep_dedup_meta(L.ptr(idx), L.ptr(w), L.ptr(ridx), L.ptr(slot_row), L.ptr(own_count), T, k,
+                                        El, ws, L.ptr(meta_e), L.ptr(meta_w), L.ptr(own_e), L.stream_handle(dev)),
+            "smoe_ep_dedup_meta")
+    return meta_e, meta_w, own_e
+
+
 def read_device_error(device) -> int:
     import ctypes as C
     flag = C.c_int(0)

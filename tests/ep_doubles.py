@@ -11,14 +11,17 @@ def dispatch_plan(idx, num_experts, capacity=0, row_align=1):
     idx_n = idx.numpy()
     T, k = idx_n.shape
     E = num_experts
-    counts = np.bincount(idx_n.ravel(), minlength=E).astype(np.int32)
+    flat = idx_n.ravel()
+    counts = np.bincount(flat[flat >= 0], minlength=E).astype(np.int32)   # -1: skipped slot
     kept = np.minimum(counts, capacity) if capacity > 0 else counts
     offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
     slot_row = -np.ones(T * k, np.int32)
     row_token = -np.ones(max(int(offsets[-1]), 1), np.int32)
     seen = np.zeros(E, np.int64)
     for s in range(T * k):
-        e = idx_n.ravel()[s]
+        e = flat[s]
+        if e < 0:
+            continue
         if capacity <= 0 or seen[e] < capacity:
             r = offsets[e] + seen[e]
             slot_row[s] = r
@@ -110,3 +113,35 @@ def ep_return_rows(row_src, offsets, recv_dst, n_recv, seg_table, row_bytes, row
             if rd[r] < 0:
                 ctypes.memset(addr(r), 0, row_bytes)
     return torch.from_numpy(ptrs)
+
+
+def ep_dedup_ranks(idx, El, ws, rank):
+    it = idx.numpy()
+    T, k = it.shape
+    r = it // El
+    ridx = -np.ones((T, k), np.int32)
+    for t in range(T):
+        for j in range(k):
+            if r[t, j] not in r[t, :j]:
+                ridx[t, j] = (r[t, j] - rank) % ws
+    return torch.from_numpy(ridx)
+
+
+def ep_dedup_meta(idx, w, ridx, slot_row, own_count, El, ws, rows_cap):
+    it, wn, rn = idx.numpy(), w.numpy(), ridx.numpy()
+    sr = slot_row.numpy().reshape(it.shape)
+    T, k = it.shape
+    meta_e = -np.ones((max(rows_cap, 1), k), np.int32)
+    meta_w = np.zeros((max(rows_cap, 1), k), np.float32)
+    own_e = -np.ones((max(T, 1), k), np.int32)
+    for t in range(T):
+        for j in range(k):
+            if rn[t, j] < 0 or sr[t, j] < 0:
+                continue
+            p = sr[t, j]
+            same = it[t] // El == it[t, j] // El
+            meta_e[p] = np.where(same, it[t] % El, -1)
+            meta_w[p] = np.where(same, wn[t], 0.0)
+            if rn[t, j] == 0:
+                own_e[p] = meta_e[p]
+    return torch.from_numpy(meta_e), torch.from_numpy(meta_w), torch.from_numpy(own_e)

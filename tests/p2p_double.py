@@ -94,9 +94,10 @@ class HostRuntime:
         return ShmBuffers(group, rank, world_size, f"{self.tag}b{self.n_buffers}", self.registry)
 
     def view(self, ptr, shape, dtype, dev):
-        shm = self.registry[ptr]
+        base = max(b for b in self.registry if b <= ptr)
+        shm = self.registry[base]
         n = int(np.prod(shape))
-        return torch.frombuffer(shm.buf, dtype=dtype, count=n).view(*shape)
+        return torch.frombuffer(shm.buf, dtype=dtype, count=n, offset=ptr - base).view(*shape)
 
     @staticmethod
     def copy(segs, s):

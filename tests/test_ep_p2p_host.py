@@ -3,7 +3,8 @@ gloo CPU ranks, world sizes 2, 4 and 8: the CUDA runtime is replaced by a host d
 whose peer buffers are shared-memory segments (tests/p2p_double.py) and the kernels by
 the numpy double, so the host bookkeeping (copy segments, buffer layouts, the two-half
 split of the own rows, the capacity cut of the own rows, the return addresses of the
-fused return) is checked against the oracle's multi-rank forward without a GPU."""
+fused return, the token dedup) is checked against the oracle's multi-rank forward
+without a GPU."""
 import ctypes
 import os
 import zlib
@@ -24,7 +25,7 @@ def _rdzv(tmp_path):
 
 
 def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, result_dir):
-    schedule, _, return_mode = schedule.partition("+")
+    schedule, *opts = schedule.split("+")
     sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
     import torch.distributed as dist
     import ep_doubles
@@ -41,7 +42,9 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     idx, w, _ = O.route(x, gate, k)
     ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=3, min_chunk_tokens=1,
                                 transport="p2p", schedule=schedule, runtime=HostRuntime(f"smoet{zlib.crc32(rdzv.encode()):08x}"))
-    ex.return_mode = return_mode or "fused"
+    ex.return_mode = "copy" if "copy" in opts else "fused"
+    if "dedup" in opts:
+        ex.dedup = "on"
     cap = capacity_rows(cap_factor, T, ws, k, E)
     El = E // ws
 
@@ -90,7 +93,11 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     (4, 8, 3, None, "local_first", False), (4, 16, 2, 0.5, "local_first", False),
     (8, 8, 2, 0.7, "local_first", False), (8, 16, 2, None, "local_first", True),
     (2, 8, 2, 1.0, "local_first+copy", False), (4, 16, 2, 0.5, "local_first+copy", True),
-    (2, 8, 2, 1.0, "chunked", False), (4, 8, 2, 0.5, "chunked", True)])
+    (2, 8, 2, 1.0, "chunked", False), (4, 8, 2, 0.5, "chunked", True),
+    # token dedup: automatic from k = 4 on, forced at k = 2
+    (2, 16, 4, None, "local_first", True), (4, 16, 6, None, "local_first", False),
+    (8, 16, 8, None, "local_first", True), (2, 8, 2, None, "local_first+dedup", False),
+    (4, 16, 5, 0.5, "local_first", False)])
 def test_p2p_schedules_match_oracle(tmp_path, ws, E, k, cf, schedule, shared):
     T, d = 23, 12
     mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, T, k, cf, schedule, shared, str(tmp_path)), nprocs=ws, join=True)

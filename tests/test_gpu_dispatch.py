@@ -149,3 +149,48 @@ def test_ep_regroup_plan_chunked_capacity(K, ws, El, cap, chunks):
     kept = sum(int(K.ep_regroup_plan(to_dev(rc_all[c], torch.int32), cap, int(rc_all[c].sum()),
                                      pos_base=to_dev(pos[c], torch.int32))["offsets"][-1]) for c in range(chunks))
     assert kept == int(np.minimum(rc_all.sum((0, 1)), cap).sum())
+
+
+def _doubles():
+    import ep_doubles
+    return ep_doubles
+
+
+@pytest.mark.parametrize("T,k,E", [(1, 2, 8), (777, 4, 16), (5000, 8, 128)])
+def test_plan_skips_minus_one(K, T, k, E):
+    """idx entries of -1 are skipped slots: slot_row -1, not counted, no device error."""
+    rng = np.random.default_rng(T)
+    idx = np.array([rng.choice(E, size=k, replace=False) for _ in range(T)], dtype=np.int32).reshape(T, k)
+    idx[rng.random((T, k)) < 0.3] = -1
+    plan = K.dispatch_plan(to_dev(idx, torch.int32), E, 0, 1)
+    ref = _doubles().dispatch_plan(torch.from_numpy(idx), E)
+    for key in ("counts", "offsets", "slot_row"):
+        assert (plan[key].cpu().numpy() == ref[key].numpy()).all(), key
+    n = int(ref["offsets"][-1])
+    assert (plan["row_token"].cpu().numpy()[:n] == ref["row_token"].numpy()[:n]).all()
+    assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("T,k,El,ws,me", [(1, 2, 4, 2, 1), (300, 4, 8, 2, 0), (2000, 8, 16, 8, 3), (999, 6, 2, 4, 2)])
+def test_ep_dedup_plan_and_meta(K, T, k, El, ws, me):
+    """Token dedup: rotated ranks, the rank plan and the per-row slot metadata, bit-exact
+    against the numpy restatement."""
+    D = _doubles()
+    E = El * ws
+    rng = np.random.default_rng(T + k)
+    idx = np.array([rng.choice(E, size=k, replace=False) for _ in range(T)], dtype=np.int32).reshape(T, k)
+    w = rng.random((T, k)).astype(np.float32)
+    ridx = K.ep_dedup_ranks(to_dev(idx, torch.int32), El, ws, me)
+    ridx_ref = D.ep_dedup_ranks(torch.from_numpy(idx), El, ws, me)
+    assert (ridx.cpu().numpy() == ridx_ref.numpy()).all()
+    plan = K.dispatch_plan(ridx, ws, 0, 1)
+    me_, mw, oe = K.ep_dedup_meta(to_dev(idx, torch.int32), to_dev(w, torch.float32), ridx, plan["slot_row"],
+                                  plan["counts"][0:1], El, ws, plan["rows_cap"])
+    ref_plan = D.dispatch_plan(ridx_ref, ws)
+    me_r, mw_r, oe_r = D.ep_dedup_meta(torch.from_numpy(idx), torch.from_numpy(w), ridx_ref, ref_plan["slot_row"],
+                                       ref_plan["counts"][0:1], El, ws, plan["rows_cap"])
+    n = int(ref_plan["offsets"][-1])
+    assert (me_.cpu().numpy()[:n] == me_r.numpy()[:n]).all()
+    assert (mw.cpu().numpy()[:n] == mw_r.numpy()[:n]).all()
+    assert (oe.cpu().numpy()[:T] == oe_r.numpy()[:T]).all()
+    assert K.read_device_error("cuda") == 0
