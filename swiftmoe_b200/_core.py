@@ -123,6 +123,7 @@ class MoECore(nn.Module):
         self._timer = _StageTimer()
         self._ws_buf: Optional[torch.Tensor] = None
         self._wcache: Dict[str, tuple] = {}
+        self._soff: Dict[tuple, torch.Tensor] = {}   # shared expert: [0, T] per batch size
         self.comm = None
 
     # ------------------------------------------------------------ accessors
@@ -246,7 +247,10 @@ class MoECore(nn.Module):
             return None
         s1, s3, s2 = sh
         T = x.shape[0]
-        soff = torch.tensor([0, T], dtype=torch.int32).to(x.device, non_blocking=True)
+        key = (T, x.device)
+        soff = self._soff.get(key)
+        if soff is None:    # one group of all T rows; built once per batch size
+            soff = self._soff[key] = torch.tensor([0, T], dtype=torch.int32, device=x.device)
         hs = K.grouped_gemm(x, s1.unsqueeze(0), soff, B3=s3.unsqueeze(0), epilogue=L.SMOE_EPI_SWIGLU)
         return K.grouped_gemm(hs, s2.unsqueeze(0), soff)
 
