@@ -225,7 +225,8 @@ class MoEParams:
 
 def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int = 2,
                 weighting: str = "post", capacity_factor: Optional[float] = None,
-                acc=np.float32, round_hidden=None, return_aux: bool = False):
+                acc=np.float32, round_hidden=None, return_aux: bool = False,
+                capacity: Optional[int] = None):
     """Full layer forward for ``ws`` ranks; ``xs[r]`` is rank r's [T_r, d] input.
 
     Control flow follows ``StandardMoE.forward`` (``models/baseline_moe.py:191-213``):
@@ -237,6 +238,8 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
     weights are not renormalised.  The shared expert output is added unweighted.
     ``round_hidden`` (e.g. ``bf16_round``) rounds the intermediates a 16-bit pipeline
     stores: the SwiGLU hidden activation and each expert's output before weighting.
+    ``capacity`` (rows per expert, > 0) overrides the one derived from
+    ``capacity_factor``, e.g. for ranks with unequal batches.
     """
     E = p.num_experts
     if E % ws:
@@ -250,6 +253,8 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
     if capacity_factor is not None:
         # capacity is defined on the per-rank token count times ws (equal batches)
         cap = capacity_for(capacity_factor, xs[0].shape[0] * ws, k, E)
+    if capacity is not None and capacity > 0:
+        cap = capacity
     plan, kept = dispatch_plan([r[0] for r in routed], E, ws, cap)
 
     d = xs[0].shape[1] if len(xs) else p.gate.shape[1]

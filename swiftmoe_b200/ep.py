@@ -54,7 +54,10 @@ class DispatchState:
 
 
 def chunk_bounds(T: int, chunks: int) -> List[tuple]:
-    c = max(1, min(chunks, T)) if T > 0 else 1
+    """``chunks`` token ranges covering [0, T), some empty when T < chunks.  The count is
+    the same on every rank whatever its batch size, because the ranks exchange one count
+    vector per chunk."""
+    c = max(1, chunks)
     edges = [T * i // c for i in range(c + 1)]
     return [(edges[i], edges[i + 1]) for i in range(c)]
 
@@ -80,7 +83,7 @@ def kept_rows(rows_per_expert: np.ndarray, capacity: int) -> int:
 class ExpertParallelExchange:
     def __init__(self, num_experts: int, world_size: int, rank: int, d_model: int,
                  group: Optional[dist.ProcessGroup] = None, kernels=None, chunks: int = 4,
-                 min_chunk_tokens: int = 2048, transport: str = "auto", schedule: str = "local_first",
+                 transport: str = "auto", schedule: str = "local_first",
                  runtime=None):
         if num_experts % world_size:
             raise ValueError("num_experts must be divisible by the world size")
@@ -91,7 +94,6 @@ class ExpertParallelExchange:
         self.exp_per_rank = num_experts // world_size
         self.group = group
         self.chunks = chunks
-        self.min_chunk_tokens = min_chunk_tokens
         if kernels is None:
             from . import kernels as _k
             kernels = _k
@@ -170,7 +172,9 @@ class ExpertParallelExchange:
         self._last_rows, self._rows_dev = int(v), None
 
     def n_chunks(self, T: int) -> int:
-        return max(1, min(self.chunks, T // max(self.min_chunk_tokens, 1)))
+        """Token chunks of the chunked schedules: the same on every rank (the ranks'
+        batches may differ in size), so it does not depend on T."""
+        return max(1, self.chunks)
 
     # ------------------------------------------------------------------ the layer
     def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, capacity: int,

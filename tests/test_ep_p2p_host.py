@@ -26,6 +26,8 @@ def _rdzv(tmp_path):
 
 def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, result_dir):
     schedule, *opts = schedule.split("+")
+    Ts = list(T) if isinstance(T, (list, tuple)) else [T] * ws     # tokens per rank (ragged)
+    T = Ts[rank]
     sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
     import torch.distributed as dist
     import ep_doubles
@@ -37,15 +39,15 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     rng = np.random.default_rng(0)
     gate = (rng.standard_normal((E, d)) * 0.3).astype(np.float32)
     W = (rng.standard_normal((E, d, d)) * 0.1).astype(np.float32)   # nn.Linear [out, in]
-    xs = [np.random.default_rng(10 + r).standard_normal((T, d)).astype(np.float32) for r in range(ws)]
+    xs = [np.random.default_rng(10 + r).standard_normal((Ts[r], d)).astype(np.float32) for r in range(ws)]
     x = xs[rank]
     idx, w, _ = O.route(x, gate, k)
-    ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=3, min_chunk_tokens=1,
+    ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=3,
                                 transport="p2p", schedule=schedule, runtime=HostRuntime(f"smoet{zlib.crc32(rdzv.encode()):08x}"))
     ex.return_mode = "copy" if "copy" in opts else "fused"
     if "dedup" in opts:
         ex.dedup = "on"
-    cap = capacity_rows(cap_factor, T, ws, k, E)
+    cap = capacity_rows(cap_factor, max(Ts), ws, k, E)
     El = E // ws
 
     def experts(xe, offsets, ends=None, out=None, row_ptrs=None):
@@ -76,13 +78,14 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     out1 = ex.forward(*args, **kw).numpy().copy()
     out2 = ex.forward(*args, **kw).numpy().copy()      # buffers reused
     p = O.MoEParams(gate=gate, expert_type="linear", expert_w=np.ascontiguousarray(W.transpose(0, 2, 1)))
-    refs, aux = O.moe_forward(xs, p, ws=ws, k=k, capacity_factor=cap_factor, return_aux=True)
+    refs, aux = O.moe_forward(xs, p, ws=ws, k=k, capacity=cap, return_aux=True)
     ref = refs[rank] + (shared if shared is not None else 0)
     kept_ref = sum(int(min(cap, c)) if cap > 0 else int(c)
                    for c in np.bincount(np.concatenate([aux["routed"][r][0].ravel() for r in range(ws)]),
                                         minlength=E)[rank * El:(rank + 1) * El])
+    err = float(np.abs(out1 - ref).max()) if T else 0.0
     np.save(os.path.join(result_dir, f"err{rank}.npy"),
-            np.array([np.abs(out1 - ref).max(), float(np.array_equal(out1, out2)), ex.last_rows - kept_ref]))
+            np.array([err, float(np.array_equal(out1, out2)), ex.last_rows - kept_ref]))
     ex.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -101,6 +104,23 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
 def test_p2p_schedules_match_oracle(tmp_path, ws, E, k, cf, schedule, shared):
     T, d = 23, 12
     mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, T, k, cf, schedule, shared, str(tmp_path)), nprocs=ws, join=True)
+    _check(tmp_path, ws)
+
+
+@pytest.mark.parametrize("Ts,E,k,cf,schedule", [
+    ((0, 23), 8, 2, None, "local_first"), ((5, 0, 23, 1), 8, 2, None, "local_first"),
+    ((0, 17), 16, 4, None, "local_first"), ((5, 0, 23, 1), 16, 6, None, "local_first"),
+    ((0, 23), 8, 2, 1.0, "local_first"), ((5, 0, 23, 1), 8, 2, 0.5, "chunked")])
+def test_p2p_schedules_ragged_and_empty_batches(tmp_path, Ts, E, k, cf, schedule):
+    """Ranks with different token counts, some with none: every rank still takes part in
+    every collective step, and the ranks with tokens match the oracle."""
+    ws, d = len(Ts), 12
+    mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, Ts, k, cf, schedule, False, str(tmp_path)), nprocs=ws,
+             join=True)
+    _check(tmp_path, ws)
+
+
+def _check(tmp_path, ws):
     for r in range(ws):
         err, same, rows_diff = np.load(tmp_path / f"err{r}.npy")
         assert err <= 1e-5, (r, err)

@@ -48,7 +48,6 @@ def _worker(rank, ws, rdzv, cfg, transport, out_dir):
     m.comm.return_mode = "copy" if "copy" in opts else "fused"
     if "split" in opts:                   # own rows in two halves even with 2 ranks
         m.comm.split_min_ws = 2
-    m.comm.min_chunk_tokens = 64          # several chunks even at these small sizes
     El = E // ws
     sl = slice(rank * El, (rank + 1) * El)
     with torch.no_grad():
