@@ -49,9 +49,9 @@ WORKLOADS = {
                               name="small-moe-layer-fwd: d_model 512, 8 experts top-2, SwiGLU d_ff 2048, "
                                    "4096 tok, fp32"),
 }
-W = WORKLOADS["mixtral"]
-D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = W["d"], W["E"], W["k"], W["F"], W["T"]
-WORKLOAD = W["name"]
+WL = WORKLOADS["mixtral"]     # the selected workload (main() sets it from --workload)
+D_MODEL, N_EXPERTS, TOP_K, D_FF, TOKENS = WL["d"], WL["E"], WL["k"], WL["F"], WL["T"]
+WORKLOAD = WL["name"]
 # dram__bytes_read.sum + dram__bytes_write.sum of one grouped SwiGLU (gate/up) GEMM launch
 # of the default workload at full size (2.906 GB read + 0.929 GB written), from the ncu
 # capture summarised in profiles/grouped_gemm_mixtral_T16384_dram.md
@@ -163,26 +163,42 @@ def _host_threads():
     return threadpool_limits(limits=len(os.sched_getaffinity(0)))
 
 
+def _oracle_layer(rng, sample_tokens: int):
+    """The selected workload's layer as the oracle's fp32 parameters (seeded; shared
+    expert and router offsets when the workload has them) and a sample input batch."""
+    import numpy as np
+
+    from oracle import moe_oracle as O
+    E, d, F = N_EXPERTS, D_MODEL, D_FF
+
+    def w(shape):
+        return rng.standard_normal(shape, dtype=np.float32) * 0.02
+
+    p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
+    if WL["shared"]:
+        p.sw1, p.sw3, p.sw2 = w((1, F, d)), w((1, F, d)), w((1, d, F))
+    if WL["bias_std"]:
+        p.logit_bias = rng.standard_normal(E).astype(np.float32) * WL["bias_std"]
+    return p, rng.standard_normal((sample_tokens, d), dtype=np.float32)
+
+
+def _oracle_forward(p, x):
+    """One layer forward of the numpy restatement (capacity scaled to the batch)."""
+    from oracle import moe_oracle as O
+    return O.moe_forward([x], p, k=TOP_K, capacity_factor=WL["cf"])
+
+
 def cpu_reference(tokens_budget_s: float, sample_tokens: int = 64, seed: int = 0):
     """Time the numpy restatement of the reference forward on this host's cores."""
     import numpy as np
     from threadpoolctl import threadpool_info
 
-    from oracle import moe_oracle as O
-
-    rng = np.random.default_rng(seed)
-    E, d, F = N_EXPERTS, D_MODEL, D_FF
-
-    def w(shape):
-        return (rng.standard_normal(shape, dtype=np.float32) * 0.02)
-
-    p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
-    x = rng.standard_normal((sample_tokens, d), dtype=np.float32)
+    p, x = _oracle_layer(np.random.default_rng(seed), sample_tokens)
     with _host_threads():
-        O.moe_forward([x[:8]], p, k=TOP_K)  # warm BLAS
+        _oracle_forward(p, x[:8])  # warm BLAS
         done, t0 = 0, time.perf_counter()
         while True:
-            O.moe_forward([x], p, k=TOP_K)
+            _oracle_forward(p, x)
             done += sample_tokens
             el = time.perf_counter() - t0
             if el >= tokens_budget_s:
@@ -200,22 +216,14 @@ def run_reference_arm(args):
     import numpy as np
     from threadpoolctl import threadpool_info
 
-    from oracle import moe_oracle as O
-    rng = np.random.default_rng(0)
-    E, d, F = N_EXPERTS, D_MODEL, D_FF
-
-    def w(shape):
-        return rng.standard_normal(shape, dtype=np.float32) * 0.02
-
-    p = O.MoEParams(gate=w((E, d)), expert_type="swiglu", w1=w((E, F, d)), w3=w((E, F, d)), w2=w((E, d, F)))
     sample = 64
-    x = rng.standard_normal((sample, d), dtype=np.float32)
+    p, x = _oracle_layer(np.random.default_rng(0), sample)
     with _host_threads():
         for _ in range(args.warmup):
-            O.moe_forward([x], p, k=TOP_K)
+            _oracle_forward(p, x)
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            O.moe_forward([x], p, k=TOP_K)
+            _oracle_forward(p, x)
         el = time.perf_counter() - t0
         threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     v = sample * args.steps / el
@@ -273,8 +281,8 @@ def count_launches(fn):
 
 def main():
     args = parse()
-    global D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD
-    wl = WORKLOADS[args.workload]
+    global D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD, WL
+    wl = WL = WORKLOADS[args.workload]
     D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD = wl["d"], wl["E"], wl["k"], wl["F"], wl["name"]
     if args.tokens is None:
         args.tokens = wl["T"]
@@ -473,7 +481,7 @@ def main():
         launches_per_step = 8 if ws == 1 else (16 if ws >= 4 else 14)
         launches_src = f"static count (trace failed: {type(e).__name__})"
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "mixtral":
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
             if binding is not None:     # the CPU baseline uses every host thread again
                 os.sched_setaffinity(0, binding[1])
