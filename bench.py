@@ -265,7 +265,7 @@ def bind_near_gpu(index: int):
             return None
         os.sched_setaffinity(0, sel)
         return sel, before
-    except (OSError, ValueError, AttributeError):
+    except (OSError, ValueError, AttributeError, RuntimeError):
         return None
 
 

@@ -2,6 +2,7 @@
 parity with the reference, capacity arithmetic, and the no-CPU-fallback rule."""
 import math
 import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -107,3 +108,37 @@ def test_bench_records_grid_matches_reference():
     grid = reference_grid()
     assert {e for e, _ in grid} == {64, 128, 256}
     assert {b for _, b in grid} == {512, 1024, 2048, 4096, 8192}
+
+
+def test_chunk_bounds_same_count_for_every_batch_size():
+    """The chunked schedules exchange one count vector per chunk, so the chunk count may
+    not depend on the rank's batch size (ranks may hold different numbers of tokens)."""
+    from swiftmoe_b200.ep import chunk_bounds
+    for T in (0, 1, 3, 4, 23, 1000):
+        b = chunk_bounds(T, 4)
+        assert len(b) == 4
+        assert b[0][0] == 0 and b[-1][1] == T
+        assert all(b[i][1] == b[i + 1][0] and b[i][0] <= b[i][1] for i in range(3))
+
+
+def test_kept_rows_and_capacity_positions():
+    from swiftmoe_b200.ep import capacity_positions, kept_rows
+    assert kept_rows(np.array([5, 0, 9]), 0) == 14
+    assert kept_rows(np.array([5, 0, 9]), 4) == 8
+    rc = np.array([[[2, 0], [1, 3]], [[4, 1], [0, 2]]])            # [chunk, src, expert]
+    pos = capacity_positions(rc, 3)
+    # source-major, then chunk: src 0 chunk 0, src 0 chunk 1, src 1 chunk 0, src 1 chunk 1
+    assert pos[:, 0, 0].tolist() == [0, 2] and pos[:, 1, 0].tolist() == [6, 7]
+    assert pos[:, 0, 1].tolist() == [0, 0] and pos[:, 1, 1].tolist() == [1, 4]
+
+
+def test_bench_host_helpers(monkeypatch):
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    import bench
+    assert bench._cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench._cpulist("") == set()
+    # without a GPU the topology is unknown: no binding, no exception
+    assert bench.bind_near_gpu(0) is None
+    for name, wl in bench.WORKLOADS.items():
+        assert {"d", "E", "k", "F", "T", "dtype", "cf", "shared", "bias_std", "name"} <= set(wl), name
+        assert wl["E"] % 8 == 0, name          # expert parallelism up to 8 GPUs
