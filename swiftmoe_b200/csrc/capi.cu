@@ -197,7 +197,7 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   if (rows_cap > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
   if (dtype == SMOE_F32) {
     if (out_dtype != SMOE_F32 || G > simt::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
-    dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, 32) : cdiv(N, simt::BN)));
+    dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, simt::BN / 2) : cdiv(N, simt::BN)));
     if (epi == SMOE_EPI_SWIGLU)
       simt::grouped_gemm_f32_kernel<SMOE_EPI_SWIGLU><<<grid, simt::THREADS, 0, st>>>(
           (const float*)A, (const float*)B, (const float*)B3, (float*)C, N, row_ptrs, offsets, ends, G, N, K,
