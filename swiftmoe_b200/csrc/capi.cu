@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "dispatch.cuh"
 #include "gemm_simt.cuh"
+#include "gemv.cuh"
 #include "gemm_tc.cuh"
 #include "router.cuh"
 
@@ -170,6 +171,39 @@ int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return SMOE_OK;
 }
 
+template <int EPI, typename T, typename OutT>
+int launch_gemv_t(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs,
+                  const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
+                  cudaStream_t st) {
+  const int64_t warps = (int64_t)G * N;
+  const unsigned grid = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>(cdiv(warps * 32, gemv::THREADS), (int64_t)device_sms() * 4));
+  gemv::grouped_gemv_kernel<EPI, T, OutT><<<grid, gemv::THREADS, 0, st>>>(
+      (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int launch_gemv(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs, int dtype,
+                int out_dtype, int epi, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N,
+                int K, cudaStream_t st) {
+  const bool bf = dtype == SMOE_BF16;
+  if (epi == SMOE_EPI_SWIGLU)
+    return bf ? launch_gemv_t<SMOE_EPI_SWIGLU, __nv_bfloat16, __nv_bfloat16>(A, B, B3, C, row_ptrs, offsets, ends,
+                                                                             G, rows_cap, N, K, st)
+              : launch_gemv_t<SMOE_EPI_SWIGLU, __half, __half>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N,
+                                                               K, st);
+  if (out_dtype == SMOE_F32)
+    return bf ? launch_gemv_t<SMOE_EPI_STORE, __nv_bfloat16, float>(A, B, B3, C, row_ptrs, offsets, ends, G,
+                                                                    rows_cap, N, K, st)
+              : launch_gemv_t<SMOE_EPI_STORE, __half, float>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N, K,
+                                                             st);
+  return bf ? launch_gemv_t<SMOE_EPI_STORE, __nv_bfloat16, __nv_bfloat16>(A, B, B3, C, row_ptrs, offsets, ends, G,
+                                                                          rows_cap, N, K, st)
+            : launch_gemv_t<SMOE_EPI_STORE, __half, __half>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N, K,
+                                                            st);
+}
+
 // Which tensor-core kernel runs a grouped GEMM.  Measured on the Mixtral-shaped layer
 // (power-capped B200, 16384 tokens): the CTA-pair kernel takes 6.37 ms for the gate/up
 // GEMM against 6.03 ms for single CTAs -- the tensor pipe is power-bound, so the
@@ -208,7 +242,12 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
     SMOE_CK(cudaGetLastError());
     return SMOE_OK;
   }
-  // 16-bit inputs on tensor cores
+  // 16-bit inputs: decode-sized batches stream the weights on the SIMT pipes, the rest
+  // runs on tensor cores
+  if (rows_cap <= gemv::MAX_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 && aligned16(A) && aligned16(B) &&
+      (!B3 || aligned16(B3)) && (epi == SMOE_EPI_STORE || out_dtype == dtype) &&
+      (out_dtype == SMOE_F32 || out_dtype == dtype))
+    return launch_gemv(A, B, B3, C, row_ptrs, dtype, out_dtype, epi, offsets, ends, G, rows_cap, N, K, st);
   if (G > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
   if (K % 8 != 0 || N % 8 != 0) return SMOE_ERR_UNSUPPORTED;
   if (!aligned16(A) || !aligned16(B) || (C && !aligned16(C)) || (B3 && !aligned16(B3))) return SMOE_ERR_UNSUPPORTED;

@@ -1,0 +1,110 @@
+// Grouped GEMM for decode-sized batches (at most MAX_ROWS rows in all groups together),
+// 16-bit inputs.  With a handful of rows the layer is a stream of expert weights: the
+// tensor-core kernel's 128-row tiles would give the down projection of one token
+// 2 experts x 16 column tiles = 32 CTAs for 148 SMs.  Here one warp owns one output
+// column n of one group: its lanes read the weight row B[g][n][:] (and B3[g][n][:] for
+// SwiGLU) in 16-byte pieces, 4 pieces in flight per lane, multiply them with every row
+// of the group (A rows stay in L1/L2) and reduce across the warp.  Groups without rows
+// read nothing, so a token routed to 2 of 8 experts streams 2 experts' weights.
+//
+// Same grouping contract as the other grouped GEMMs: group g owns rows
+// [offsets[g], ends ? ends[g] : offsets[g+1]) of A [rows, K], clamped to rows_cap;
+// B is [G, N, K].  K % 8 == 0, A and B 16-byte aligned.
+#pragma once
+#include "common.cuh"
+
+namespace smoe {
+namespace gemv {
+
+constexpr int THREADS = 256, MAX_ROWS = 16, MAX_GROUPS = 1024, UNROLL = 4;
+
+template <typename T>
+__device__ __forceinline__ void fma8(const uint4& a, const uint4& b, float& acc) {
+  const T* x = reinterpret_cast<const T*>(&a);
+  const T* y = reinterpret_cast<const T*>(&b);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc = fmaf(Num<T>::to_f(x[i]), Num<T>::to_f(y[i]), acc);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int EPI, typename T, typename OutT>
+__global__ void __launch_bounds__(THREADS) grouped_gemv_kernel(const T* __restrict__ A, const T* __restrict__ B,
+                                                               const T* __restrict__ B3, OutT* __restrict__ C,
+                                                               int64_t ldc, const uint64_t* __restrict__ row_ptrs,
+                                                               const int32_t* __restrict__ offsets,
+                                                               const int32_t* __restrict__ ends, int G, int N, int K,
+                                                               int rows_cap) {
+  __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    const int b = min(max(offsets[g], 0), rows_cap);
+    s_beg[g] = b;
+    s_fin[g] = min(max(ends != nullptr ? ends[g] : offsets[g + 1], b), min(rows_cap, b + MAX_ROWS));
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t tasks = (int64_t)G * N;
+  const int chunks = K / 8;  // 16-byte pieces per row
+  for (int64_t task = warp; task < tasks; task += nwarps) {
+    const int g = (int)(task / N);
+    const int n = (int)(task - (int64_t)g * N);
+    const int b = s_beg[g], nr = s_fin[g] - b;
+    if (nr <= 0) continue;
+    const uint4* brow = reinterpret_cast<const uint4*>(B + ((int64_t)g * N + n) * K);
+    const uint4* b3row = EPI == SMOE_EPI_SWIGLU ? reinterpret_cast<const uint4*>(B3 + ((int64_t)g * N + n) * K)
+                                                : nullptr;
+    float acc[MAX_ROWS], acc3[MAX_ROWS];
+#pragma unroll
+    for (int r = 0; r < MAX_ROWS; ++r) acc[r] = acc3[r] = 0.0f;
+    for (int c0 = lane; c0 < chunks; c0 += 32 * UNROLL) {
+      uint4 wv[UNROLL], w3[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int c = c0 + u * 32;
+        wv[u] = c < chunks ? __ldcs(brow + c) : make_uint4(0u, 0u, 0u, 0u);  // weights: streamed once
+        if (EPI == SMOE_EPI_SWIGLU) w3[u] = c < chunks ? __ldcs(b3row + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int r = 0; r < MAX_ROWS; ++r) {
+        if (r < nr) {
+          const uint4* arow = reinterpret_cast<const uint4*>(A + (int64_t)(b + r) * K);
+#pragma unroll
+          for (int u = 0; u < UNROLL; ++u) {
+            const int c = c0 + u * 32;
+            if (c < chunks) {
+              const uint4 av = __ldg(arow + c);
+              fma8<T>(av, wv[u], acc[r]);
+              if (EPI == SMOE_EPI_SWIGLU) fma8<T>(av, w3[u], acc3[r]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MAX_ROWS; ++r) {
+      if (r < nr) {
+        const float v = warp_sum(acc[r]);
+        float out = v;
+        if (EPI == SMOE_EPI_SWIGLU) {
+          const float u = warp_sum(acc3[r]);
+          out = v / (1.0f + __expf(-v)) * u;
+        }
+        if (lane == 0) {
+          const int row = b + r;
+          OutT* crow = row_ptrs ? reinterpret_cast<OutT*>(row_ptrs[row]) : C + (int64_t)row * ldc;
+          if (crow != nullptr) crow[n] = Num<OutT>::from_f(out);
+        }
+      }
+    }
+  }
+  if (row_ptrs) __threadfence_system();  // rows in another GPU's memory: visible before exit
+}
+
+}  // namespace gemv
+}  // namespace smoe
