@@ -244,7 +244,7 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   }
   // 16-bit inputs: decode-sized batches stream the weights on the SIMT pipes, the rest
   // runs on tensor cores
-  if (rows_cap <= gemv::MAX_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 && aligned16(A) && aligned16(B) &&
+  if (rows_cap <= gemv::DISPATCH_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 && aligned16(A) && aligned16(B) &&
       (!B3 || aligned16(B3)) && (epi == SMOE_EPI_STORE || out_dtype == dtype) &&
       (out_dtype == SMOE_F32 || out_dtype == dtype))
     return launch_gemv(A, B, B3, C, row_ptrs, dtype, out_dtype, epi, offsets, ends, G, rows_cap, N, K, st);

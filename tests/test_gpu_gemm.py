@@ -42,6 +42,7 @@ def ref_swiglu(A, B1, B3, offs):
 SHAPES = [
     ([128], 64, 256),            # one full tile
     ([1], 64, 256),              # one row
+    ([0, 1, 0, 1], 520, 264),    # one token's two experts (decode kernel)
     ([0, 300, 0, 77], 128, 256),  # empty groups, ragged rows
     ([129, 255, 3], 72, 200),    # K % 64 != 0, N % 256 != 0
     ([513, 64, 1000], 256, 512),
