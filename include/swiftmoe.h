@@ -138,7 +138,9 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
  *   epilogue SMOE_EPI_STORE  : C[r, n] = acc                       (C is [rows_cap, N])
  *   epilogue SMOE_EPI_SWIGLU : C[r, n] = silu(A B1_g^T) * (A B3_g^T) (B3 = B2 arg, C [rows_cap, N])
  * bf16 / fp16 run on tcgen05 tensor cores (TMEM accumulators, TMA-fed shared memory,
- * requires K % 8 == 0 and N % 8 == 0); fp32 runs on FFMA (SIMT) for full fp32 accuracy.
+ * requires K % 8 == 0 and N % 8 == 0), except batches of at most 2 rows, which stream the
+ * weights of the groups that have rows on the SIMT pipes (one warp per output column);
+ * fp32 runs on FFMA (SIMT) for full fp32 accuracy.
  * C may be fp32 for the bf16/fp16 STORE epilogue when out_dtype == SMOE_F32.
  * Replaces: the per-expert loop of torch.mm at models/ultimate_moe.py:237-250 and
  * nn.Linear experts at models/baseline_moe.py:151-162.                               */
