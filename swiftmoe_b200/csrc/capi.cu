@@ -177,7 +177,7 @@ int launch_gemv_t(const void* A, const void* B, const void* B3, void* C, const u
                   cudaStream_t st) {
   const int64_t warps = (int64_t)G * N;
   const unsigned grid = (unsigned)std::max<int64_t>(
-      1, std::min<int64_t>(cdiv(warps * 32, gemv::THREADS), (int64_t)device_sms() * 4));
+      1, std::min<int64_t>(cdiv(warps * 32, gemv::THREADS), (int64_t)device_sms() * 8));
   gemv::grouped_gemv_kernel<EPI, T, OutT><<<grid, gemv::THREADS, 0, st>>>(
       (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap);
   SMOE_CK(cudaGetLastError());

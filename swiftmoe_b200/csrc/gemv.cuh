@@ -1,9 +1,9 @@
-// Grouped GEMM for decode-sized batches (at most DISPATCH_ROWS rows in all groups
-// together take it; the kernel handles up to MAX_ROWS), 16-bit inputs.  With a handful of rows the layer is a stream of expert weights: the
+// Grouped GEMM for decode-sized batches (at most MAX_ROWS rows in all groups together),
+// 16-bit inputs.  With a handful of rows the layer is a stream of expert weights: the
 // tensor-core kernel's 128-row tiles would give the down projection of one token
 // 2 experts x 16 column tiles = 32 CTAs for 148 SMs.  Here one warp owns one output
 // column n of one group: its lanes read the weight row B[g][n][:] (and B3[g][n][:] for
-// SwiGLU) in 16-byte pieces, 4 pieces in flight per lane, multiply them with every row
+// SwiGLU) in 16-byte pieces, 8 pieces per row in flight per lane, multiply them with every row
 // of the group (A rows stay in L1/L2) and reduce across the warp.  Groups without rows
 // read nothing, so a token routed to 2 of 8 experts streams 2 experts' weights.
 //
@@ -16,12 +16,13 @@
 namespace smoe {
 namespace gemv {
 
-constexpr int THREADS = 256, MAX_ROWS = 16, MAX_GROUPS = 1024, UNROLL = 4;
+constexpr int THREADS = 256, MAX_ROWS = 2, MAX_GROUPS = 1024, UNROLL = 8;
 // Batches this small take this kernel.  Measured on the Mixtral layer (1 B200, 1965 MHz):
-// one token (2 rows, one per expert) runs the down GEMM in 80 us against 95 us on the
-// tensor cores (gate/up 119 us either way); at 8 tokens (2 rows per expert) this kernel
-// takes 553 + 546 us against 322 + 146 us, its per-row work outgrowing the weight stream.
-constexpr int DISPATCH_ROWS = 2;
+// one token (2 rows, one per expert) runs gate/up in 92 us and down in 62 us against 119
+// and 95 us on the tensor cores.  An earlier build of this kernel for up to 16 rows took
+// 553 + 546 us at 8 tokens (2 rows per expert) against 322 + 146 us on the tensor cores,
+// its per-row work outgrowing the weight stream, hence the 2-row limit.
+constexpr int DISPATCH_ROWS = MAX_ROWS;
 
 template <typename T>
 __device__ __forceinline__ void fma8(const uint4& a, const uint4& b, float& acc) {
@@ -38,7 +39,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 template <int EPI, typename T, typename OutT>
-__global__ void __launch_bounds__(THREADS) grouped_gemv_kernel(const T* __restrict__ A, const T* __restrict__ B,
+__global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                                const T* __restrict__ B3, OutT* __restrict__ C,
                                                                int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                                                                const int32_t* __restrict__ offsets,
