@@ -24,7 +24,7 @@ def _rdzv(tmp_path):
     return str(tmp_path / "rendezvous")
 
 
-def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, result_dir):
+def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, result_dir, skew=0.0):
     schedule, *opts = schedule.split("+")
     Ts = list(T) if isinstance(T, (list, tuple)) else [T] * ws     # tokens per rank (ragged)
     T = Ts[rank]
@@ -41,7 +41,9 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     W = (rng.standard_normal((E, d, d)) * 0.1).astype(np.float32)   # nn.Linear [out, in]
     xs = [np.random.default_rng(10 + r).standard_normal((Ts[r], d)).astype(np.float32) for r in range(ws)]
     x = xs[rank]
-    idx, w, _ = O.route(x, gate, k)
+    # skew > 0: every token prefers the experts of rank 0 (the other ranks receive nothing)
+    bias = np.where(np.arange(E) < E // ws, skew, 0.0).astype(np.float32) if skew else None
+    idx, w, _ = O.route(x, gate, k, bias)
     ex = ExpertParallelExchange(E, ws, rank, d, kernels=ep_doubles, chunks=3,
                                 transport="p2p", schedule=schedule, runtime=HostRuntime(f"smoet{zlib.crc32(rdzv.encode()):08x}"))
     ex.return_mode = "copy" if "copy" in opts else "fused"
@@ -73,11 +75,12 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     # a first batch with other routing leaves other rows in every buffer, so a row the
     # checked batch fails to write shows up as a mismatch
     xo = np.random.default_rng(99 + rank).standard_normal((T, d)).astype(np.float32)
-    io, wo, _ = O.route(xo, gate, k)
+    io, wo, _ = O.route(xo, gate, k, bias)
     ex.forward(torch.from_numpy(xo), torch.from_numpy(io), torch.from_numpy(wo), cap, experts, **kw)
     out1 = ex.forward(*args, **kw).numpy().copy()
     out2 = ex.forward(*args, **kw).numpy().copy()      # buffers reused
     p = O.MoEParams(gate=gate, expert_type="linear", expert_w=np.ascontiguousarray(W.transpose(0, 2, 1)))
+    p.logit_bias = bias
     refs, aux = O.moe_forward(xs, p, ws=ws, k=k, capacity=cap, return_aux=True)
     ref = refs[rank] + (shared if shared is not None else 0)
     kept_ref = sum(int(min(cap, c)) if cap > 0 else int(c)
@@ -126,3 +129,15 @@ def _check(tmp_path, ws):
         assert err <= 1e-5, (r, err)
         assert same == 1.0
         assert rows_diff == 0
+
+
+@pytest.mark.parametrize("ws,E,k,cf,schedule,skew", [
+    (2, 8, 2, None, "local_first", 50.0), (4, 8, 2, 0.5, "local_first", 50.0),
+    (4, 16, 4, None, "local_first", 50.0), (4, 8, 8, None, "local_first", 0.0),
+    (2, 8, 8, 1.0, "local_first", 0.0), (4, 8, 2, None, "chunked", 50.0)])
+def test_p2p_schedules_extreme_routing(tmp_path, ws, E, k, cf, schedule, skew):
+    """All tokens routed to one rank's experts (the others compute nothing and receive
+    nothing), and k = E (every token to every expert, every rank once with dedup)."""
+    mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, 12, 23, k, cf, schedule, False, str(tmp_path), skew),
+             nprocs=ws, join=True)
+    _check(tmp_path, ws)
