@@ -291,3 +291,91 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
     if return_aux:
         return results, dict(routed=routed, plan=plan, kept=kept, capacity=cap)
     return results
+
+
+# --------------------------------------------------------------------------- backward
+def _swiglu_backward(xin, w1, w3, w2, dy, acc):
+    """Gradients of ``y = w2(silu(w1 x) * w3 x)`` given dy: (dx, dw1, dw3, dw2)."""
+    w1, w3, w2 = (np.asarray(a, acc) for a in (w1, w3, w2))
+    g = xin @ w1.T
+    u = xin @ w3.T
+    s = 1.0 / (1.0 + np.exp(-g))
+    h = g * s * u
+    dh = dy @ w2
+    dg = dh * u * s * (1.0 + g * (1.0 - s))      # d silu(g) / dg = s (1 + g (1 - s))
+    du = dh * g * s
+    return dg @ w1 + du @ w3, dg.T @ xin, du.T @ xin, dy.T @ h
+
+
+def moe_backward(x: np.ndarray, p: MoEParams, dout: np.ndarray, *, k: int = 2, weighting: str = "post",
+                 capacity_factor: Optional[float] = None, capacity: Optional[int] = None, acc=np.float64):
+    """Gradients of one rank's layer output (``moe_forward`` with ws = 1) for the upstream
+    gradient ``dout`` [T, d]: a dict with ``x``, ``gate`` and the expert weights in
+    ``MoEParams`` layout (``expert_w``, or ``w1, w3, w2``; ``sw1, sw3, sw2`` for the shared
+    expert).  Expert parallelism only moves rows, so the gradients of a multi-rank
+    forward are these, rank by rank, with the capacity of the whole batch.
+
+    The reference is forward-only; its torch ops differentiate as: top-k passes the
+    gradient to the selected logits, ``softmax`` over them (``models/baseline_moe.py:62-65``),
+    the expert ``Linear(x) * w`` (post-weighting, :159-162) or ``(x * w) @ W``
+    (pre-weighting, ``models/ultimate_moe.py:245-249``), the k slots summed in slot order
+    (:188-189).  Dropped slots (capacity) contribute 0 and stay in the softmax, as in the
+    forward.  ``acc`` is the arithmetic precision (float64 by default)."""
+    x = np.asarray(x, acc)
+    dout = np.asarray(dout, acc)
+    T, d = x.shape
+    E = p.num_experts
+    idx, w, _ = route(x.astype(np.float32), p.gate, k, p.logit_bias)
+    cap = capacity if capacity else capacity_for(capacity_factor, T, k, E)
+    plan, _ = dispatch_plan([idx], E, 1, cap)
+    wk = w.astype(acc)
+    dw = np.zeros((T, k), acc)
+    dx = np.zeros((T, d), acc)
+    g = {}
+    if p.expert_type == "linear":
+        g["expert_w"] = np.zeros(p.expert_w.shape, acc)
+    else:
+        for n in ("w1", "w3", "w2"):
+            g[n] = np.zeros(getattr(p, n).shape, acc)
+    for e in range(E):
+        rows = plan[e]
+        if rows.shape[0] == 0:
+            continue
+        ts, js = rows[:, 1], rows[:, 2]
+        xin, go, wts = x[ts], dout[ts], wk[ts, js][:, None]
+        if p.expert_type == "linear":
+            We = np.asarray(p.expert_w[e], acc)           # x @ W layout [d_in, d_out]
+            if weighting == "pre":
+                g["expert_w"][e] += (xin * wts).T @ go
+                dxw = go @ We.T
+                dw[ts, js] = (dxw * xin).sum(1)
+                np.add.at(dx, ts, dxw * wts)
+            else:
+                y = xin @ We
+                dw[ts, js] = (go * y).sum(1)
+                g["expert_w"][e] += xin.T @ (go * wts)
+                np.add.at(dx, ts, (go * wts) @ We.T)
+        else:
+            y = swiglu_expert(xin, p.w1[e], p.w3[e], p.w2[e], acc)
+            dw[ts, js] = (go * y).sum(1)
+            dxe, d1, d3, d2 = _swiglu_backward(xin, p.w1[e], p.w3[e], p.w2[e], go * wts, acc)
+            g["w1"][e] += d1
+            g["w3"][e] += d3
+            g["w2"][e] += d2
+            np.add.at(dx, ts, dxe)
+    # softmax over the k selected logits, then top-k scatters back to the logits
+    dv = wk * (dw - (wk * dw).sum(1, keepdims=True))
+    dlog = np.zeros((T, E), acc)
+    np.add.at(dlog, (np.repeat(np.arange(T), k), idx.reshape(-1)), dv.reshape(-1))
+    gate = np.asarray(p.gate, acc)
+    dx += dlog @ gate
+    g["gate"] = dlog.T @ x
+    if p.sw1 is not None:
+        for n in ("sw1", "sw3", "sw2"):
+            g[n] = np.zeros(getattr(p, n).shape, acc)
+        for s in range(p.sw1.shape[0]):
+            dxs, d1, d3, d2 = _swiglu_backward(x, p.sw1[s], p.sw3[s], p.sw2[s], dout, acc)
+            g["sw1"][s], g["sw3"][s], g["sw2"][s] = d1, d3, d2
+            dx += dxs
+    g["x"] = dx
+    return g

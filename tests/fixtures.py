@@ -64,3 +64,22 @@ def std_swiglu_lowp(name: str):
     p = MoEParams(gate=g, expert_type="swiglu", w1=w1, w3=w3, w2=w2)
     f.update(E=E, d=d, F=F, M=M)
     return f, p
+
+
+GRADS = ["grad_std_linear_fp32_E8_d48_M41", "grad_std_swiglu_fp32_E4_d32_F64_M29",
+         "grad_std_swiglu_fp32_E8_d32_F48_M57"]
+
+
+def std_grads(name: str):
+    """Reference StandardMoE gradients (autograd through its forward, fp32)."""
+    f = load(name)
+    E, d, F, M, seed, swiglu = [int(v) for v in f["meta"]]
+    if swiglu:
+        w1, w3, w2 = synth.swiglu_weights(seed, E, d, F, init="xavier")
+        p = MoEParams(gate=synth.xavier_normal(seed + 5, (E, d)), expert_type="swiglu", w1=w1, w3=w3, w2=w2)
+    else:
+        W = synth.normal(seed + 1, (E, d, d), 0.02)       # nn.Linear weight [out, in]
+        p = MoEParams(gate=synth.normal(seed, (E, d), 0.02), expert_type="linear",
+                      expert_w=np.ascontiguousarray(W.transpose(0, 2, 1)))
+    f.update(E=E, d=d, F=F, M=M)
+    return f, p

@@ -2,7 +2,8 @@
 
 Run from the repository root in a container where the reference checkout exists:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py /root/reference          # every fixture
+    python tests/golden/make_golden.py /root/reference grads    # gradient fixtures only
 
 It imports ``models.baseline_moe.StandardMoE`` and ``models.ultimate_moe.UltimateMoE``
 from that checkout, loads seeded weights into them through their own parameter names,
@@ -169,7 +170,40 @@ def topk_ties(torch, name, seed):
     np.savez_compressed(HERE / f"{name}.npz", **cases)
 
 
-def main(ref: str):
+def standard_grads(torch, nn, StandardMoE, name, kind, E, d, F, M, seed):
+    """Gradients of the reference's StandardMoE (fp32, no process group) for a seeded
+    upstream gradient: its forward is torch ops end to end, so autograd differentiates
+    the reference's own route / dispatch / combine code (the reference itself is
+    forward-only).  ``kind`` "linear" or "swiglu" (SwiGLU modules substituted)."""
+    m = StandardMoE(num_experts=E, d_model=d, use_fp16=False)
+    if kind == "linear":
+        g = synth.normal(seed, (E, d), 0.02)
+        W = synth.normal(seed + 1, (E, d, d), 0.02)
+        with torch.no_grad():
+            for i in range(E):
+                m.experts[i].weight.copy_(torch.from_numpy(W[i]))
+    else:
+        w1, w3, w2 = synth.swiglu_weights(seed, E, d, F, init="xavier")
+        g = synth.xavier_normal(seed + 5, (E, d))
+        m.experts = nn.ModuleList([_swiglu_module(torch, nn, w1[i], w3[i], w2[i]) for i in range(E)])
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy(g))
+    x = synth.normal(seed + 2, (M, d), 1.0)
+    dout = synth.normal(seed + 3, (M, d), 1.0)
+    xt = torch.from_numpy(x).requires_grad_(True)
+    out = m(xt)
+    out.backward(torch.from_numpy(dout))
+    grads = dict(dx=xt.grad.numpy(), dgate=m.gate.weight.grad.numpy())
+    if kind == "linear":
+        grads["dexpert"] = np.stack([m.experts[i].weight.grad.numpy() for i in range(E)])   # [out, in]
+    else:
+        for n in ("w1", "w3", "w2"):
+            grads["d" + n] = np.stack([getattr(m.experts[i], n).weight.grad.numpy() for i in range(E)])
+    np.savez_compressed(HERE / f"{name}.npz", x=x, dout=dout, out=out.detach().numpy(),
+                        meta=np.array([E, d, F, M, seed, int(kind == "swiglu")]), **grads)
+
+
+def main(ref: str, only=None):
     sys.path.insert(0, ref)
     import warnings
     warnings.simplefilter("ignore")
@@ -178,6 +212,9 @@ def main(ref: str):
     torch.set_num_threads(4)
     from models.baseline_moe import StandardMoE
 
+    if only == "grads":
+        grads_fixtures(torch, nn, StandardMoE)
+        return
     standard_linear(torch, StandardMoE, "std_linear_fp32_E8_d64_M37", 8, 64, 37, 11)
     standard_linear(torch, StandardMoE, "std_linear_fp32_E16_d128_M1", 16, 128, 1, 12)
     standard_linear(torch, StandardMoE, "std_linear_fp32_E8_d64_M0", 8, 64, 0, 13)
@@ -196,8 +233,16 @@ def main(ref: str):
     ultimate_linear("ult_linear_fp32_ws2_E8_d32_M23", ref, 8, 32, 23, 32, 2)
     ultimate_linear("ult_linear_fp32_ws4_E8_d32_M17", ref, 8, 32, 17, 33, 4)
     topk_ties(torch, "topk_ties", 41)
+    grads_fixtures(torch, nn, StandardMoE)
     print("fixtures written to", HERE)
 
 
+def grads_fixtures(torch, nn, StandardMoE):
+    standard_grads(torch, nn, StandardMoE, "grad_std_linear_fp32_E8_d48_M41", "linear", 8, 48, 0, 41, 61)
+    standard_grads(torch, nn, StandardMoE, "grad_std_swiglu_fp32_E4_d32_F64_M29", "swiglu", 4, 32, 64, 29, 62)
+    standard_grads(torch, nn, StandardMoE, "grad_std_swiglu_fp32_E8_d32_F48_M57", "swiglu", 8, 32, 48, 57, 63)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # python tests/golden/make_golden.py [reference checkout] [grads]
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2] if len(sys.argv) > 2 else None)
