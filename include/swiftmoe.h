@@ -54,6 +54,13 @@ SMOE_API int smoe_device_sm_count(void);
 /* Read and clear the device-side error word set by bounded waits inside kernels.
  * Synchronises the stream.  *flag receives 0 when no wait timed out. */
 SMOE_API int smoe_read_device_error(int* flag, smoe_stream_t stream);
+/* Self-test of the give-up path every bounded device wait of this library takes: one
+ * thread waits on a shared-memory mbarrier that nothing arrives at, with a time limit
+ * of limit_ns (0 < limit_ns <= 1 s) instead of the kernels' 2 s.  When the limit runs
+ * out the wait returns, the kernel stores 1 in *gave_up (device int) and records the
+ * timeout in the error word (smoe_read_device_error then reports 1), and the context
+ * stays usable.  No counterpart in the reference (its kernels have no bounded waits). */
+SMOE_API int smoe_selftest_wait_timeout(uint64_t limit_ns, int* gave_up, smoe_stream_t stream);
 
 /* ------------------------------------------------------------------------------ router
  * logits[t,e] = sum_i x[t,i] * wg[e,i] (+ logit_bias[e]) accumulated in fp32; top-k over

@@ -226,7 +226,7 @@ class MoEParams:
 def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int = 2,
                 weighting: str = "post", capacity_factor: Optional[float] = None,
                 acc=np.float32, round_hidden=None, return_aux: bool = False,
-                capacity: Optional[int] = None):
+                capacity: Optional[int] = None, routing=None):
     """Full layer forward for ``ws`` ranks; ``xs[r]`` is rank r's [T_r, d] input.
 
     Control flow follows ``StandardMoE.forward`` (``models/baseline_moe.py:191-213``):
@@ -240,12 +240,19 @@ def moe_forward(xs: Sequence[np.ndarray], p: MoEParams, *, ws: int = 1, k: int =
     stores: the SwiGLU hidden activation and each expert's output before weighting.
     ``capacity`` (rows per expert, > 0) overrides the one derived from
     ``capacity_factor``, e.g. for ranks with unequal batches.
+    ``routing`` (optional): per rank, the (idx [T,k], w [T,k]) to use instead of this
+    restatement's own router -- e.g. the routing a device computed, so that dispatch,
+    capacity cut, experts and combine are checked on exactly its decisions.
     """
     E = p.num_experts
     if E % ws:
         raise ValueError("num_experts must be divisible by world size")
     routed = []
-    for x in xs:
+    for r, x in enumerate(xs):
+        if routing is not None:
+            idx, w = routing[r]
+            routed.append((np.asarray(idx, np.int64), np.asarray(w, np.float32), None))
+            continue
         idx, w, lg = route(x, p.gate, k, p.logit_bias)
         routed.append((idx, w, lg))
     t_glob = sum(x.shape[0] for x in xs)

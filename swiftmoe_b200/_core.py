@@ -25,6 +25,8 @@ from . import _lib as L
 from . import kernels as K
 
 STAGES = ("Router", "Dispatch_Comm", "Expert_Compute", "Combine_Comm")
+# The reference's profile_data keys (models/ultimate_moe.py:211-216), in STAGES order.
+DATA_KEYS = ("router", "dispatch", "compute", "combine")
 
 
 def resolve_dtype(use_fp16: bool, dtype) -> torch.dtype:
@@ -46,13 +48,25 @@ def capacity_rows(capacity_factor: Optional[float], tokens_per_rank: int, world_
     return int(math.ceil(capacity_factor * tokens_per_rank * world_size * k / num_experts))
 
 
+def exposed_span(name: str) -> bool:
+    """Whether the compute stream is idle for communication from the stage mark ``name``
+    to the next mark: the count exchange, a wait on an exchange event ("wait_*_before"),
+    or a host wait on the exchange ("host_wait", which also covers the host's
+    bookkeeping until the next mark)."""
+    return name == "counts_start" or name == "host_wait" or (name.startswith("wait_") and name.endswith("_before"))
+
+
 class _StageTimer:
-    """CUDA-event stage timing without host synchronisation inside forward."""
+    """CUDA-event stage timing without host synchronisation inside forward.
+
+    ``data`` holds, per forward, milliseconds under the reference's keys ``router``,
+    ``dispatch``, ``compute`` and ``combine`` (models/ultimate_moe.py:211-216) plus
+    ``exposed_a2a``: the time the compute stream sat idle waiting for the exchange."""
 
     def __init__(self):
         self.pending: List[tuple] = []
-        self.data: Dict[str, List[float]] = {s: [] for s in STAGES}
-        self.data["Exposed_A2A"] = []
+        self.data: Dict[str, List[float]] = {s: [] for s in DATA_KEYS}
+        self.data["exposed_a2a"] = []
         self.spans: Dict[str, List[float]] = {}   # expert-parallel forward: mark -> next mark
 
     def mark(self, device) -> torch.cuda.Event:
@@ -60,45 +74,35 @@ class _StageTimer:
         ev.record(torch.cuda.current_stream(device))
         return ev
 
-    def add(self, events: List[torch.cuda.Event], exposed_a2a: Optional[tuple] = None):
-        self.pending.append(("torch", events, exposed_a2a))
-
     def add_marks(self, marks: List[tuple]):
-        """(name, event) marks of an expert-parallel forward (see ep.ExpertParallelExchange)."""
-        self.pending.append(("marks", marks, None))
+        """(name, event) marks of a stage-by-stage forward (see ep.ExpertParallelExchange)."""
+        self.pending.append(("marks", marks))
 
     def add_library(self, ev: "L.StageEvents"):
         """Events recorded inside smoe_layer_fwd: start, router, dispatch, gemm1, gemm2, combine."""
-        self.pending.append(("lib", ev, None))
+        self.pending.append(("lib", ev))
 
     def flush(self):
-        for kind, events, a2a in self.pending:
+        for kind, events in self.pending:
             if kind == "marks":
                 ev = dict(events)
                 events[-1][1].synchronize()
                 span = lambda a, b: ev[a].elapsed_time(ev[b])
                 names = [n for n, _ in events]
-                self.data["Router"].append(span("start", "router"))
-                self.data["Dispatch_Comm"].append(span("router", "counts_done"))
-                self.data["Expert_Compute"].append(sum(span(n, n[:-len("_start")] + "_end") for n in names
-                                                       if n.startswith("experts") and n.endswith("_start")))
-                self.data["Combine_Comm"].append(span("combine_start", "end"))
-                exposed = span("counts_start", "counts_done") + sum(
-                    span(n, n.replace("_before", "_after")) for n in names if n.endswith("_before"))
-                self.data["Exposed_A2A"].append(exposed)
+                self.data["router"].append(span("start", "router"))
+                self.data["dispatch"].append(span("router", "counts_done"))
+                self.data["compute"].append(sum(span(n, n[:-len("_start")] + "_end") for n in names
+                                                if n.startswith("experts") and n.endswith("_start")))
+                self.data["combine"].append(span("combine_start", "end"))
+                self.data["exposed_a2a"].append(sum(ea.elapsed_time(eb) for (a, ea), (_, eb)
+                                                    in zip(events[:-1], events[1:]) if exposed_span(a)))
                 for (a, ea), (b, eb) in zip(events[:-1], events[1:]):
                     self.spans.setdefault(f"{a}>{b}", []).append(ea.elapsed_time(eb))
                 continue
-            if kind == "lib":
-                spans = [(0, 1), (1, 2), (2, 4), (4, 5)]
-                for name, (i, j) in zip(STAGES, spans):
-                    self.data[name].append(events.elapsed(i, j))
-                continue
-            events[-1].synchronize()
-            for name, a, b in zip(STAGES, events[:-1], events[1:]):
-                self.data[name].append(a.elapsed_time(b))
-            if a2a is not None:
-                self.data["Exposed_A2A"].append(sum(s.elapsed_time(e) for s, e in a2a))
+            spans = [(0, 1), (1, 2), (2, 4), (4, 5)]
+            for key, (i, j) in zip(DATA_KEYS, spans):
+                self.data[key].append(events.elapsed(i, j))
+            self.data["exposed_a2a"].append(0.0)
         self.pending.clear()
 
 
@@ -288,11 +292,14 @@ class MoECore(nn.Module):
 
     # ------------------------------------------------------------ profiling API
     def get_profile_summary(self) -> Dict[str, float]:
-        """Mean milliseconds per stage (models/ultimate_moe.py:344-352) + Exposed_A2A."""
+        """Mean milliseconds per stage under the reference's summary keys
+        (models/ultimate_moe.py:344-352), plus ``Exposed_A2A``: the mean time per forward
+        the compute stream waited for the expert-parallel exchange (counted from the
+        stage marks, including host waits; 0 at world size 1)."""
         self._timer.flush()
-        out = {}
-        for k_, v in self._timer.data.items():
-            out[k_] = float(sum(v) / len(v)) if v else 0.0
+        mean = lambda v: float(sum(v) / len(v)) if v else 0.0
+        out = {name: mean(self._timer.data[key]) for name, key in zip(STAGES, DATA_KEYS)}
+        out["Exposed_A2A"] = mean(self._timer.data["exposed_a2a"])
         return out
 
     def get_profile_spans(self) -> Dict[str, float]:
@@ -309,6 +316,9 @@ class MoECore(nn.Module):
         self._timer.spans.clear()
 
     @property
-    def profile_data(self):
+    def profile_data(self) -> Dict[str, List[float]]:
+        """Per-forward stage milliseconds under the reference's keys ``router``,
+        ``dispatch``, ``compute``, ``combine`` (models/ultimate_moe.py:211-216), plus
+        ``exposed_a2a``.  Reading it waits for the recorded forwards to finish."""
         self._timer.flush()
         return self._timer.data

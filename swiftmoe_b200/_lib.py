@@ -43,6 +43,7 @@ SIGNATURES = {
     "smoe_status_string": (C.c_char_p, [_i32]),
     "smoe_device_sm_count": (_i32, []),
     "smoe_read_device_error": (_i32, [C.POINTER(C.c_int), _vp]),
+    "smoe_selftest_wait_timeout": (_i32, [C.c_uint64, _vp, _vp]),
     "smoe_router_fwd": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "smoe_router_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "smoe_topk_from_logits": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _vp]),

@@ -2,9 +2,10 @@
 
 Keeps the reference constructor, the ``gate`` / ``experts[i]`` ``nn.Linear`` parameters
 (so reference state_dicts load unchanged) and the private stage methods
-``_route_tokens`` / ``_dispatch_tokens`` / ``_expert_forward`` / ``_combine_tokens``.
-``forward`` runs the fused sm_100a path.  Gate weights are applied after the expert
-(post-weighting, models/baseline_moe.py:162) by the combine kernel.
+``_route_tokens`` / ``_dispatch_tokens`` / ``_expert_forward`` / ``_combine_tokens``,
+which chained as the reference's ``forward`` chains them compute the same output as
+``forward`` bit for bit.  ``forward`` runs the fused sm_100a path.  Gate weights are
+applied after the expert (post-weighting, models/baseline_moe.py:162).
 """
 from __future__ import annotations
 
@@ -15,6 +16,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from . import kernels as K
+from . import stages
 from ._core import MoECore, resolve_dtype
 from .ep import ExpertParallelExchange
 
@@ -105,40 +107,29 @@ class StandardMoE(MoECore):
         s = self.shared_expert
         return s.w1.weight, s.w3.weight, s.w2.weight
 
-    # ---- the reference's stage methods (models/baseline_moe.py:56-189)
+    # ---- the reference's stage methods (models/baseline_moe.py:56-189), chained by
+    # forward in the reference (:191-213); see stages.py for their contract
     def _route_tokens(self, x: torch.Tensor):
-        """(top-k expert indices [M,k] int64, softmax weights [M,k] in x.dtype)."""
+        """(top-k expert indices [M,k] int64, softmax weights [M,k] float32)."""
         x = self._prepare_input(x)
         idx, w = K.router(x, self._gate(), self.top_k, self._logit_bias())
-        return idx.long(), w.to(x.dtype)
+        return idx.long(), w
 
     def _dispatch_tokens(self, x: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor):
-        """Rows grouped by local expert.  Returns (rows, expert offsets, fp32 weights,
-        send split list, recv split list, exchange state)."""
+        """(recv_x [R,d] grouped by local expert, recv_idx [R] local expert of each row,
+        recv_weights [R,1] float32, send_list, recv_list, state for _combine_tokens)."""
         x = self._prepare_input(x)
-        T = x.shape[0]
-        idx = indices.to(torch.int32).contiguous()
-        w = weights.float().contiguous()
-        cap = self._capacity(T)
-        if self.ws == 1:
-            plan = K.dispatch_plan(idx, self.num_experts, cap)
-            rows = K.permute_rows(x, plan["row_token"], plan["offsets"], plan["rows_cap"])
-            return rows, plan["offsets"], w, [T * self.top_k], [T * self.top_k], plan
-        rows, offsets, st = self.comm.dispatch(x, idx, cap)
-        return rows, offsets, w, st.send_splits, st.recv_splits, st
+        return stages.dispatch(x, indices, weights, self.num_experts, self._capacity(x.shape[0]),
+                               self.comm if self.ws > 1 else None, shared=self._shared_out(x))
 
-    def _expert_forward(self, recv_x: torch.Tensor, recv_idx: torch.Tensor, recv_weights=None):
-        """Expert outputs for rows grouped by local expert (``recv_idx`` = the expert
-        offsets returned by ``_dispatch_tokens``); weighting happens in combine."""
-        return self._experts(recv_x, recv_idx)
+    def _expert_forward(self, recv_x: torch.Tensor, recv_idx: torch.Tensor, recv_weights: torch.Tensor):
+        """Expert outputs times their gate weights (post-weighting, :155-162), float32."""
+        return stages.expert_rows(self._experts, self.exp_per_rank, recv_x, recv_idx, recv_weights)
 
-    def _combine_tokens(self, expert_output, send_list, recv_list, reverse_indices, original_batch_size,
-                        weights=None, x=None):
-        T = original_batch_size
-        shared = self._shared_out(x) if (x is not None and self.num_shared_experts) else None
-        if self.ws == 1:
-            return K.combine(expert_output, reverse_indices["slot_row"], weights, T, self.top_k, shared=shared)
-        return self.comm.combine(expert_output, reverse_indices, weights, shared=shared)
+    def _combine_tokens(self, expert_output, send_list, recv_list, reverse_indices, original_batch_size):
+        """Back to the source ranks, k slots summed in slot order: [M, d] in x.dtype."""
+        return stages.combine(expert_output, reverse_indices, original_batch_size,
+                              self.comm if self.ws > 1 else None)
 
 
 BaselineMoE = StandardMoE

@@ -387,6 +387,24 @@ __global__ void __launch_bounds__(256) router_logits_generic_kernel(const T* __r
   }
 }
 
+// Self-test of the bounded wait: one thread waits for phase 0 of an mbarrier that
+// expects one arrival and gets none, giving up after limit_ns.  *gave_up = 1 when the
+// wait returned without the phase completing (the normal outcome).
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int* gave_up) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_word;
+  if (threadIdx.x == 0) {
+    abort_word = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool completed = mbar_wait(smem_u32(&bar), 0, &abort_word, limit_ns);
+    *gave_up = completed ? 0 : 1;
+  }
+}
+
 }  // namespace
 
 // =============================================================================== C ABI
@@ -417,6 +435,13 @@ int smoe_read_device_error(int* flag, smoe_stream_t stream) {
   const int zero = 0;
   SMOE_CK(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
   *flag = v;
+  return SMOE_OK;
+}
+
+int smoe_selftest_wait_timeout(uint64_t limit_ns, int* gave_up, smoe_stream_t stream) {
+  if (!gave_up || limit_ns == 0 || limit_ns > 1000000000ull) return SMOE_ERR_INVALID;
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns, gave_up);
+  SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
 

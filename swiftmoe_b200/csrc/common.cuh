@@ -142,7 +142,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // a shared-memory word of this launch), and returns false.  A timeout also records
 // kErrWaitTimeout in the global error word for the host; that word is only reported,
 // never consulted, so an old error cannot make later launches skip work.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* cta_abort) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* cta_abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
 #pragma unroll 1
   for (int i = 0; i < 256; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -151,7 +152,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*cta_abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *cta_abort = 1;
       set_device_error(kErrWaitTimeout);
       return false;

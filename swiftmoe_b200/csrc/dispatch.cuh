@@ -198,6 +198,10 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const unsigned char* 
 }
 
 // out[t, c..c+VEC) = sum_j w[t,j] * y[slot_row[t,j], c..] (+ shared[t, c..]).
+// Each product is rounded to fp32 before it is added (no fused multiply-add), in slot
+// order: the same arithmetic as weighting the expert rows first and summing the k
+// weighted fp32 rows afterwards, which is how the stage-by-stage API (expert outputs
+// weighted in _expert_forward, slots summed in _combine_tokens) computes the layer.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ slot_row,
                                                       const float* __restrict__ w, int T_, int k, int d,
@@ -217,13 +221,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, c
       float v[VEC];
       load_vec_f<T, VEC>(y + (size_t)r * d + c, v);
 #pragma unroll
-      for (int q = 0; q < VEC; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+      for (int q = 0; q < VEC; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(wj, v[q]));
     }
     if (shared != nullptr) {
       float v[VEC];
       load_vec_f<T, VEC>(shared + (size_t)t * d + c, v);
 #pragma unroll
-      for (int q = 0; q < VEC; ++q) acc[q] += v[q];
+      for (int q = 0; q < VEC; ++q) acc[q] = __fadd_rn(acc[q], v[q]);
     }
     if constexpr (VEC == 1) {
       out[(size_t)t * d + c] = Num<T>::from_f(acc[0]);

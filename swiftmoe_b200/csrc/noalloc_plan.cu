@@ -23,6 +23,9 @@ namespace noalloc {
 constexpr int kMaxSlots = SMOE_NOALLOC_PLAN_MAX_SLOTS;     // T * k
 constexpr int kMaxExperts = SMOE_NOALLOC_PLAN_MAX_EXPERTS;  // E
 constexpr int kMaxBlocks = kMaxSlots / kPlanChunk;          // plan blocks at most
+// A call at the slot limit launches cdiv(kMaxSlots, kPlanChunk) plan blocks; the scratch
+// holds histograms for kMaxBlocks of them, so the limit must be a whole number of chunks.
+static_assert(kMaxSlots % kPlanChunk == 0, "SMOE_NOALLOC_PLAN_MAX_SLOTS must be a multiple of the plan chunk");
 constexpr size_t kWords = 2ull * kMaxBlocks * kMaxExperts;  // hist + base
 
 // The scratch: [0, kMaxBlocks*kMaxExperts) histograms, then the per-block bases.

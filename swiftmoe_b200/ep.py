@@ -171,6 +171,15 @@ class ExpertParallelExchange:
     def last_rows(self, v: int):
         self._last_rows, self._rows_dev = int(v), None
 
+    def describe(self) -> str:
+        """The exchange configuration in words (benchmark records)."""
+        if self.transport == "collective":
+            return f"collective transport (all_to_all_single), {self.chunks} token chunks"
+        if self.schedule == "chunked":
+            return f"{self.transport} transport, chunked schedule, {self.chunks} token chunks"
+        return (f"{self.transport} transport, local_first schedule, {self.return_mode} return, "
+                f"token dedup {self.dedup}, own rows split from {self.split_min_ws} ranks")
+
     def n_chunks(self, T: int) -> int:
         """Token chunks of the chunked schedules: the same on every rank (the ranks'
         batches may differ in size), so it does not depend on T."""
@@ -476,6 +485,7 @@ class ExpertParallelExchange:
         y_a = experts(send, starts, ends=mids)
         mark("experts_selfA_end")
         ev_a = rt.record(comp)
+        mark("host_wait")       # the compute stream idles from here until the host enqueues again
         rt.host_wait(ev_counts)
         Gh = self._host[:ws * E].numpy().reshape(ws, ws, El).astype(np.int64)   # [src, dst, El]
         R = Gh.sum(2)                                  # slots src -> dst
@@ -635,6 +645,7 @@ class ExpertParallelExchange:
         mark("experts_selfA_end")
         part_own = self.k.combine(yo, oplan["slot_row"], meta_w[:T], T, k)
         ev_a = rt.record(comp)
+        mark("host_wait")
         rt.host_wait(ev_counts)
         Gc = self._host[:ws * ws].numpy().reshape(ws, ws).astype(np.int64)
         ex = np.cumsum(Gc, 1) - Gc
@@ -703,9 +714,15 @@ class ExpertParallelExchange:
             self._bufs = None
 
     # ------------------------------------------------------------------ stage API
-    def dispatch(self, x: torch.Tensor, idx: torch.Tensor, capacity: int = 0):
+    def dispatch(self, x: torch.Tensor, idx: torch.Tensor, capacity: int = 0,
+                 slot_payload: Optional[torch.Tensor] = None):
         """Unchunked dispatch for the stage-by-stage API (StandardMoE._dispatch_tokens):
-        returns (rows grouped by local expert, expert offsets [E_l+1], state)."""
+        returns (rows grouped by local expert, expert offsets [E_l+1], state).
+
+        ``slot_payload`` (optional, float32 [T, k]: one value per (token, slot), e.g. the
+        gate weights): travels with the rows, as the reference sends its weights next to
+        its rows (models/baseline_moe.py:131-133); returned as a fourth value, one entry
+        per returned row."""
         ws, El = self.world_size, self.exp_per_rank
         T, k = idx.shape
         plan = self.k.dispatch_plan(idx, self.num_experts)
@@ -721,7 +738,18 @@ class ExpertParallelExchange:
         dist.all_to_all_single(recv_rows[:n_recv], send_rows[:n_send], recv_splits, send_splits, group=self.group)
         rg = self.k.ep_regroup_plan(recv_counts.view(ws, El), capacity, n_recv)
         xe = self.k.permute_rows(recv_rows, rg["row_src"], rg["offsets"], rg["rows_cap"])
-        return xe, rg["offsets"], DispatchState(plan, rg, send_splits, recv_splits, n_send, n_recv, T, k)
+        st = DispatchState(plan, rg, send_splits, recv_splits, n_send, n_recv, T, k)
+        if slot_payload is None:
+            return xe, rg["offsets"], st
+        # payload of every send row: the value of the (token, slot) that row holds
+        flat = slot_payload.reshape(-1).float()
+        sr = plan["slot_row"].reshape(-1).long()
+        send_p = torch.zeros(n_send + 1, dtype=torch.float32, device=x.device)   # last: spare for skipped slots
+        send_p.scatter_(0, torch.where(sr >= 0, sr, torch.full_like(sr, n_send)), flat)
+        recv_p = torch.empty(max(n_recv, 1), dtype=torch.float32, device=x.device)
+        dist.all_to_all_single(recv_p[:n_recv], send_p[:n_send], recv_splits, send_splits, group=self.group)
+        pe = self.k.gather_rows(recv_p.view(-1, 1), rg["row_src"], rg["rows_cap"])
+        return xe, rg["offsets"], st, pe.view(-1)
 
     def combine(self, y: torch.Tensor, st: DispatchState, w: torch.Tensor,
                 shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):

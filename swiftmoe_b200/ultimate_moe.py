@@ -15,21 +15,31 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from . import kernels as K
+from . import stages
 from ._core import MoECore, resolve_dtype
 from .ep import ExpertParallelExchange
 
 
 def setup_nccl_optimizations():
-    """Default NCCL settings for one NVLink/NVSwitch node (models/ultimate_moe.py:15-31).
+    """The reference's NCCL settings (models/ultimate_moe.py:15-31), with one left out.
+
+    Same values as the reference for NCCL_IB_DISABLE, NCCL_P2P_LEVEL,
+    NCCL_NET_GDR_LEVEL, NCCL_MIN_NCHANNELS, NCCL_BUFFSIZE and NCCL_NTHREADS.
+    NCCL_SOCKET_IFNAME=eth0 is not set: it names a host interface, and on a machine
+    whose interface has another name NCCL's bootstrap cannot find it and the group fails
+    to form; NCCL's own interface choice works on every host.
 
     Only variables that are not already set are written.  They take effect for process
     groups created AFTER this call (the reference calls it from the layer constructor,
-    after the group exists, where it has no effect)."""
+    after the group exists, where it has no effect); ``init_expert_parallel`` applies
+    them before it creates the group."""
     nccl_config = {
+        "NCCL_IB_DISABLE": "0",
         "NCCL_P2P_LEVEL": "NVL",
         "NCCL_NET_GDR_LEVEL": "5",
-        "NCCL_MIN_NCHANNELS": "16",
-        "NCCL_BUFFSIZE": "8388608",
+        "NCCL_MIN_NCHANNELS": "12",
+        "NCCL_BUFFSIZE": "4194304",
+        "NCCL_NTHREADS": "512",
     }
     for key, value in nccl_config.items():
         if key not in os.environ:
@@ -100,6 +110,14 @@ class UltimateMoE(MoECore):
         """Per-expert offsets added to the router logits before top-k (extension)."""
         self.logit_bias = None if bias is None else bias.detach().float().to(self.gate_weight.device).contiguous()
 
+    def _expert_compute(self, recv_x: torch.Tensor, recv_idx: torch.Tensor, recv_w: torch.Tensor):
+        """Expert stage of the reference's forward (models/ultimate_moe.py:222-252): the
+        received rows (any order) through their local experts, each weighted by its gate
+        weight.  The weight scales the expert's output in float32 (the reference scales
+        its input, which is the same for a linear expert up to rounding), and the rows
+        come back in float32 so that MoEAsyncCommHandler.combine rounds once."""
+        return stages.expert_rows(self._experts, self.exp_per_rank, recv_x, recv_idx, recv_w)
+
     # accessors
     def _gate(self):
         return self.gate_weight
@@ -117,5 +135,5 @@ class UltimateMoE(MoECore):
         return self.shared_w1, self.shared_w3, self.shared_w2
 
 
-# The reference's exchange class name, kept for callers that import it.
-MoEAsyncCommHandler = ExpertParallelExchange
+# The reference's exchange class, with its constructor and dispatch / combine signatures.
+MoEAsyncCommHandler = stages.MoEAsyncCommHandler

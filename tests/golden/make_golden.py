@@ -244,5 +244,7 @@ def grads_fixtures(torch, nn, StandardMoE):
 
 
 if __name__ == "__main__":
-    # python tests/golden/make_golden.py [reference checkout] [grads]
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2] if len(sys.argv) > 2 else None)
+    # python tests/golden/make_golden.py <path of the reference checkout> [grads]
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_golden.py <path of the SwiftMoE reference checkout> [grads]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

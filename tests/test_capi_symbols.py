@@ -53,6 +53,8 @@ def test_invalid_arguments_rejected_before_any_device_call(lib):
     assert lib.smoe_topk_from_logits(None, 10, 64, 33, None, None, None) == -1
     assert lib.smoe_grouped_gemm(None, None, None, None, 2, 2, 0, None, None, 1, 10, 8, 8, None) == -1
     assert lib.smoe_combine(None, 9, None, None, 1, 2, 8, None, None, None) == -1
+    assert lib.smoe_selftest_wait_timeout(0, None, None) == -1               # no limit
+    assert lib.smoe_selftest_wait_timeout(2_000_000_000, None, None) == -1   # above 1 s
     a = _lib.LayerArgs()
     a.tokens, a.d_model, a.num_experts, a.top_k, a.dtype = 10, 64, 8, 9, 2
     assert lib.smoe_layer_fwd(C.byref(a), None) == -1

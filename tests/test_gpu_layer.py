@@ -147,18 +147,65 @@ def test_profiling_summary(M):
     torch.testing.assert_close(m(x), out, rtol=0, atol=0)   # staged == fused, bit for bit
 
 
-def test_staged_private_methods_match_forward(M):
+def _reference_chain(m, x):
+    """The stage calls of the reference's StandardMoE.forward (models/baseline_moe.py:191-213),
+    in its order and with its argument passing, over this library's module."""
+    indices, weights = m._route_tokens(x)
+    recv_x, recv_idx, recv_weights, send_list, recv_list, rev_idx = m._dispatch_tokens(x, indices, weights)
+    expert_output = m._expert_forward(recv_x, recv_idx, recv_weights)
+    return m._combine_tokens(expert_output, send_list, recv_list, rev_idx, x.shape[0])
+
+
+@pytest.mark.parametrize("dtype,kw", [
+    (torch.bfloat16, {}), (torch.float32, {}),
+    (torch.bfloat16, dict(expert_type="swiglu", d_ff=256)),
+    (torch.bfloat16, dict(expert_type="swiglu", d_ff=256, capacity_factor=0.6, num_shared_experts=1)),
+    (torch.float16, dict(top_k=3))])
+def test_reference_stage_chain_matches_forward(M, dtype, kw):
+    """StandardMoE's private stages chained as the reference's forward chains them give
+    forward's output bit for bit (the weights travel through _dispatch_tokens' third
+    return value into _expert_forward, as in the reference)."""
+    m = M.StandardMoE(8, 128, use_fp16=False, dtype=dtype, **kw).cuda()
+    x = torch.randn(77, 128, device="cuda", dtype=dtype)
+    idx, w = m._route_tokens(x)
+    assert idx.dtype == torch.int64 and w.dtype == torch.float32
+    recv_x, recv_idx, recv_w, s_list, r_list, _ = m._dispatch_tokens(x, idx, w)
+    assert recv_x.shape[0] == recv_idx.shape[0] == recv_w.shape[0] == s_list[0] == r_list[0]
+    assert recv_w.shape[1] == 1 and int(recv_idx.min()) >= 0 and int(recv_idx.max()) < 8
+    torch.testing.assert_close(_reference_chain(m, x), m(x), rtol=0, atol=0)
+
+
+def test_expert_stage_accepts_any_row_order(M):
+    """_expert_forward groups the rows itself: permuting its input rows permutes its output."""
+    m = M.StandardMoE(8, 128, use_fp16=False, dtype=torch.bfloat16, expert_type="swiglu", d_ff=256).cuda()
+    x = torch.randn(50, 128, device="cuda", dtype=torch.bfloat16)
+    idx, w = m._route_tokens(x)
+    rx, ri, rw, *_ = m._dispatch_tokens(x, idx, w)
+    perm = torch.randperm(rx.shape[0], device="cuda")
+    y = m._expert_forward(rx, ri, rw)
+    yp = m._expert_forward(rx[perm].contiguous(), ri[perm], rw[perm])
+    torch.testing.assert_close(yp, y[perm], rtol=0, atol=0)
+
+
+def test_ultimate_reference_chain_with_comm_handler(M):
+    """UltimateMoE's forward stages (models/ultimate_moe.py:301-338): the reference's
+    MoEAsyncCommHandler constructor and dispatch / combine signatures around
+    _expert_compute reproduce forward bit for bit; profile_data has the reference's keys."""
+    m = M.UltimateMoE(8, 128, use_fp16=False, dtype=torch.bfloat16, enable_profiling=True).cuda()
+    x = torch.randn(64, 128, device="cuda", dtype=torch.bfloat16)
+    comm = M.MoEAsyncCommHandler(8, 1, 128, "cuda:0")
     from swiftmoe_b200 import kernels
-    m = M.StandardMoE(8, 128, use_fp16=False, dtype=torch.bfloat16).cuda()
-    x = torch.randn(77, 128, device="cuda", dtype=torch.bfloat16)
-    idx, w = m._route_tokens(x)          # reference types: int64 indices, weights in x.dtype
-    assert idx.dtype == torch.int64 and w.dtype == torch.bfloat16
-    idx32, w32 = kernels.router(x, m.gate.weight, 2)
-    assert torch.equal(idx, idx32.long())
-    rows, offs, wf, s, r_, plan = m._dispatch_tokens(x, idx, w32)
-    y = m._expert_forward(rows, offs)
-    out = m._combine_tokens(y, s, r_, plan, x.shape[0], weights=wf)
-    torch.testing.assert_close(out, m(x), rtol=0, atol=0)   # same kernels, same bits
+    idx32, w32 = kernels.router(x, m.gate_weight, 2)
+    target_ranks, local_idx = idx32 // m.exp_per_rank, idx32 % m.exp_per_rank
+    recv_x, recv_idx, recv_w, s_list, r_list, rev = comm.dispatch(x, idx32, w32, target_ranks.view(-1),
+                                                                  local_idx.view(-1))
+    expert_out = m._expert_compute(recv_x, recv_idx, recv_w)
+    out = comm.combine(expert_out, s_list, r_list, rev, x.shape[0])
+    torch.testing.assert_close(out, m(x), rtol=0, atol=0)
+    assert set(m.profile_data) >= {"router", "dispatch", "compute", "combine"}
+    assert len(m.profile_data["router"]) == 1
+    m.reset_profiling()
+    assert all(len(v) == 0 for v in m.profile_data.values())
 
 
 def test_bf16_layer_vs_reference_bf16_output(M):

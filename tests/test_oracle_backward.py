@@ -42,14 +42,23 @@ def _torch_layer(x, p, k, idx, keep, weighting, dout):
     params = {}
     if p.expert_type == "linear":
         params["expert_w"] = t(p.expert_w)
-        Y = torch.stack([X @ params["expert_w"][e] for e in range(p.num_experts)])
+        expert = lambda e, inp: inp @ params["expert_w"][e]
     else:
         for n in ("w1", "w3", "w2"):
             params[n] = t(getattr(p, n))
-        Y = torch.stack([torch.nn.functional.silu(X @ params["w1"][e].T) * (X @ params["w3"][e].T)
-                         @ params["w2"][e].T for e in range(p.num_experts)])
+        expert = lambda e, inp: (torch.nn.functional.silu(inp @ params["w1"][e].T) * (inp @ params["w3"][e].T)
+                                 @ params["w2"][e].T)
     rows = torch.arange(x.shape[0])
-    out = sum(w[:, j:j + 1] * Y[torch.from_numpy(idx[:, j].astype(np.int64)), rows] for j in range(k))
+    out = 0
+    for j in range(k):
+        e_j = torch.from_numpy(idx[:, j].astype(np.int64))
+        wj = w[:, j:j + 1]
+        if weighting == "pre":      # the gate weight scales the expert's input
+            Y = torch.stack([expert(e, wj * X) for e in range(p.num_experts)])
+            out = out + Y[e_j, rows]
+        else:                       # ... or its output
+            Y = torch.stack([expert(e, X) for e in range(p.num_experts)])
+            out = out + wj * Y[e_j, rows]
     if p.sw1 is not None:
         for n in ("sw1", "sw3", "sw2"):
             params[n] = t(getattr(p, n))
