@@ -81,8 +81,8 @@ def parse():
     ap.add_argument("--parity-sample", type=int, default=64, help="tokens per rank checked after timing")
     ap.add_argument("--ep-chunks", type=int, default=None, help="token chunks of the EP exchange")
     ap.add_argument("--ep-transport", default=None, choices=["p2p", "collective"])
-    ap.add_argument("--ep-schedule", default=None, choices=["local_first", "chunked"],
-                    help="overlap schedule of the p2p exchange")
+    ap.add_argument("--ep-schedule", default=None, choices=["device", "local_first", "chunked"],
+                    help="schedule of the p2p exchange (default: device)")
     ap.add_argument("--ep-return", default=None, choices=["fused", "copy"],
                     help="local-first return: GEMM epilogue stores to the peers, or copies")
     ap.add_argument("--ep-dedup", default=None, choices=["auto", "on", "off"],
@@ -383,6 +383,12 @@ def full_expert_weights(model, R: Ranks):
 
 
 def parity_check(model, x, out, wl, R: Ranks, sample: int):
+    import torch
+    with torch.no_grad():
+        return _parity_check(model, x, out, wl, R, sample)
+
+
+def _parity_check(model, x, out, wl, R: Ranks, sample: int):
     """A sample of this rank's output rows against a float32 torch evaluation of the same
     layer (full-precision matmuls of the bf16 inputs and weights), on the routing the
     layer itself chose; capacity drops follow the (source rank, token, slot) order over

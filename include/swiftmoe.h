@@ -122,7 +122,9 @@ SMOE_API int smoe_dispatch_plan_noalloc(const int32_t* idx, int T, int k, int E,
                                         int32_t* row_token, int64_t rows_cap,
                                         smoe_stream_t stream);
 
-/* rows[r,:] = x[row_token[r],:] for r < expert_offsets[E] (zero rows for token -1).
+/* rows[r,:] = x[row_token[r],:] for expert_offsets[0] <= r < expert_offsets[E] (zero
+ * rows for token -1).  A plan's offsets start at 0; passing a slice of them (E experts
+ * starting at some expert) fills only that range of rows, at their plan positions.
  * Replaces: x.repeat_interleave(2)[sort_idx] and recv_x[expert_order]
  * (models/ultimate_moe.py:123,225).                                                  */
 SMOE_API int smoe_permute_rows(const void* x, int dtype, int T, int d, const int32_t* row_token,
@@ -211,6 +213,48 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
  * (the senders placed their rows in expert-major order; rows_cap <= n_recv); recv_dst
  * NULL: nothing was dropped.  Replaces, with the GEMM above, the return path of
  * models/ultimate_moe.py:152,224-231.                                                 */
+/* ------------------------------------------------- expert-parallel exchange on device
+ * The per-forward bookkeeping of the exchange without a host round trip (the reference
+ * reads the counts on the host: models/ultimate_moe.py:128-137, and sends three
+ * payloads: :139-141).  counts_all [ws][E] (device): rows each rank routes to each
+ * global expert (every rank's plan counts, all-gathered); experts live in contiguous
+ * blocks of E_l = E/ws per rank.  The capacity cut keeps, per expert, the first
+ * `capacity` rows in (source rank, token, slot) order (0 = no cut).
+ * smoe_ep_layout (one block; ws*E <= 8192) writes this rank's
+ *   send_addr[E]      byte address, in the owner's receive buffer (recv_base[owner],
+ *                     this GPU's mapping of it), of this rank's first row for expert e;
+ *                     0 for its own experts
+ *   keep[E]           rows of this rank's segment for expert e kept by the cut
+ *   recv_offsets[E_l+1] expert offsets of its own receive buffer, which holds the other
+ *                     ranks' rows expert-major (local expert, source rank, token, slot)
+ *   seg_table[2*E_l*ws+1] the received segments in (local expert, source) order: first
+ *                     receive row of each, the row total, then the byte address of each
+ *                     segment's first row in the source's return buffer (ret_base[s]),
+ *                     which has the source's send layout -- the format of
+ *                     smoe_ep_return_rows (row_src = recv_dst = NULL)
+ * If any rank's receive rows would exceed recv_rows_max, every rank (all compute the
+ * same counts) sends and computes nothing and the device error word is set (4).
+ * smoe_ep_send_rows: every row i of the send layout (expert_offsets [E+1] of this rank's
+ * dispatch plan over global experts; row_token from the same plan) outside this rank's
+ * own experts [own_first, own_first+own_count) is read from x[row_token[i]] and stored
+ * at send_addr[e] + p*row_bytes (p = position in expert e's segment) when p < keep[e]:
+ * the permute and the dispatch all-to-all in one kernel, writing straight into the
+ * peers' memory (CUDA IPC mappings, NVLink).  row_bytes % 16 == 0; rows_cap bounds the
+ * rows of the layout (expert_offsets[E] <= rows_cap).  Order the receivers after it
+ * with a collective on the same stream.
+ * smoe_ep_drop_slots: slot_row[s] = -1 for the slots the cut dropped (row position in
+ * its expert's segment >= keep[e]), so that smoe_combine skips them.                 */
+SMOE_API int smoe_ep_layout(const int32_t* counts_all, int ws, int E, int rank, int capacity,
+                            const uint64_t* recv_base, const uint64_t* ret_base, int64_t row_bytes,
+                            int64_t recv_rows_max, uint64_t* send_addr, int32_t* keep, int32_t* recv_offsets,
+                            int64_t* seg_table, smoe_stream_t stream);
+SMOE_API int smoe_ep_send_rows(const void* x, int64_t row_bytes, const int32_t* row_token,
+                               const int32_t* expert_offsets, int E, int own_first, int own_count,
+                               const uint64_t* send_addr, const int32_t* keep, int64_t rows_cap,
+                               smoe_stream_t stream);
+SMOE_API int smoe_ep_drop_slots(const int32_t* idx, int64_t n_slots, const int32_t* expert_offsets, int E,
+                                const int32_t* keep, int32_t* slot_row, smoe_stream_t stream);
+
 /* Expert-parallel token dedup (top-k with several experts per rank).  A token whose
  * slots go to several experts of one rank is sent to that rank once:
  *   smoe_ep_dedup_ranks: ridx[T, k] = destination rank of each slot in this rank's

@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "dispatch.cuh"
+#include "ep_device.cuh"
 #include "gemm_simt.cuh"
 #include "gemv.cuh"
 #include "gemm_tc.cuh"
@@ -714,6 +715,51 @@ int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, i
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)device_sms() * 8));
   ep_return_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(row_src, expert_offsets, E_l, recv_dst, n_recv,
                                                                 seg_table, n_src, row_bytes, row_ptrs, rows_cap);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_ep_layout(const int32_t* counts_all, int ws, int E, int rank, int capacity, const uint64_t* recv_base,
+                   const uint64_t* ret_base, int64_t row_bytes, int64_t recv_rows_max, uint64_t* send_addr,
+                   int32_t* keep, int32_t* recv_offsets, int64_t* seg_table, smoe_stream_t stream) {
+  if (ws < 1 || E < 1 || E % ws != 0 || rank < 0 || rank >= ws || capacity < 0) return SMOE_ERR_INVALID;
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || recv_rows_max < 0 || recv_rows_max > INT32_MAX) return SMOE_ERR_INVALID;
+  if (!counts_all || !recv_base || !ret_base || !send_addr || !keep || !recv_offsets || !seg_table)
+    return SMOE_ERR_INVALID;
+  if ((int64_t)ws * E > kLayoutMaxCells) return SMOE_ERR_UNSUPPORTED;
+  const int smem = (ws * E + 2 * E) * (int)sizeof(int);
+  static SmemGrant done;
+  SMOE_CK(ensure_smem(ep_layout_kernel, smem, &done));
+  ep_layout_kernel<<<1, 256, smem, (cudaStream_t)stream>>>(counts_all, ws, E, rank, capacity, recv_base, ret_base,
+                                                           row_bytes, recv_rows_max, send_addr, keep, recv_offsets,
+                                                           seg_table);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_ep_send_rows(const void* x, int64_t row_bytes, const int32_t* row_token, const int32_t* expert_offsets,
+                      int E, int own_first, int own_count, const uint64_t* send_addr, const int32_t* keep,
+                      int64_t rows_cap, smoe_stream_t stream) {
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || E < 1 || own_first < 0 || own_count < 0 || own_first + own_count > E ||
+      rows_cap < 0)
+    return SMOE_ERR_INVALID;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!x || !row_token || !expert_offsets || !send_addr || !keep || !aligned16(x)) return SMOE_ERR_INVALID;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(cdiv(rows_cap, 8), (int64_t)device_sms() * 2));
+  ep_send_rows_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const unsigned char*>(x), row_bytes, row_token, expert_offsets, E, own_first,
+      own_first + own_count, send_addr, keep);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_ep_drop_slots(const int32_t* idx, int64_t n_slots, const int32_t* expert_offsets, int E, const int32_t* keep,
+                       int32_t* slot_row, smoe_stream_t stream) {
+  if (n_slots < 0 || E < 1) return SMOE_ERR_INVALID;
+  if (n_slots == 0) return SMOE_OK;
+  if (!idx || !expert_offsets || !keep || !slot_row) return SMOE_ERR_INVALID;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n_slots, 256), (int64_t)device_sms() * 8);
+  ep_drop_slots_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, n_slots, expert_offsets, E, keep, slot_row);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

@@ -169,16 +169,18 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(const int32_
   }
 }
 
-// rows[r,:] = x[row_token[r],:] for r < offsets[E]; one warp per row, 16-byte vectors
+// rows[r,:] = x[row_token[r],:] for offsets[0] <= r < offsets[E] (a plan's offsets start
+// at 0; a slice of them selects a range of experts); one warp per row, 16-byte vectors
 // when every row starts on a 16-byte boundary.
 __global__ void __launch_bounds__(256) permute_rows_kernel(const unsigned char* __restrict__ x, int64_t row_bytes,
                                                            bool vec, const int32_t* __restrict__ row_token,
                                                            const int32_t* __restrict__ offsets, int E,
                                                            unsigned char* __restrict__ rows) {
   const int lane = threadIdx.x & 31;
+  const int64_t first = offsets[0];
   const int64_t total = offsets[E];
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total; r += warps) {
+  for (int64_t r = first + (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total; r += warps) {
     const int t = row_token[r];
     unsigned char* dst = rows + r * row_bytes;
     if (vec) {

@@ -83,7 +83,7 @@ def kept_rows(rows_per_expert: np.ndarray, capacity: int) -> int:
 class ExpertParallelExchange:
     def __init__(self, num_experts: int, world_size: int, rank: int, d_model: int,
                  group: Optional[dist.ProcessGroup] = None, kernels=None, chunks: int = 4,
-                 transport: str = "auto", schedule: str = "local_first",
+                 transport: str = "auto", schedule: str = "device",
                  runtime=None):
         if num_experts % world_size:
             raise ValueError("num_experts must be divisible by the world size")
@@ -107,9 +107,16 @@ class ExpertParallelExchange:
             raise ValueError("transport must be 'auto', 'p2p' or 'collective'")
         self.transport = transport
         self._bufs = None           # (receive, return) PeerBuffers of the p2p transport
-        if schedule not in ("local_first", "chunked"):
-            raise ValueError("schedule must be 'local_first' or 'chunked'")
-        self.schedule = schedule    # p2p transport: local-first or chunk-by-chunk overlap
+        if schedule not in ("device", "local_first", "chunked"):
+            raise ValueError("schedule must be 'device', 'local_first' or 'chunked'")
+        # p2p transport: "device" (layout on the device, rows stored into the peers by the
+        # send kernel, no host wait), "local_first" (host-computed layout, copy engines)
+        # or "chunked" (chunk-by-chunk overlap)
+        self.schedule = schedule
+        # device schedule: tokens any rank may pass to forward; sizes the peer buffers.
+        # None: the largest batch of the first device-schedule forward (one collective).
+        self.max_tokens: Optional[int] = None
+        self._dev = None            # device schedule: persistent layout tensors
         # local-first return of the other ranks' rows: "fused" = the expert GEMM stores
         # them into the source ranks' buffers; "copy" = gather + device-to-device copies
         self.return_mode = "fused"
@@ -177,6 +184,10 @@ class ExpertParallelExchange:
             return f"collective transport (all_to_all_single), {self.chunks} token chunks"
         if self.schedule == "chunked":
             return f"{self.transport} transport, chunked schedule, {self.chunks} token chunks"
+        if self.schedule == "device":
+            return (f"{self.transport} transport, device schedule (layout on the device, rows stored into "
+                    f"the peers by the send kernel, fused return, no host wait), token dedup {self.dedup} "
+                    f"(dedup forwards use the local-first schedule), max {self.max_tokens} tokens per rank")
         return (f"{self.transport} transport, local_first schedule, {self.return_mode} return, "
                 f"token dedup {self.dedup}, own rows split from {self.split_min_ws} ranks")
 
@@ -194,8 +205,10 @@ class ExpertParallelExchange:
         CUDA tensors use the peer-copy transport (``_forward_p2p``) unless
         ``transport="collective"``; CPU tensors (gloo) use all_to_all_single."""
         use_p2p = self.transport == "p2p" or (self.transport == "auto" and x.is_cuda)
-        if use_p2p and self.schedule == "local_first" and capacity <= 0 and self._use_dedup(idx.shape[1]):
+        if use_p2p and self.schedule in ("device", "local_first") and capacity <= 0 and self._use_dedup(idx.shape[1]):
             return self._forward_p2p_dedup(x, idx, w, experts, shared, timer)
+        if use_p2p and self.schedule == "device":
+            return self._forward_p2p_device(x, idx, w, capacity, experts, shared, timer)
         if use_p2p and self.schedule == "local_first":
             return self._forward_p2p_local_first(x, idx, w, capacity, experts, shared, timer)
         if use_p2p:
@@ -591,6 +604,127 @@ class ExpertParallelExchange:
         rt.wait(comp, ev_ret)
         mark("wait_ret0_after")
         return self.k.combine(ret_local[:int(send_tot[me])], plan["slot_row"], w, T, k, shared=shared)
+
+    # ------------------------------------------------------------ device schedule
+    def reserve(self, max_tokens: int, k: int, dev) -> None:
+        """Collective: size the device schedule's peer buffers for batches of up to
+        ``max_tokens`` tokens on every rank (the largest value any rank passes wins).
+        Called by the first device-schedule forward with its batch size; call it up
+        front when later batches may be larger."""
+        t = torch.tensor([int(max_tokens)], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        self.max_tokens = max(int(t.item()), 1)
+        self._dev = None
+        self._reserved_k = k
+
+    def _device_state(self, k: int, row_bytes: int, dev):
+        """Peer buffers sized for ``max_tokens`` and the persistent layout tensors."""
+        ws, El, E = self.world_size, self.exp_per_rank, self.num_experts
+        recv_rows = ws * self.max_tokens * min(k, El)        # rows one rank can receive at most
+        ret_rows = self.max_tokens * k                       # this rank's send layout
+        recv_buf, ret_buf = self._peer_buffers(dev)
+        recv_buf.ensure(recv_rows * row_bytes)
+        ret_buf.ensure(ret_rows * row_bytes)
+        key = (recv_buf.local, ret_buf.local, k, row_bytes, str(dev))
+        if self._dev is None or self._dev["key"] != key:
+            nseg = El * ws
+            i64 = dict(dtype=torch.int64, device=dev)
+            i32 = dict(dtype=torch.int32, device=dev)
+            self._dev = dict(
+                key=key, recv_rows=recv_rows, ret_rows=ret_rows,
+                recv_base=torch.tensor(recv_buf.ptrs, **i64), ret_base=torch.tensor(ret_buf.ptrs, **i64),
+                G=torch.zeros((ws, E), **i32),
+                lay=dict(send_addr=torch.zeros(E, **i64), keep=torch.zeros(E, **i32),
+                         recv_offsets=torch.zeros(El + 1, **i32), seg=torch.zeros(2 * nseg + 1, **i64)),
+                send=None)
+        return self._dev, recv_buf, ret_buf
+
+    def _forward_p2p_device(self, x, idx, w, capacity, experts, shared=None, timer=None):
+        """Device schedule: the host never waits for the device.
+
+        * compute stream: plan (rows grouped by global expert); this rank's own rows
+          permuted into the send buffer and run through its experts straight into the
+          return buffer (their rows there follow the send layout);
+        * communication stream, meanwhile: the per-expert counts of every rank
+          all-gathered into device memory, ``ep_layout`` turning them into addresses
+          (each segment's place in its owner's expert-major receive buffer, the kept
+          prefix under the capacity cut, this rank's receive offsets and the return
+          address of every received segment), ``ep_send_rows`` storing every routed row
+          of the other ranks' experts from x straight into the owners' receive buffers
+          over NVLink, then a one-int all-reduce that orders those stores before every
+          rank's next step;
+        * compute stream: the experts over the received rows (offsets read from device
+          memory), whose epilogue stores each output row into its source rank's return
+          buffer (fused return); an all-reduce, then the combine over the return buffer
+          (slots the capacity cut dropped are marked -1 first).
+
+        Buffers are sized for ``max_tokens`` tokens per rank (set by the first forward
+        or by ``reserve``), so no size depends on this batch's routing."""
+        rt = self.rt
+        ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
+        T, k = idx.shape
+        d = x.shape[1]
+        dev = x.device
+        rb = d * x.element_size()
+        if rb % 16:
+            raise ValueError("the device schedule needs rows of a multiple of 16 bytes")
+        if self.max_tokens is None or getattr(self, "_reserved_k", k) != k:
+            self.reserve(T, k, dev)
+        if T > self.max_tokens:
+            from ._lib import SwiftMoEError
+            raise SwiftMoEError(f"batch of {T} tokens exceeds the exchange's max_tokens={self.max_tokens}; "
+                                f"call reserve() with the largest batch on every rank first")
+        comp, comm = rt.compute(dev), rt.comm(dev)
+
+        def mark(name):
+            if timer is not None:
+                timer(name)
+
+        st, recv_buf, ret_buf = self._device_state(k, rb, dev)
+        lay, G = st["lay"], st["G"]
+        plan = self.k.dispatch_plan(idx, E)
+        rows_cap = plan["rows_cap"]
+        send = st["send"]
+        if send is None or send.shape[0] < rows_cap or send.dtype != x.dtype:
+            send = st["send"] = torch.empty((max(self.max_tokens * k, 1), d), dtype=x.dtype, device=dev)
+        own = plan["offsets"][me * El:(me + 1) * El + 1]
+        self.k.permute_rows(x, plan["row_token"], own, rows_cap, out=send)
+        mark("counts_start")
+        rt.join(comm, comp)
+        for t in (x, plan["row_token"], plan["offsets"], plan["counts"]):
+            rt.keep(t, comm)
+        with rt.on(comm):
+            dist.all_gather_into_tensor(G.view(-1), plan["counts"], group=self.group)
+            self.k.ep_layout(G, me, capacity, st["recv_base"], st["ret_base"], rb, st["recv_rows"], lay)
+            self.k.ep_send_rows(x, plan["row_token"], plan["offsets"], me * El, El, lay["send_addr"], lay["keep"],
+                                rows_cap)
+        self._barrier(comm, dev)
+        ev_sent = rt.record(comm)
+        mark("counts_done")
+        ret_local = rt.view(ret_buf.local, (st["ret_rows"], d), x.dtype, dev)
+        mark("experts_self_start")
+        experts(send, own[:-1], ends=own[1:], out=ret_local)
+        mark("experts_self_end")
+        mark("wait_sent0_before")
+        rt.wait(comp, ev_sent)
+        mark("wait_sent0_after")
+        if capacity > 0:
+            self.k.ep_drop_slots(idx, plan["offsets"], lay["keep"], plan["slot_row"])
+        recv_local = rt.view(recv_buf.local, (st["recv_rows"], d), x.dtype, dev)
+        R = st["recv_rows"]
+        row_ptrs = self.k.ep_return_rows(None, lay["recv_offsets"], None, R, lay["seg"], rb, R)
+        mark("experts0_start")
+        experts(recv_local, lay["recv_offsets"], row_ptrs=row_ptrs)
+        mark("experts0_end")
+        self._rows_dev = (lay["keep"][me * El:(me + 1) * El].sum().view(1), lay["recv_offsets"][El:])
+        rt.join(comm, comp)
+        self._barrier(comm, dev)
+        ev_ret = rt.record(comm)
+        mark("combine_start")
+        mark("wait_ret0_before")
+        rt.wait(comp, ev_ret)
+        mark("wait_ret0_after")
+        return self.k.combine(ret_local[:max(T * k, 1)], plan["slot_row"], w, T, k, shared=shared)
 
     def _forward_p2p_dedup(self, x, idx, w, experts, shared=None, timer=None):
         """Local-first schedule with token dedup, for top-k routing with several experts

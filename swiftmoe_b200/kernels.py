@@ -191,6 +191,38 @@ def ep_return_rows(row_src: torch.Tensor, offsets: torch.Tensor, recv_dst: torch
     return row_ptrs
 
 
+def ep_layout(counts_all: torch.Tensor, rank: int, capacity: int, recv_base: torch.Tensor, ret_base: torch.Tensor,
+              row_bytes: int, recv_rows_max: int, out: dict):
+    """Device-side layout of the exchange from the all-gathered counts [ws, E] (see
+    smoe_ep_layout).  ``out`` holds the preallocated outputs: send_addr [E] int64, keep [E]
+    int32, recv_offsets [E_l+1] int32, seg [2*E_l*ws+1] int64; returns it."""
+    _need_cuda(counts_all, recv_base, ret_base)
+    ws_, E = counts_all.shape
+    L.check(L.load().smoe_ep_layout(L.ptr(counts_all), ws_, E, rank, capacity, L.ptr(recv_base), L.ptr(ret_base),
+                                    row_bytes, recv_rows_max, L.ptr(out["send_addr"]), L.ptr(out["keep"]),
+                                    L.ptr(out["recv_offsets"]), L.ptr(out["seg"]),
+                                    L.stream_handle(counts_all.device)), "smoe_ep_layout")
+    return out
+
+
+def ep_send_rows(x: torch.Tensor, row_token: torch.Tensor, offsets: torch.Tensor, own_first: int, own_count: int,
+                 send_addr: torch.Tensor, keep: torch.Tensor, rows_cap: int) -> None:
+    """Rows of the other ranks' experts from x straight into their receive buffers."""
+    _need_cuda(x, row_token, offsets, send_addr, keep)
+    E = offsets.numel() - 1
+    L.check(L.load().smoe_ep_send_rows(L.ptr(x), x.shape[1] * x.element_size(), L.ptr(row_token), L.ptr(offsets), E,
+                                       own_first, own_count, L.ptr(send_addr), L.ptr(keep), rows_cap,
+                                       L.stream_handle(x.device)), "smoe_ep_send_rows")
+
+
+def ep_drop_slots(idx: torch.Tensor, offsets: torch.Tensor, keep: torch.Tensor, slot_row: torch.Tensor) -> None:
+    """slot_row[s] = -1 (in place) for the slots the capacity cut dropped."""
+    _need_cuda(idx, offsets, keep, slot_row)
+    E = offsets.numel() - 1
+    L.check(L.load().smoe_ep_drop_slots(L.ptr(idx), idx.numel(), L.ptr(offsets), E, L.ptr(keep), L.ptr(slot_row),
+                                        L.stream_handle(idx.device)), "smoe_ep_drop_slots")
+
+
 def ep_dedup_ranks(idx: torch.Tensor, El: int, ws: int, rank: int) -> torch.Tensor:
     """ridx [T, k] int32: rotated destination rank of the first slot of each token bound
     for a rank, -1 for its later slots to the same rank (see smoe_ep_dedup_ranks)."""

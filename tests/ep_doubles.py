@@ -33,12 +33,12 @@ def dispatch_plan(idx, num_experts, capacity=0, row_align=1):
 
 
 def permute_rows(x, row_token, offsets, rows_cap, out=None):
-    total = int(offsets[-1])
-    rt = row_token.numpy()[:total]
+    first, total = int(offsets[0]), int(offsets[-1])
+    rt = row_token.numpy()[first:total]
     xr = x.numpy()
-    rows = np.zeros((max(rows_cap, 1), x.shape[1]), xr.dtype)
-    rows[:total] = np.where(rt[:, None] >= 0, xr[np.maximum(rt, 0)], 0)
-    return torch.from_numpy(rows)
+    rows = np.zeros((max(rows_cap, 1), x.shape[1]), xr.dtype) if out is None else out.numpy()
+    rows[first:total] = np.where(rt[:, None] >= 0, xr[np.maximum(rt, 0)], 0)
+    return torch.from_numpy(rows) if out is None else out
 
 
 def gather_rows(src, index, n_rows, out=None):
@@ -145,3 +145,68 @@ def ep_dedup_meta(idx, w, ridx, slot_row, own_count, El, ws, rows_cap):
             if rn[t, j] == 0:
                 own_e[p] = meta_e[p]
     return torch.from_numpy(meta_e), torch.from_numpy(meta_w), torch.from_numpy(own_e)
+
+
+def ep_layout(counts_all, rank, capacity, recv_base, ret_base, row_bytes, recv_rows_max, out):
+    G = counts_all.numpy().astype(np.int64)
+    ws, E = G.shape
+    El, me = E // ws, rank
+    before = np.cumsum(G, 0) - G
+    Kp = np.clip(capacity - before, 0, G) if capacity > 0 else G.copy()
+    owner = np.arange(E) // El
+    per_exp = (Kp * (owner[None, :] != np.arange(ws)[:, None])).sum(0)
+    eo = np.zeros(E, np.int64)
+    n_recv = np.zeros(ws, np.int64)
+    for r in range(ws):
+        seg = per_exp[r * El:(r + 1) * El]
+        eo[r * El:(r + 1) * El] = np.cumsum(seg) - seg
+        n_recv[r] = seg.sum()
+    overflow = bool((n_recv > recv_rows_max).any())
+    rbase, tbase = recv_base.numpy(), ret_base.numpy()
+    send_addr = np.zeros(E, np.int64)
+    keep = np.zeros(E, np.int32)
+    for e in range(E):
+        so = sum(int(Kp[s, e]) for s in range(me) if s != owner[e])
+        if owner[e] != me and not overflow:
+            send_addr[e] = int(rbase[owner[e]]) + int(eo[e] + so) * row_bytes
+        keep[e] = 0 if overflow else Kp[me, e]
+    nseg = El * ws
+    seg = np.zeros(2 * nseg + 1, np.int64)
+    for i in range(nseg):
+        le, s = divmod(i, ws)
+        e = me * El + le
+        so = sum(int(Kp[q, e]) for q in range(s) if q != me)
+        seg[i] = 0 if overflow else eo[e] + so
+        seg[nseg + 1 + i] = int(tbase[s]) + int(G[s, :e].sum()) * row_bytes
+    seg[nseg] = 0 if overflow else n_recv[me]
+    roff = np.concatenate([eo[me * El:(me + 1) * El], [n_recv[me]]]) if not overflow else np.zeros(El + 1)
+    out["send_addr"].copy_(torch.from_numpy(send_addr))
+    out["keep"].copy_(torch.from_numpy(keep))
+    out["recv_offsets"].copy_(torch.from_numpy(roff.astype(np.int32)))
+    out["seg"].copy_(torch.from_numpy(seg))
+    return out
+
+
+def ep_send_rows(x, row_token, offsets, own_first, own_count, send_addr, keep, rows_cap):
+    off = offsets.numpy().astype(np.int64)
+    E = off.size - 1
+    rt, sa, kp = row_token.numpy(), send_addr.numpy(), keep.numpy()
+    xr = np.ascontiguousarray(x.numpy())
+    rb = xr.shape[1] * xr.itemsize
+    for i in range(int(off[E])):
+        if off[own_first] <= i < off[own_first + own_count]:
+            continue
+        e = int(np.searchsorted(off[:E], i, side="right")) - 1
+        p = i - int(off[e])
+        if p >= kp[e] or sa[e] == 0 or rt[i] < 0:
+            continue
+        ctypes.memmove(int(sa[e]) + p * rb, xr[rt[i]].ctypes.data, rb)
+
+
+def ep_drop_slots(idx, offsets, keep, slot_row):
+    it, off, kp = idx.numpy().reshape(-1), offsets.numpy(), keep.numpy()
+    sr = slot_row.numpy().reshape(-1)
+    for s in range(it.size):
+        e, r = int(it[s]), int(sr[s])
+        if 0 <= e < kp.size and r >= 0 and r - off[e] >= kp[e]:
+            sr[s] = -1

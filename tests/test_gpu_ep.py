@@ -38,7 +38,10 @@ CASES = {
     # offsets ~ N(0, 1.5) for load imbalance (d_ff reduced)
     "fine-grained-shape": (160, 2048, 128, 8, 128, None, True, 1.5),
 }
-TRANSPORTS = ["p2p", "p2p+copy", "p2p+split", "p2p-chunked", "collective"]
+# "p2p" = the default schedule (device-side layout, rows stored into the peers by the
+# send kernel); the host-laid-out schedules and the collective transport stay selectable
+TRANSPORTS = ["p2p", "p2p-local_first", "p2p+copy-local_first", "p2p+split-local_first", "p2p-chunked",
+              "collective"]
 
 
 def _rdzv(tmp_path):
@@ -49,7 +52,7 @@ def _rdzv(tmp_path):
 def _configure(m, transport):
     tr, _, sched = transport.partition("-")
     tr, *opts = tr.split("+")
-    m.comm.transport, m.comm.schedule = tr, sched or "local_first"
+    m.comm.transport, m.comm.schedule = tr, sched or "device"
     m.comm.return_mode = "copy" if "copy" in opts else "fused"
     if "split" in opts:                   # own rows in two halves even with 2 ranks
         m.comm.split_min_ws = 2
