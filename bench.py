@@ -567,6 +567,12 @@ def extra_workloads(R: Ranks, pk, steps: int, warmup: int, decode_model=None, sa
 
 # --------------------------------------------------------------------- GPU arm
 def main():
+    import torch
+    with torch.no_grad():      # a forward (inference) benchmark: no autograd graph is recorded
+        _main()
+
+
+def _main():
     args = parse()
     global D_MODEL, N_EXPERTS, TOP_K, D_FF, WORKLOAD, WL
     wl = WL = WORKLOADS[args.workload]

@@ -155,6 +155,7 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
  * nn.Linear experts at models/baseline_moe.py:151-162.                               */
 #define SMOE_EPI_STORE 0
 #define SMOE_EPI_SWIGLU 1
+#define SMOE_EPI_GATEUP 3 /* C[r, n] = A B1_g^T, C[r, N + n] = A B3_g^T (C is [rows_cap, 2N]) */
 SMOE_API int smoe_grouped_gemm(const void* A, const void* B, const void* B3, void* C, int dtype,
                       int out_dtype, int epilogue, const int32_t* offsets, const int32_t* ends,
                       int G, int64_t rows_cap, int N, int K, smoe_stream_t stream);
@@ -341,6 +342,59 @@ SMOE_API int smoe_event_elapsed(void* start, void* end, float* ms);
 
 SMOE_API size_t smoe_layer_workspace_size(const smoe_layer_args* a);
 SMOE_API int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream);
+
+/* --------------------------------------------------------------- layer backward
+ * Gradients of smoe_layer_fwd's output (16-bit SwiGLU layers, one GPU) with respect to
+ * x, the gate and every expert weight.  The reference is forward-only; these are the
+ * gradients of its forward (models/baseline_moe.py:56-189 with SwiGLU experts,
+ * post-weighting, k slots summed, capacity drops contributing zero, softmax over the k
+ * selected logits).  The routing, the gate/up pre-activations and the per-slot outputs
+ * are recomputed from x (nothing is kept from the forward).  Weights as in the forward,
+ * plus two K-major copies the dgrad GEMMs read (make them once per weight update with
+ * smoe_transpose_batched):  w2t [E, F, d] = w2 transposed;  w13t [E, d, 2F] = the
+ * transpose of [w1; w3] stacked along F.  Gradients (fp32) go to
+ *   dx [T, d] (dtype), dgate [E, d], dw13 [E, 2F, d] (each expert's dW1 rows, then its
+ *   dW3 rows), dw2 [E, d, F], and for the shared expert dsw13 [2F_s, d], dsw2 [d, F_s].
+ * No counterpart in the reference (forward-only).                                     */
+typedef struct smoe_layer_bwd_args {
+  int32_t tokens, d_model, num_experts, top_k;
+  int32_t d_ff, dtype, capacity;
+  int32_t num_shared, d_ff_shared;
+  const void* x;           /* [T, d]                          */
+  const void* dout;        /* [T, d] gradient of the output   */
+  const void* gate_w;      /* [E, d]                          */
+  const float* logit_bias; /* [E] or NULL                     */
+  const void* w1;          /* [E, F, d]                       */
+  const void* w3;          /* [E, F, d]                       */
+  const void* w2t;         /* [E, F, d]                       */
+  const void* w13t;        /* [E, d, 2F]                      */
+  const void* sw1;         /* shared [F_s, d]                 */
+  const void* sw3;         /* shared [F_s, d]                 */
+  const void* sw2t;        /* shared [F_s, d] (sw2 transposed) */
+  const void* sw13t;       /* shared [d, 2F_s]                */
+  void* dx;
+  float* dgate;
+  float* dw13;
+  float* dw2;
+  float* dsw13;
+  float* dsw2;
+  void* workspace;
+  size_t workspace_bytes;
+} smoe_layer_bwd_args;
+SMOE_API size_t smoe_layer_bwd_workspace_size(const smoe_layer_bwd_args* a);
+SMOE_API int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream);
+
+/* Weight-gradient GEMM grouped along K: for g < G,
+ *   C[g][m][n] = sum over k in [k_offsets[g], k_offsets[g+1]) of A[m][k] * B[n][k],
+ * A [M, K] and B [N, K] 16-bit, K-major with row strides lda, ldb >= K elements (multiples
+ * of 8); C [G, M, N] fp32.  Group starts must be multiples of 64 (a dispatch plan with
+ * row_align 64 gives that; a start that is not is reported in the device error word, 5);
+ * a group without rows gets zeros.  Replaces the weight gradients autograd would take
+ * through the reference's per-expert Linear / torch.mm (models/baseline_moe.py:155-162,
+ * models/ultimate_moe.py:245-249).                                                     */
+SMOE_API int smoe_wgrad_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int dtype,
+                             const int32_t* k_offsets, int G, int M, int N, int64_t K, float* C,
+                             smoe_stream_t stream);
 
 #ifdef __cplusplus
 }

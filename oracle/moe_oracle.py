@@ -315,7 +315,8 @@ def _swiglu_backward(xin, w1, w3, w2, dy, acc):
 
 
 def moe_backward(x: np.ndarray, p: MoEParams, dout: np.ndarray, *, k: int = 2, weighting: str = "post",
-                 capacity_factor: Optional[float] = None, capacity: Optional[int] = None, acc=np.float64):
+                 capacity_factor: Optional[float] = None, capacity: Optional[int] = None, acc=np.float64,
+                 routing=None):
     """Gradients of one rank's layer output (``moe_forward`` with ws = 1) for the upstream
     gradient ``dout`` [T, d]: a dict with ``x``, ``gate`` and the expert weights in
     ``MoEParams`` layout (``expert_w``, or ``w1, w3, w2``; ``sw1, sw3, sw2`` for the shared
@@ -327,12 +328,17 @@ def moe_backward(x: np.ndarray, p: MoEParams, dout: np.ndarray, *, k: int = 2, w
     the expert ``Linear(x) * w`` (post-weighting, :159-162) or ``(x * w) @ W``
     (pre-weighting, ``models/ultimate_moe.py:245-249``), the k slots summed in slot order
     (:188-189).  Dropped slots (capacity) contribute 0 and stay in the softmax, as in the
-    forward.  ``acc`` is the arithmetic precision (float64 by default)."""
+    forward.  ``acc`` is the arithmetic precision (float64 by default).  ``routing``
+    (optional): the (idx, w) to use instead of this restatement's router, as in
+    ``moe_forward``."""
     x = np.asarray(x, acc)
     dout = np.asarray(dout, acc)
     T, d = x.shape
     E = p.num_experts
-    idx, w, _ = route(x.astype(np.float32), p.gate, k, p.logit_bias)
+    if routing is not None:
+        idx, w = np.asarray(routing[0], np.int64), np.asarray(routing[1], np.float32)
+    else:
+        idx, w, _ = route(x.astype(np.float32), p.gate, k, p.logit_bias)
     cap = capacity if capacity else capacity_for(capacity_factor, T, k, E)
     plan, _ = dispatch_plan([idx], E, 1, cap)
     wk = w.astype(acc)

@@ -106,6 +106,25 @@ class _StageTimer:
         self.pending.clear()
 
 
+class _LayerFunction(torch.autograd.Function):
+    """The layer as one autograd node: the fused forward, and ``smoe_layer_bwd`` for
+    the gradients of x, the gate and every expert weight (16-bit SwiGLU layers on one
+    GPU; other layers raise in backward)."""
+
+    @staticmethod
+    def forward(ctx, module, x, *params):
+        ctx.module = module
+        ctx.save_for_backward(x)
+        return module._forward_impl(x)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (x,) = ctx.saved_tensors
+        m = ctx.module
+        grads = m._backward_fused(x, dout.contiguous())
+        return (None, grads["x"] if ctx.needs_input_grad[1] else None, *m._param_grads(grads))
+
+
 class MoECore(nn.Module):
     """Base class; subclasses provide the parameter accessors."""
 
@@ -182,6 +201,13 @@ class MoECore(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = self._prepare_input(x)
+        if torch.is_grad_enabled():
+            params = self._grad_params()
+            if x.requires_grad or any(p.requires_grad for p in params):
+                return _LayerFunction.apply(self, x, *params)
+        return self._forward_impl(x)
+
+    def _forward_impl(self, x: torch.Tensor) -> torch.Tensor:
         if self.ws == 1 and not self._force_staged:
             ev = None
             if self.enable_profiling:
@@ -288,6 +314,66 @@ class MoECore(nn.Module):
         mark("end")
         if prof:
             self._timer.add_marks(marks)
+        return out
+
+    # ------------------------------------------------------------ backward
+    def _grad_params(self) -> List[torch.Tensor]:
+        """The parameters the layer's autograd node differentiates, in _param_grads order."""
+        raise NotImplementedError
+
+    def _param_grads(self, g: Dict[str, torch.Tensor]) -> List[torch.Tensor]:
+        """The gradients of _grad_params() from _backward_fused's dict."""
+        raise NotImplementedError
+
+    def _backward_fused(self, x: torch.Tensor, dout: torch.Tensor) -> Dict[str, torch.Tensor]:
+        """One ``smoe_layer_bwd`` call: gradients (fp32 for the weights) of the output with
+        respect to x ("x", x.dtype), the gate ("gate" [E, d]) and the experts ("w1", "w3"
+        [E_l, F, d], "w2" [E_l, d, F]; "sw1", "sw3", "sw2" for the shared expert)."""
+        if self.ws != 1:
+            raise NotImplementedError("the backward pass runs on one GPU (expert parallelism is forward-only)")
+        if self.expert_type != "swiglu" or self.compute_dtype == torch.float32:
+            raise NotImplementedError("the backward pass covers 16-bit SwiGLU layers")
+        lib = L.load()
+        dev = x.device
+        T, d = x.shape
+        E, F = self.num_experts, self.d_ff
+        w1, w3, w2 = self._swiglu()
+        w2t = self._cached("w2t", [w2], lambda: K.transpose_batched(w2.detach().contiguous()))
+        w13t = self._cached("w13t", [w1, w3], lambda: K.transpose_batched(
+            torch.cat([w1.detach(), w3.detach()], dim=1).contiguous()))
+        a = L.LayerBwdArgs()
+        a.tokens, a.d_model, a.num_experts, a.top_k = T, d, E, self.top_k
+        a.d_ff, a.dtype, a.capacity = F, L.dtype_code(self.compute_dtype), self._capacity(T)
+        f32 = dict(dtype=torch.float32, device=dev)
+        dx = torch.empty_like(x)
+        dgate = torch.empty((E, d), **f32)
+        dw13 = torch.empty((E, 2 * F, d), **f32)
+        dw2 = torch.empty((E, d, F), **f32)
+        bias = self._logit_bias()
+        keep = [bias, w2t, w13t]
+        a.x, a.dout, a.gate_w = x.data_ptr(), dout.data_ptr(), self._gate().data_ptr()
+        a.logit_bias = bias.data_ptr() if bias is not None else None
+        a.w1, a.w3, a.w2t, a.w13t = w1.data_ptr(), w3.data_ptr(), w2t.data_ptr(), w13t.data_ptr()
+        a.dx, a.dgate, a.dw13, a.dw2 = dx.data_ptr(), dgate.data_ptr(), dw13.data_ptr(), dw2.data_ptr()
+        out = dict(x=dx, gate=dgate, w1=dw13[:, :F], w3=dw13[:, F:], w2=dw2)
+        sh = self._shared()
+        if sh is not None:
+            s1, s3, s2 = sh
+            Fs = s1.shape[0]
+            s2t = self._cached("sw2t", [s2], lambda: K.transpose_batched(s2.detach().unsqueeze(0).contiguous()))
+            s13t = self._cached("sw13t", [s1, s3], lambda: K.transpose_batched(
+                torch.cat([s1.detach(), s3.detach()], dim=0).unsqueeze(0).contiguous()))
+            dsw13 = torch.empty((2 * Fs, d), **f32)
+            dsw2 = torch.empty((d, Fs), **f32)
+            a.num_shared, a.d_ff_shared = 1, Fs
+            a.sw1, a.sw3, a.sw2t, a.sw13t = s1.data_ptr(), s3.data_ptr(), s2t.data_ptr(), s13t.data_ptr()
+            a.dsw13, a.dsw2 = dsw13.data_ptr(), dsw2.data_ptr()
+            keep += [s2t, s13t]
+            out.update(sw1=dsw13[:Fs], sw3=dsw13[Fs:], sw2=dsw2)
+        need = lib.smoe_layer_bwd_workspace_size(C.byref(a))
+        wsb = torch.empty(max(int(need), 1), dtype=torch.uint8, device=dev)
+        a.workspace, a.workspace_bytes = wsb.data_ptr(), wsb.numel()
+        L.check(lib.smoe_layer_bwd(C.byref(a), L.stream_handle(dev)), "smoe_layer_bwd")
         return out
 
     # ------------------------------------------------------------ profiling API

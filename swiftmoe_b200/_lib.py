@@ -16,7 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libswiftmoe.so"
 SMOE_OK = 0
 SMOE_F32, SMOE_F16, SMOE_BF16 = 0, 1, 2
 SMOE_EXPERT_LINEAR, SMOE_EXPERT_SWIGLU = 0, 1
-SMOE_EPI_STORE, SMOE_EPI_SWIGLU = 0, 1
+SMOE_EPI_STORE, SMOE_EPI_SWIGLU, SMOE_EPI_GATEUP = 0, 1, 3
 
 DTYPE_CODE = {torch.float32: SMOE_F32, torch.float16: SMOE_F16, torch.bfloat16: SMOE_BF16}
 
@@ -34,6 +34,20 @@ class LayerArgs(C.Structure):
         ("topk_idx", _vp), ("topk_w", _vp), ("expert_counts", _vp),
         ("workspace", _vp), ("workspace_bytes", _sz),
         ("stage_events", _vp * 6),
+    ]
+
+
+class LayerBwdArgs(C.Structure):
+    """Mirror of ``smoe_layer_bwd_args``."""
+    _fields_ = [
+        ("tokens", C.c_int32), ("d_model", C.c_int32), ("num_experts", C.c_int32), ("top_k", C.c_int32),
+        ("d_ff", C.c_int32), ("dtype", C.c_int32), ("capacity", C.c_int32),
+        ("num_shared", C.c_int32), ("d_ff_shared", C.c_int32),
+        ("x", _vp), ("dout", _vp), ("gate_w", _vp), ("logit_bias", _vp),
+        ("w1", _vp), ("w3", _vp), ("w2t", _vp), ("w13t", _vp),
+        ("sw1", _vp), ("sw3", _vp), ("sw2t", _vp), ("sw13t", _vp),
+        ("dx", _vp), ("dgate", _vp), ("dw13", _vp), ("dw2", _vp), ("dsw13", _vp), ("dsw2", _vp),
+        ("workspace", _vp), ("workspace_bytes", _sz),
     ]
 
 
@@ -76,6 +90,9 @@ SIGNATURES = {
     "smoe_event_elapsed": (_i32, [_vp, _vp, C.POINTER(C.c_float)]),
     "smoe_layer_workspace_size": (_sz, [C.POINTER(LayerArgs)]),
     "smoe_layer_fwd": (_i32, [C.POINTER(LayerArgs), _vp]),
+    "smoe_layer_bwd_workspace_size": (_sz, [C.POINTER(LayerBwdArgs)]),
+    "smoe_layer_bwd": (_i32, [C.POINTER(LayerBwdArgs), _vp]),
+    "smoe_wgrad_gemm": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -85,6 +85,27 @@ class StandardMoE(MoECore):
     def set_logit_bias(self, bias: Optional[torch.Tensor]):
         self.logit_bias = None if bias is None else bias.detach().float().to(self.gate.weight.device).contiguous()
 
+    # autograd: gate, each expert's Linear weights, the shared expert
+    def _grad_params(self):
+        if self.expert_type == "swiglu":
+            ps = [self.gate.weight] + [e.w1.weight for e in self.experts] + [e.w3.weight for e in self.experts] \
+                + [e.w2.weight for e in self.experts]
+        else:
+            ps = [self.gate.weight] + [e.weight for e in self.experts]
+        if self.num_shared_experts:
+            s = self.shared_expert
+            ps += [s.w1.weight, s.w3.weight, s.w2.weight]
+        return ps
+
+    def _param_grads(self, g):
+        dt = self.compute_dtype
+        out = [g["gate"].to(dt)]
+        for n in ("w1", "w3", "w2"):
+            out += [g[n][i].to(dt) for i in range(self.experts_per_rank)]
+        if self.num_shared_experts:
+            out += [g[n].to(dt) for n in ("sw1", "sw3", "sw2")]
+        return out
+
     # accessors: experts are separate nn.Linear modules; the kernels want them stacked
     def _gate(self):
         return self.gate.weight

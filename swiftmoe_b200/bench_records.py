@@ -28,8 +28,10 @@ from .baseline_moe import StandardMoE
 from .ultimate_moe import UltimateMoE
 
 
+@torch.no_grad()
 def measure_latency(model, x, iterations: int = 100):
-    """Per-iteration CUDA-event latency with a synchronize on both sides (:50-77)."""
+    """Per-iteration CUDA-event latency with a synchronize on both sides (:50-77); the
+    forward runs as inference (no gradient recording)."""
     times = []
     for _ in range(iterations):
         s = torch.cuda.Event(enable_timing=True)
@@ -57,8 +59,9 @@ def run_single_config(model_type: str, num_experts: int, d_model: int, batch_siz
     else:
         raise ValueError(f"unknown model type {model_type}")
     x = torch.randn(batch_size, d_model, device=device, dtype=torch.float16)
-    for _ in range(warmup):
-        model(x)
+    with torch.no_grad():
+        for _ in range(warmup):
+            model(x)
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     torch.cuda.reset_peak_memory_stats()

@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "dispatch.cuh"
 #include "ep_device.cuh"
+#include "backward.cuh"
 #include "gemm_simt.cuh"
 #include "gemv.cuh"
 #include "gemm_tc.cuh"
@@ -111,6 +112,20 @@ bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over the first K columns of a row-major [rows, ld] 16-bit matrix (ld >= K,
+// ld * 2 bytes a multiple of 16): columns from K on read as zeros.
+bool make_map_2d_ld(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t rows, int64_t K, int64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 3-D map over [G, N, K] weights; box = 64 (K) x 128 (N) x 1 group.
 bool make_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t G, int64_t N, int64_t K) {
   EncodeTiledFn enc = encode_fn();
@@ -141,7 +156,7 @@ int raster_band(int epi) {
     const int v = atoi(forced);
     if (v > 0) return v;
   }
-  return epi == SMOE_EPI_SWIGLU ? 32 : tc::GM_DEFAULT;
+  return (epi == SMOE_EPI_SWIGLU || epi == SMOE_EPI_GATEUP) ? 32 : tc::GM_DEFAULT;
 }
 
 template <int EPI, typename OutT>
@@ -168,6 +183,18 @@ int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   const int grid = device_sms() & ~1;  // whole CTA pairs
   kern<<<grid, tc::THREADS, tc::pair::SMEM_BYTES, st>>>(ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
                                                         K, (int)rows_cap, raster_band(EPI) / 2, idesc);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int launch_wgrad(const CUtensorMap& ma, const CUtensorMap& mb, float* C, const int32_t* koff, int G, int M, int N,
+                 uint32_t idesc, cudaStream_t st) {
+  static SmemGrant done;
+  auto kern = tc::wgrad_gemm_kernel<float>;
+  SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
+  const int64_t tiles = (int64_t)G * cdiv(M, tc::BM) * cdiv(N, tc::BN);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, device_sms()));
+  kern<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, C, koff, G, M, N, idesc);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
@@ -225,8 +252,9 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
                       cudaStream_t st, const uint64_t* row_ptrs = nullptr) {
   if (row_ptrs) C = nullptr;
   if (!A || !B || (!C && !row_ptrs) || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
-  if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU) return SMOE_ERR_INVALID;
-  if (epi == SMOE_EPI_SWIGLU && !B3) return SMOE_ERR_INVALID;
+  if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU && epi != SMOE_EPI_GATEUP) return SMOE_ERR_INVALID;
+  if ((epi == SMOE_EPI_SWIGLU || epi == SMOE_EPI_GATEUP) && !B3) return SMOE_ERR_INVALID;
+  if (epi == SMOE_EPI_GATEUP && (row_ptrs || dtype == SMOE_F32 || out_dtype != dtype)) return SMOE_ERR_UNSUPPORTED;
   if (elt_size(dtype) == 0 || elt_size(out_dtype) == 0) return SMOE_ERR_INVALID;
   if (rows_cap == 0) return SMOE_OK;
   if (rows_cap > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
@@ -245,7 +273,8 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   }
   // 16-bit inputs: decode-sized batches stream the weights on the SIMT pipes, the rest
   // runs on tensor cores
-  if (rows_cap <= gemv::DISPATCH_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 && aligned16(A) && aligned16(B) &&
+  if (epi != SMOE_EPI_GATEUP && rows_cap <= gemv::DISPATCH_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 &&
+      aligned16(A) && aligned16(B) &&
       (!B3 || aligned16(B3)) && (epi == SMOE_EPI_STORE || out_dtype == dtype) &&
       (out_dtype == SMOE_F32 || out_dtype == dtype))
     return launch_gemv(A, B, B3, C, row_ptrs, dtype, out_dtype, epi, offsets, ends, G, rows_cap, N, K, st);
@@ -258,10 +287,18 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   CUtensorMap ma, mb, mb3;
   if (!make_map_2d(&ma, A, dt, rows_cap, K)) return SMOE_ERR_CUDA;
   if (!make_map_3d(&mb, B, dt, G, N, K)) return SMOE_ERR_CUDA;
-  if (epi == SMOE_EPI_SWIGLU) {
+  if (epi == SMOE_EPI_SWIGLU || epi == SMOE_EPI_GATEUP) {
     if (!make_map_3d(&mb3, B3, dt, G, N, K)) return SMOE_ERR_CUDA;
   } else {
     mb3 = mb;
+  }
+  if (epi == SMOE_EPI_GATEUP) {  // [gate | up] pre-activations, rows of 2N
+    const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
+    return dtype == SMOE_BF16
+               ? launch_tc<tc::EPI_GATEUP, __nv_bfloat16>(ma, mb, mb3, C, 2 * (int64_t)N, nullptr, offsets, ends, G,
+                                                          rows_cap, N, K, idesc, st)
+               : launch_tc<tc::EPI_GATEUP, __half>(ma, mb, mb3, C, 2 * (int64_t)N, nullptr, offsets, ends, G,
+                                                   rows_cap, N, K, idesc, st);
   }
   if (row_ptrs && epi == SMOE_EPI_STORE && out_dtype == dtype) {  // rows staged, 128-byte stores
     const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
@@ -963,6 +1000,258 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
   rc = smoe_combine(y, dt, slot_row, w, T, k, d, ys, a->out, stream);
   if (rc) return rc;
   return mark(5);
+}
+
+int smoe_wgrad_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int dtype, const int32_t* k_offsets, int G,
+                    int M, int N, int64_t K, float* C, smoe_stream_t stream) {
+  if (!A || !B || !k_offsets || !C || G < 1 || G > tc::MAX_GROUPS || M < 1 || N < 1 || K < 0) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (lda < K || ldb < K || lda % 8 != 0 || ldb % 8 != 0 || N % 4 != 0) return SMOE_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return SMOE_ERR_UNSUPPORTED;
+  const CUtensorMapDataType dt = dtype == SMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mb;
+  // an empty K range still needs a valid map: one column wide, never loaded
+  if (!make_map_2d_ld(&ma, A, dt, M, std::max<int64_t>(K, 1), lda)) return SMOE_ERR_CUDA;
+  if (!make_map_2d_ld(&mb, B, dt, N, std::max<int64_t>(K, 1), ldb)) return SMOE_ERR_CUDA;
+  const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
+  return launch_wgrad(ma, mb, C, k_offsets, G, M, N, idesc, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ layer backward
+namespace {
+struct BwdPlan {
+  int64_t S, S8, T8, rows_cap_full;
+  size_t o_idx, o_w, o_cnt, o_off, o_sr, o_rt, o_pws, o_cntf, o_offf, o_srf, o_rtf, o_rws, o_xr, o_dr, o_roww,
+      o_dwr, o_dsel, o_ab, o_g, o_dxr, o_xrt, o_drt, o_abt, o_gt, o_abs, o_gs, o_dxs, o_xt, o_dot, o_abst, o_gst,
+      o_soff, total;
+  size_t plan_ws, router_ws;
+};
+
+bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
+  const int es = elt_size(a->dtype);
+  if (es != 2) return false;
+  const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = a->d_ff;
+  const int64_t Fs = a->num_shared > 0 ? a->d_ff_shared : 0;
+  p->S = smoe_plan_rows_cap((int)T, (int)k, (int)E, a->capacity, 64);
+  p->S8 = align_up(std::max<int64_t>(p->S, 1), 8);
+  p->T8 = align_up(std::max<int64_t>(T, 1), 8);
+  p->rows_cap_full = smoe_plan_rows_cap((int)T, (int)k, (int)E, 0, 1);
+  p->plan_ws = smoe_plan_workspace_size((int)T, (int)k, (int)E);
+  p->router_ws = smoe_router_workspace_size((int)T, (int)d, (int)E, a->dtype);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  const int64_t S = p->S, S8 = p->S8, T8 = p->T8;
+  p->o_idx = take(T * k * 4);
+  p->o_w = take(T * k * 4);
+  p->o_cnt = take(E * 4);
+  p->o_off = take((E + 1) * 4);
+  p->o_sr = take(T * k * 4);
+  p->o_rt = take(std::max<int64_t>(S, 1) * 4);
+  p->o_pws = take(p->plan_ws);
+  p->o_cntf = take(E * 4);
+  p->o_offf = take((E + 1) * 4);
+  p->o_srf = take(T * k * 4);
+  p->o_rtf = take(std::max<int64_t>(p->rows_cap_full, 1) * 4);
+  p->o_rws = take(p->router_ws);
+  p->o_xr = take(S * d * es);
+  p->o_dr = take(S * d * es);
+  p->o_roww = take(S * 4);
+  p->o_dwr = take(S * 4);
+  p->o_dsel = take(std::max<int64_t>(p->rows_cap_full, 1) * 4);
+  p->o_ab = take(S * 2 * F * es);
+  p->o_g = take(S * F * es);
+  p->o_dxr = take(S * d * es);
+  p->o_xrt = take(d * S8 * es);
+  p->o_drt = take(d * S8 * es);
+  p->o_abt = take(2 * F * S8 * es);
+  p->o_gt = take(F * S8 * es);
+  p->o_abs = take(T * 2 * Fs * es);
+  p->o_gs = take(T * Fs * es);
+  p->o_dxs = take(Fs > 0 ? T * d * es : 0);
+  p->o_xt = take(Fs > 0 ? d * T8 * es : 0);
+  p->o_dot = take(Fs > 0 ? d * T8 * es : 0);
+  p->o_abst = take(2 * Fs * T8 * es);
+  p->o_gst = take(Fs * T8 * es);
+  p->o_soff = take(16);
+  p->total = o;
+  return true;
+}
+
+template <typename T>
+int transpose_ld(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, cudaStream_t st) {
+  if (R == 0 || C == 0) return SMOE_OK;
+  if (R > INT32_MAX || C > INT32_MAX || cdiv(R, 32) > 65535) return SMOE_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(R, 32), 1), block(32, 8);
+  transpose_ld_kernel<T><<<grid, block, 0, st>>>((const T*)src, (T*)dst, (int)R, (int)C, ldd);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int transpose16(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, cudaStream_t st) {
+  return transpose_ld<unsigned short>(src, dst, R, C, ldd, st);
+}
+
+template <typename T>
+int swiglu_bwd_launch(void* ab, void* g, const float* row_w, const int32_t* n_rows, int64_t rows_cap, int F,
+                      float* dw_row, cudaStream_t st) {
+  if (rows_cap == 0) return SMOE_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>(rows_cap, (int64_t)device_sms() * 16);
+  swiglu_bwd_kernel<T><<<grid, 256, 0, st>>>((T*)ab, (T*)g, row_w, n_rows, rows_cap, F, dw_row);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+template <typename T>
+int bwd_tail(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, cudaStream_t st) {
+  const int64_t T_ = a->tokens, d = a->d_model, k = a->top_k;
+  const int E = a->num_experts;
+  const int32_t* idx = reinterpret_cast<const int32_t*>(ws + p.o_idx);
+  const float* w = reinterpret_cast<const float*>(ws + p.o_w);
+  const bool vec = d % 8 == 0 && aligned16(a->dx) && aligned16(a->gate_w) && aligned16(ws + p.o_dxr);
+  const T* dxs = a->num_shared > 0 ? reinterpret_cast<const T*>(ws + p.o_dxs) : nullptr;
+  const int64_t items = T_ * (vec ? d / 8 : d);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(items, 256), (int64_t)device_sms() * 32));
+  if (T_ > 0) {
+    if (vec)
+      moe_bwd_dx_kernel<T, 8><<<grid, 256, 0, st>>>(
+          reinterpret_cast<const T*>(ws + p.o_dxr), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
+          reinterpret_cast<const float*>(ws + p.o_dwr), (const T*)a->gate_w, dxs, (int)T_, (int)k, (int)d, (T*)a->dx,
+          reinterpret_cast<const int32_t*>(ws + p.o_srf), reinterpret_cast<float*>(ws + p.o_dsel));
+    else
+      moe_bwd_dx_kernel<T, 1><<<grid, 256, 0, st>>>(
+          reinterpret_cast<const T*>(ws + p.o_dxr), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
+          reinterpret_cast<const float*>(ws + p.o_dwr), (const T*)a->gate_w, dxs, (int)T_, (int)k, (int)d, (T*)a->dx,
+          reinterpret_cast<const int32_t*>(ws + p.o_srf), reinterpret_cast<float*>(ws + p.o_dsel));
+    SMOE_CK(cudaGetLastError());
+  }
+  dim3 g2((unsigned)cdiv(d, 256), (unsigned)E);
+  router_dwg_kernel<T><<<g2, 256, 0, st>>>((const T*)a->x, reinterpret_cast<const int32_t*>(ws + p.o_rtf),
+                                           reinterpret_cast<const int32_t*>(ws + p.o_offf),
+                                           reinterpret_cast<const float*>(ws + p.o_dsel), (int)d, a->dgate);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t smoe_layer_bwd_workspace_size(const smoe_layer_bwd_args* a) {
+  BwdPlan p;
+  if (!a || !bwd_plan(a, &p)) return 0;
+  return p.total;
+}
+
+int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
+  if (!a) return SMOE_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = a->d_ff, dt = a->dtype;
+  if (T < 0 || d < 1 || E < 1 || k < 1 || k > E || F < 1) return SMOE_ERR_INVALID;
+  if (dt != SMOE_BF16 && dt != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (d % 8 != 0 || F % 8 != 0 || E > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
+  if (a->num_shared < 0 || a->num_shared > 1) return SMOE_ERR_UNSUPPORTED;
+  const int Fs = a->num_shared ? a->d_ff_shared : 0;
+  if (a->num_shared && (Fs < 1 || Fs % 8 != 0 || !a->sw1 || !a->sw3 || !a->sw2t || !a->sw13t || !a->dsw13 || !a->dsw2))
+    return SMOE_ERR_INVALID;
+  if (!a->gate_w || !a->w1 || !a->w3 || !a->w2t || !a->w13t || !a->dgate || !a->dw13 || !a->dw2)
+    return SMOE_ERR_INVALID;
+  if (T > 0 && (!a->x || !a->dout || !a->dx)) return SMOE_ERR_INVALID;
+  BwdPlan p;
+  bwd_plan(a, &p);
+  if (!a->workspace || a->workspace_bytes < p.total) return SMOE_ERR_WORKSPACE;
+  if (T == 0) {  // no tokens: every gradient is zero
+    SMOE_CK(cudaMemsetAsync(a->dgate, 0, (size_t)E * d * 4, st));
+    SMOE_CK(cudaMemsetAsync(a->dw13, 0, (size_t)E * 2 * F * d * 4, st));
+    SMOE_CK(cudaMemsetAsync(a->dw2, 0, (size_t)E * d * F * 4, st));
+    if (Fs) {
+      SMOE_CK(cudaMemsetAsync(a->dsw13, 0, (size_t)2 * Fs * d * 4, st));
+      SMOE_CK(cudaMemsetAsync(a->dsw2, 0, (size_t)d * Fs * 4, st));
+    }
+    return SMOE_OK;
+  }
+  unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.o_idx);
+  float* w = reinterpret_cast<float*>(ws + p.o_w);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + p.o_off);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + p.o_sr);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + p.o_rt);
+  float* row_w = reinterpret_cast<float*>(ws + p.o_roww);
+  float* dw_row = reinterpret_cast<float*>(ws + p.o_dwr);
+  void* xr = ws + p.o_xr;
+  void* dr = ws + p.o_dr;
+  void* ab = ws + p.o_ab;
+  void* g = ws + p.o_g;
+  void* dxr = ws + p.o_dxr;
+  const int64_t S = p.S, S8 = p.S8;
+  int rc;
+  // routing and dispatch, as in the forward (rows padded to 64 per expert for the K groups)
+  rc = smoe_router_fwd(a->x, a->gate_w, dt, a->logit_bias, T, d, E, k, idx, w, nullptr, ws + p.o_rws, p.router_ws,
+                       stream);
+  if (rc) return rc;
+  rc = smoe_dispatch_plan(idx, T, k, E, a->capacity, 64, reinterpret_cast<int32_t*>(ws + p.o_cnt), offsets, slot_row,
+                          row_token, S, ws + p.o_pws, p.plan_ws, stream);
+  if (rc) return rc;
+  rc = smoe_dispatch_plan(idx, T, k, E, 0, 1, reinterpret_cast<int32_t*>(ws + p.o_cntf),
+                          reinterpret_cast<int32_t*>(ws + p.o_offf), reinterpret_cast<int32_t*>(ws + p.o_srf),
+                          reinterpret_cast<int32_t*>(ws + p.o_rtf), p.rows_cap_full, ws + p.o_pws, p.plan_ws, stream);
+  if (rc) return rc;
+  if ((rc = smoe_permute_rows(a->x, dt, T, d, row_token, offsets, E, S, xr, stream))) return rc;
+  if ((rc = smoe_permute_rows(a->dout, dt, T, d, row_token, offsets, E, S, dr, stream))) return rc;
+  SMOE_CK(cudaMemsetAsync(row_w, 0, (size_t)S * 4, st));
+  slot_weights_to_rows_kernel<<<(unsigned)std::min<int64_t>(cdiv((int64_t)T * k, 256), (int64_t)device_sms() * 8), 256,
+                                0, st>>>(slot_row, w, (int64_t)T * k, row_w);
+  SMOE_CK(cudaGetLastError());
+  // recomputed pre-activations, the gradient reaching h, the element-wise backward
+  if ((rc = grouped_gemm_impl(xr, a->w1, a->w3, ab, dt, dt, SMOE_EPI_GATEUP, offsets, nullptr, E, S, F, d, st))) return rc;
+  if ((rc = grouped_gemm_impl(dr, a->w2t, nullptr, g, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, S, F, d, st))) return rc;
+  rc = dt == SMOE_BF16 ? swiglu_bwd_launch<__nv_bfloat16>(ab, g, row_w, offsets + E, S, F, dw_row, st)
+                       : swiglu_bwd_launch<__half>(ab, g, row_w, offsets + E, S, F, dw_row, st);
+  if (rc) return rc;
+  // input gradient of the routed rows: [da | db] against [W1 | W3]
+  if ((rc = grouped_gemm_impl(ab, a->w13t, nullptr, dxr, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, S, d, 2 * F, st)))
+    return rc;
+  if (Fs) {  // shared expert: one group of all T rows, weight 1
+    int32_t* soff = reinterpret_cast<int32_t*>(ws + p.o_soff);
+    fill_two_kernel<<<1, 1, 0, st>>>(soff, 0, T);
+    SMOE_CK(cudaGetLastError());
+    void* abs_ = ws + p.o_abs;
+    void* gs = ws + p.o_gs;
+    if ((rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, abs_, dt, dt, SMOE_EPI_GATEUP, soff, nullptr, 1, T, Fs, d, st)))
+      return rc;
+    if ((rc = grouped_gemm_impl(a->dout, a->sw2t, nullptr, gs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, Fs, d, st)))
+      return rc;
+    rc = dt == SMOE_BF16 ? swiglu_bwd_launch<__nv_bfloat16>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st)
+                         : swiglu_bwd_launch<__half>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st);
+    if (rc) return rc;
+    if ((rc = grouped_gemm_impl(abs_, a->sw13t, nullptr, ws + p.o_dxs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, d,
+                                2 * Fs, st)))
+      return rc;
+    // weight gradients of the shared expert: K = the T tokens
+    const int64_t T8 = p.T8;
+    if ((rc = transpose16(a->x, ws + p.o_xt, T, d, T8, st))) return rc;
+    if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, T8, st))) return rc;
+    if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, T8, st))) return rc;
+    if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, T8, st))) return rc;
+    if ((rc = smoe_wgrad_gemm(ws + p.o_abst, T8, ws + p.o_xt, T8, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
+      return rc;
+    if ((rc = smoe_wgrad_gemm(ws + p.o_dot, T8, ws + p.o_gst, T8, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
+  }
+  // dx (routed rows + shared expert + router) and the gate's gradient
+  rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, st) : bwd_tail<__half>(a, p, ws, st);
+  if (rc) return rc;
+  // expert weight gradients: K runs over the routed rows, grouped by expert
+  if ((rc = transpose16(xr, ws + p.o_xrt, S, d, S8, st))) return rc;
+  if ((rc = transpose16(dr, ws + p.o_drt, S, d, S8, st))) return rc;
+  if ((rc = transpose16(ab, ws + p.o_abt, S, 2 * F, S8, st))) return rc;
+  if ((rc = transpose16(g, ws + p.o_gt, S, F, S8, st))) return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_abt, S8, ws + p.o_xrt, S8, dt, offsets, E, 2 * F, d, S, a->dw13, stream)))
+    return rc;
+  return smoe_wgrad_gemm(ws + p.o_drt, S8, ws + p.o_gt, S8, dt, offsets, E, d, F, S, a->dw2, stream);
 }
 
 }  // extern "C"

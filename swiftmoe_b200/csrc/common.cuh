@@ -24,7 +24,8 @@ enum DeviceErrorCode : int {
   kErrNone = 0,
   kErrWaitTimeout = 1,   // an mbarrier wait exceeded its time limit
   kErrBadExpertIndex = 2, // an expert index outside [0, E) reached the dispatch plan
-  kErrBadRowAddress = 3   // a row address of the expert-parallel return was not 16-byte aligned
+  kErrBadRowAddress = 3,  // a row address of the expert-parallel return was not 16-byte aligned
+  kErrBadGroupStart = 5   // a K-grouped GEMM group did not start on a multiple of 64 rows
 };
 
 __device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }

@@ -38,6 +38,13 @@ constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 + 3 *
 // staged through shared memory so that every warp store writes 128 contiguous bytes
 // of 4 rows (expert-parallel return into other GPUs' buffers).
 constexpr int EPI_ROWS = 2;
+// Public epilogue SMOE_EPI_GATEUP (3): the SwiGLU GEMM's two pre-activations stored
+// side by side, C[r, n] = A B1_g^T and C[r, N + n] = A B3_g^T (C is [rows_cap, 2N]);
+// the backward pass recomputes them instead of keeping them from the forward.
+constexpr int EPI_GATEUP = SMOE_EPI_GATEUP;
+template <int EPI> struct EpiTraits {
+  static constexpr bool kPair = EPI == SMOE_EPI_SWIGLU || EPI == EPI_GATEUP;  // [gate | up] tiles
+};
 constexpr int ROWS_STAGE_BYTES = 32 * 128;  // per epilogue warp: 32 rows x 64 16-bit columns
 constexpr int SMEM_BYTES_ROWS = SMEM_BYTES + 16 + 4 * ROWS_STAGE_BYTES;
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 200 ms
@@ -184,7 +191,25 @@ __device__ __forceinline__ void epilogue_rows(uint32_t tbase, uint64_t row_addr,
 // the [gate | up] halves, or a plain store of all BN columns.
 template <int EPI, typename OutT>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool row_ok, int col0, int N) {
-  if constexpr (EPI == SMOE_EPI_SWIGLU) {
+  if constexpr (EPI == EPI_GATEUP) {
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t gv[32], uv[32];
+      tmem_ld32(tbase + c * 32, gv);
+      tmem_ld32(tbase + 128 + c * 32, uv);
+      tmem_ld_wait();
+      float g[32], u[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        g[j] = __uint_as_float(gv[j]);
+        u[j] = __uint_as_float(uv[j]);
+      }
+      if (row_ok) {
+        Store16<OutT>::cols32(crow, col0 + c * 32, N, g);
+        Store16<OutT>::cols32(crow + N, col0 + c * 32, N, u);
+      }
+    }
+  } else if constexpr (EPI == SMOE_EPI_SWIGLU) {
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       uint32_t gv[32], uv[32];
@@ -244,7 +269,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int NB = (EPI == SMOE_EPI_SWIGLU) ? (N + 127) / 128 : (N + BN - 1) / BN;
+  constexpr bool kPair = EpiTraits<EPI>::kPair;
+  const int NB = kPair ? (N + 127) / 128 : (N + BN - 1) / BN;
   const int KB = (K + BK - 1) / BK;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
@@ -270,7 +296,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (EPI == SMOE_EPI_SWIGLU) tma_prefetch_desc(&tmB3);
+    if (kPair) tma_prefetch_desc(&tmB3);
   }
   if (warp == 1) tmem_alloc(smem_u32(s_tmem), 2 * BN);
   tc_fence_before();
@@ -288,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
         const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
-        const int n0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
+        const int n0 = kPair ? t.nb * 128 : t.nb * BN;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
@@ -297,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
           tma_load_2d(a_dst, &tmA, fb, kb * BK, t.row0);
           tma_load_3d(b_dst, &tmB, fb, kb * BK, n0, t.g);
-          if (EPI == SMOE_EPI_SWIGLU) tma_load_3d(b_dst + B_BYTES / 2, &tmB3, fb, kb * BK, n0, t.g);
+          if (kPair) tma_load_3d(b_dst + B_BYTES / 2, &tmB3, fb, kb * BK, n0, t.g);
           else tma_load_3d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128, t.g);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -352,7 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       bool row_ok = r < t.rows_valid;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      const int col0 = (EPI == SMOE_EPI_SWIGLU) ? t.nb * 128 : t.nb * BN;
+      const int col0 = kPair ? t.nb * 128 : t.nb * BN;
       if constexpr (EPI == EPI_ROWS) {
         const uint64_t addr = row_ok ? row_ptrs[t.row0 + r] : 0;
         epilogue_rows<OutT>(tbase, addr, col0, N, s_stage + q * ROWS_STAGE_BYTES, lane);
@@ -367,6 +393,194 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (acc == 0) acc_phase ^= 1;
     }
     if (row_ptrs) __threadfence_system();  // rows in another GPU's memory: visible before exit
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ============================================================================ K-grouped GEMM
+// Weight gradients of the grouped GEMMs: for every group g,
+//   C[g][m][n] = sum over k in [koff[g], koff[g+1]) of A[m][k] * B[n][k],
+// where A [M, Ktot] and B [N, Ktot] are K-major (the transposed routed rows: K runs over
+// the rows of all groups, grouped by expert).  Same pipeline as grouped_gemm_kernel
+// (TMA producer, single-thread tcgen05.mma issuer, double-buffered TMEM accumulators,
+// four epilogue warps); the tiles are 128 (M) x 256 (N) of one group, n fastest within
+// an m-tile, so a group's B rows (its K range of B) stay in L2 while the A rows stream
+// once.  Group starts must be multiples of BK (the dispatch plan's row_align 64): the
+// K tiles of a group then never reach into the next group, and every TMA K coordinate is
+// 16-byte aligned.  A start that is not is rounded down (wrong sums, no fault) and
+// reported in the device error word.  A group without rows gets zeros.
+__device__ __forceinline__ void wgrad_tile(int L, int MT, int NB, int& g, int& m0, int& n0) {
+  const int per = MT * NB;
+  g = L / per;
+  const int local = L - g * per;
+  m0 = (local / NB) * BM;
+  n0 = (local % NB) * BN;
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(THREADS, 1)
+    wgrad_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      OutT* __restrict__ C, const int32_t* __restrict__ koff, int G, int M, int N, uint32_t idesc) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  int* s_kb0 = reinterpret_cast<int*>(s_tmem + 4);  // first K tile of each group
+  int* s_kb1 = s_kb0 + (MAX_GROUPS + 1);            // end K tile of each group
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int MT = (M + BM - 1) / BM;
+  const int NB = (N + BN - 1) / BN;
+  const int total = G * MT * NB;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+  const uint32_t mma_done_bar = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    *s_abort = 0;
+    bool misaligned = false;
+    for (int g = 0; g < G; ++g) {
+      const int a = max(koff[g], 0), b = max(koff[g + 1], a);
+      misaligned |= (a % BK) != 0;
+      s_kb0[g] = a / BK;                    // rounded down: a K coordinate stays aligned
+      s_kb1[g] = (b + BK - 1) / BK;
+    }
+    if (misaligned) set_device_error(kErrBadGroupStart);
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(mma_done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(s_tmem), 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
+        int g, m0, n0;
+        wgrad_tile(L, MT, NB, g, m0, n0);
+        for (int kb = s_kb0[g]; kb < s_kb1[g]; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, m0);
+          tma_load_2d(b_dst, &tmB, fb, kb * BK, n0);
+          tma_load_2d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        const int64_t cnt = issued / STAGES + (s < issued % STAGES ? 1 : 0);
+        if (cnt > 0) mbar_wait_drain(full_bar(s), (uint32_t)((cnt - 1) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
+        int g, m0, n0;
+        wgrad_tile(L, MT, NB, g, m0, n0);
+        const int kb0 = s_kb0[g], kb1 = s_kb1[g];
+        if (kb1 <= kb0) continue;           // no rows: the epilogue writes zeros
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, s_abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > kb0 || kk != 0) ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      umma_commit(mma_done_bar);
+      mbar_wait_drain(mma_done_bar, 0);
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int L = blockIdx.x; L < total; L += gridDim.x) {
+      int g, m0, n0;
+      wgrad_tile(L, MT, NB, g, m0, n0);
+      const bool row_ok = m0 + r < M;
+      OutT* crow = C + ((int64_t)g * M + m0 + (row_ok ? r : 0)) * N;
+      if (s_kb1[g] <= s_kb0[g]) {           // empty group: zero tile, no accumulator used
+        if (row_ok) {
+          float z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0.f;
+          for (int c = 0; c < BN / 32; ++c) {
+            if constexpr (sizeof(OutT) == 4) {
+              uint32_t zu[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) zu[j] = 0u;
+              Store<float>::cols32(reinterpret_cast<float*>(crow), n0 + c * 32, N, zu);
+            } else {
+              Store16<OutT>::cols32(crow, n0 + c * 32, N, z);
+            }
+          }
+        }
+        continue;
+      }
+      if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      epilogue_tile<SMOE_EPI_STORE, OutT>(tbase, crow, row_ok, n0, N);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
   }
   tc_fence_before();
   __syncthreads();

@@ -140,6 +140,23 @@ def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, *, B3:
     return out
 
 
+def wgrad_gemm(A: torch.Tensor, B: torch.Tensor, k_offsets: torch.Tensor, K: Optional[int] = None,
+               out: Optional[torch.Tensor] = None):
+    """C[g] = A[:, K_g] @ B[:, K_g]^T (fp32 [G, M, N]) for the K ranges K_g = [k_offsets[g],
+    k_offsets[g+1]) of the K-major 16-bit operands A [M, ld] and B [N, ld] (the first K
+    columns; group starts multiples of 64)."""
+    _need_cuda(A, B, k_offsets)
+    M, lda = A.shape
+    N, ldb = B.shape
+    G = k_offsets.numel() - 1
+    K = min(lda, ldb) if K is None else K
+    if out is None:
+        out = torch.empty((G, M, N), dtype=torch.float32, device=A.device)
+    L.check(L.load().smoe_wgrad_gemm(L.ptr(A), lda, L.ptr(B), ldb, L.dtype_code(A.dtype), L.ptr(k_offsets), G, M, N,
+                                     K, L.ptr(out), L.stream_handle(A.device)), "smoe_wgrad_gemm")
+    return out
+
+
 def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
     """[G, R, C] -> [G, C, R]."""
     _need_cuda(src)

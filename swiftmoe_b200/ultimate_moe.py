@@ -118,6 +118,21 @@ class UltimateMoE(MoECore):
         come back in float32 so that MoEAsyncCommHandler.combine rounds once."""
         return stages.expert_rows(self._experts, self.exp_per_rank, recv_x, recv_idx, recv_w)
 
+    # autograd: gate, the expert weights, the shared expert
+    def _grad_params(self):
+        ps = [self.gate_weight] + ([self.w1, self.w3, self.w2] if self.expert_type == "swiglu"
+                                   else [self.expert_weights])
+        if self.num_shared_experts:
+            ps += [self.shared_w1, self.shared_w3, self.shared_w2]
+        return ps
+
+    def _param_grads(self, g):
+        out = [g["gate"].to(self.gate_weight.dtype)]
+        out += [g[n].to(self.compute_dtype) for n in ("w1", "w3", "w2")]
+        if self.num_shared_experts:
+            out += [g[n].to(self.compute_dtype) for n in ("sw1", "sw3", "sw2")]
+        return out
+
     # accessors
     def _gate(self):
         return self.gate_weight

@@ -87,8 +87,9 @@ def _run_case(rank, ws, dev, case, transport):
     if bias is not None:
         m.set_logit_bias(torch.from_numpy(bias))
     x = torch.from_numpy(xs[rank]).to(dev, dt)
-    out = m(x).float().cpu().numpy()
-    out2 = m(x).float().cpu().numpy()          # second call: same bits
+    with torch.no_grad():
+        out = m(x).float().cpu().numpy()
+        out2 = m(x).float().cpu().numpy()      # second call: same bits
     # every rank's routing, as the GPU computed it
     idx, w = kernels.router(x, m.gate_weight, k, m.logit_bias)
     all_idx = [torch.empty_like(idx) for _ in range(ws)]
@@ -169,7 +170,8 @@ def _ref_fixture_worker(rank, ws, rdzv, name, transports, out_dir):
         with torch.no_grad():
             m.gate_weight.copy_(torch.from_numpy(p.gate))
             m.expert_weights.copy_(torch.from_numpy(p.expert_w[rank * El:(rank + 1) * El]))
-        out = m(torch.from_numpy(f["x"][rank]).to(dev)).cpu().numpy()
+        with torch.no_grad():
+            out = m(torch.from_numpy(f["x"][rank]).to(dev)).cpu().numpy()
         errs.append(float(np.abs(out - f["out"][rank]).max()))
         m.comm.close()
     np.save(os.path.join(out_dir, f"ref{rank}.npy"), np.array(errs))
