@@ -344,8 +344,8 @@ SMOE_API size_t smoe_layer_workspace_size(const smoe_layer_args* a);
 SMOE_API int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream);
 
 /* --------------------------------------------------------------- layer backward
- * Gradients of smoe_layer_fwd's output (16-bit SwiGLU layers, one GPU) with respect to
- * x, the gate and every expert weight.  The reference is forward-only; these are the
+ * Gradients of smoe_layer_fwd's output (16-bit layers, SwiGLU or linear experts, one
+ * GPU) with respect to x, the gate and every expert weight.  The reference is forward-only; these are the
  * gradients of its forward (models/baseline_moe.py:56-189 with SwiGLU experts,
  * post-weighting, k slots summed, capacity drops contributing zero, softmax over the k
  * selected logits).  The routing, the gate/up pre-activations and the per-slot outputs
@@ -380,6 +380,14 @@ typedef struct smoe_layer_bwd_args {
   float* dsw2;
   void* workspace;
   size_t workspace_bytes;
+  /* Linear experts (expert_type SMOE_EXPERT_LINEAR, y = x Wl^T with Wl [d_out, d_in]):
+   * w_lin_t [E, d_in, d_out] = Wl transposed (UltimateMoE's x @ W parameter as it is);
+   * dw_lin [E, d_out, d_in] fp32, or [E, d_in, d_out] when dw_lin_transposed != 0.
+   * The SwiGLU fields are then unused (d_ff ignored).                                */
+  int32_t expert_type;
+  int32_t dw_lin_transposed;
+  const void* w_lin_t;
+  float* dw_lin;
 } smoe_layer_bwd_args;
 SMOE_API size_t smoe_layer_bwd_workspace_size(const smoe_layer_bwd_args* a);
 SMOE_API int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream);

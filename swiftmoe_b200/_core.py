@@ -157,6 +157,11 @@ class MoECore(nn.Module):
         """Linear expert weights as [E_l, d_out, d_in] (K contiguous)."""
         raise NotImplementedError
 
+    def _linear_xw(self):
+        """Linear expert weights as [E_l, d_in, d_out] (the x @ W layout), and whether the
+        module's parameter has that layout (its gradient is then wanted in it too)."""
+        raise NotImplementedError
+
     def _swiglu(self):
         raise NotImplementedError
 
@@ -331,31 +336,44 @@ class MoECore(nn.Module):
         [E_l, F, d], "w2" [E_l, d, F]; "sw1", "sw3", "sw2" for the shared expert)."""
         if self.ws != 1:
             raise NotImplementedError("the backward pass runs on one GPU (expert parallelism is forward-only)")
-        if self.expert_type != "swiglu" or self.compute_dtype == torch.float32:
-            raise NotImplementedError("the backward pass covers 16-bit SwiGLU layers")
+        if self.compute_dtype == torch.float32:
+            raise NotImplementedError("the backward pass covers 16-bit layers (bf16 / fp16)")
         lib = L.load()
         dev = x.device
         T, d = x.shape
-        E, F = self.num_experts, self.d_ff
-        w1, w3, w2 = self._swiglu()
-        w2t = self._cached("w2t", [w2], lambda: K.transpose_batched(w2.detach().contiguous()))
-        w13t = self._cached("w13t", [w1, w3], lambda: K.transpose_batched(
-            torch.cat([w1.detach(), w3.detach()], dim=1).contiguous()))
+        E = self.num_experts
         a = L.LayerBwdArgs()
         a.tokens, a.d_model, a.num_experts, a.top_k = T, d, E, self.top_k
-        a.d_ff, a.dtype, a.capacity = F, L.dtype_code(self.compute_dtype), self._capacity(T)
+        a.dtype, a.capacity = L.dtype_code(self.compute_dtype), self._capacity(T)
         f32 = dict(dtype=torch.float32, device=dev)
         dx = torch.empty_like(x)
         dgate = torch.empty((E, d), **f32)
-        dw13 = torch.empty((E, 2 * F, d), **f32)
-        dw2 = torch.empty((E, d, F), **f32)
         bias = self._logit_bias()
-        keep = [bias, w2t, w13t]
+        keep = [bias]
         a.x, a.dout, a.gate_w = x.data_ptr(), dout.data_ptr(), self._gate().data_ptr()
         a.logit_bias = bias.data_ptr() if bias is not None else None
-        a.w1, a.w3, a.w2t, a.w13t = w1.data_ptr(), w3.data_ptr(), w2t.data_ptr(), w13t.data_ptr()
-        a.dx, a.dgate, a.dw13, a.dw2 = dx.data_ptr(), dgate.data_ptr(), dw13.data_ptr(), dw2.data_ptr()
-        out = dict(x=dx, gate=dgate, w1=dw13[:, :F], w3=dw13[:, F:], w2=dw2)
+        a.dx, a.dgate = dx.data_ptr(), dgate.data_ptr()
+        out = dict(x=dx, gate=dgate)
+        if self.expert_type == "swiglu":
+            F = self.d_ff
+            w1, w3, w2 = self._swiglu()
+            w2t = self._cached("w2t", [w2], lambda: K.transpose_batched(w2.detach().contiguous()))
+            w13t = self._cached("w13t", [w1, w3], lambda: K.transpose_batched(
+                torch.cat([w1.detach(), w3.detach()], dim=1).contiguous()))
+            dw13 = torch.empty((E, 2 * F, d), **f32)
+            dw2 = torch.empty((E, d, F), **f32)
+            keep += [w2t, w13t]
+            a.expert_type, a.d_ff = L.SMOE_EXPERT_SWIGLU, F
+            a.w1, a.w3, a.w2t, a.w13t = w1.data_ptr(), w3.data_ptr(), w2t.data_ptr(), w13t.data_ptr()
+            a.dw13, a.dw2 = dw13.data_ptr(), dw2.data_ptr()
+            out.update(w1=dw13[:, :F], w3=dw13[:, F:], w2=dw2)
+        else:
+            wlt, xw_layout = self._linear_xw()          # [E, d_in, d_out]
+            dwl = torch.empty((E, d, d), **f32)
+            keep.append(wlt)
+            a.expert_type, a.w_lin_t, a.dw_lin = L.SMOE_EXPERT_LINEAR, wlt.data_ptr(), dwl.data_ptr()
+            a.dw_lin_transposed = 1 if xw_layout else 0
+            out.update(expert_w=dwl)
         sh = self._shared()
         if sh is not None:
             s1, s3, s2 = sh

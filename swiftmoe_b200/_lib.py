@@ -48,6 +48,7 @@ class LayerBwdArgs(C.Structure):
         ("sw1", _vp), ("sw3", _vp), ("sw2t", _vp), ("sw13t", _vp),
         ("dx", _vp), ("dgate", _vp), ("dw13", _vp), ("dw2", _vp), ("dsw13", _vp), ("dsw2", _vp),
         ("workspace", _vp), ("workspace_bytes", _sz),
+        ("expert_type", C.c_int32), ("dw_lin_transposed", C.c_int32), ("w_lin_t", _vp), ("dw_lin", _vp),
     ]
 
 

@@ -100,7 +100,9 @@ class StandardMoE(MoECore):
     def _param_grads(self, g):
         dt = self.compute_dtype
         out = [g["gate"].to(dt)]
-        for n in ("w1", "w3", "w2"):
+        if self.expert_type == "linear":
+            out += [g["expert_w"][i].to(dt) for i in range(self.experts_per_rank)]
+        for n in (("w1", "w3", "w2") if self.expert_type == "swiglu" else ()):
             out += [g[n][i].to(dt) for i in range(self.experts_per_rank)]
         if self.num_shared_experts:
             out += [g[n].to(dt) for n in ("sw1", "sw3", "sw2")]
@@ -113,6 +115,11 @@ class StandardMoE(MoECore):
     def _linear_kmajor(self):
         ws_ = [e.weight for e in self.experts]
         return self._cached("lin", ws_, lambda: torch.stack([w.detach() for w in ws_]).contiguous())
+
+    def _linear_xw(self):
+        ws_ = [e.weight for e in self.experts]
+        return self._cached("lin_xw", ws_, lambda: K.transpose_batched(
+            torch.stack([w.detach() for w in ws_]).contiguous())), False
 
     def _swiglu(self):
         w1 = [e.w1.weight for e in self.experts]

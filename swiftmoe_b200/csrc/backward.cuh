@@ -79,6 +79,52 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(T* __restrict__ ab, T* 
   }
 }
 
+// Linear experts (y = x Wl^T): one block per row r < *n_rows, in place,
+//   dw_row[r] = sum_i g[r,i] * x[r,i]   (g = dout_r Wl, so that <g, x> = <dout_r, y_r>),
+//   g[r] -> w_r * g[r]   (the input gradient of the row),   dr[r] -> w_r * dr[r]   (dy_r).
+template <typename T>
+__global__ void __launch_bounds__(256) linear_bwd_kernel(T* __restrict__ g, const T* __restrict__ xr,
+                                                         T* __restrict__ dr, const float* __restrict__ row_w,
+                                                         const int32_t* __restrict__ n_rows, int64_t rows_cap, int d,
+                                                         float* __restrict__ dw_row) {
+  __shared__ float red[8];
+  const int64_t rows = (int64_t)*n_rows < rows_cap ? (int64_t)*n_rows : rows_cap;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float wr = row_w[r];
+    T* pg = g + r * (int64_t)d;
+    const T* px = xr + r * (int64_t)d;
+    T* pd = dr + r * (int64_t)d;
+    float dw = 0.f;
+    for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+      float gg[8], xx[8], dd[8];
+      load_vec_f<T, 8>(pg + c, gg);
+      load_vec_f<T, 8>(px + c, xx);
+      load_vec_f<T, 8>(pd + c, dd);
+      union {
+        uint4 u;
+        T e[8];
+      } og, od;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dw = fmaf(gg[i], xx[i], dw);
+        og.e[i] = Num<T>::from_f(wr * gg[i]);
+        od.e[i] = Num<T>::from_f(wr * dd[i]);
+      }
+      *reinterpret_cast<uint4*>(pg + c) = og.u;
+      *reinterpret_cast<uint4*>(pd + c) = od.u;
+    }
+    dw = warp_sum(dw);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dw;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+      dw_row[r] = s;
+    }
+    __syncthreads();
+  }
+}
+
 // dx[t, c] = sum_j dxr[slot_row[t,j], c] (kept slots) + dxs[t, c] (shared expert, may be
 // NULL) + sum_j dsel_tj * wg[idx[t,j], c], accumulated in fp32 and rounded once.
 // dsel_tj = w_tj (dw_tj - sum_j' w_tj' dw_tj'), dw_tj = dw_row[slot_row[t,j]] (0 when the

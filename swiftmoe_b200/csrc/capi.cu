@@ -1032,7 +1032,8 @@ struct BwdPlan {
 bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   const int es = elt_size(a->dtype);
   if (es != 2) return false;
-  const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = a->d_ff;
+  const bool lin = a->expert_type == SMOE_EXPERT_LINEAR;
+  const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = lin ? 0 : a->d_ff;
   const int64_t Fs = a->num_shared > 0 ? a->d_ff_shared : 0;
   p->S = smoe_plan_rows_cap((int)T, (int)k, (int)E, a->capacity, 64);
   p->S8 = align_up(std::max<int64_t>(p->S, 1), 8);
@@ -1065,8 +1066,8 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   p->o_dwr = take(S * 4);
   p->o_dsel = take(std::max<int64_t>(p->rows_cap_full, 1) * 4);
   p->o_ab = take(S * 2 * F * es);
-  p->o_g = take(S * F * es);
-  p->o_dxr = take(S * d * es);
+  p->o_g = take(S * (lin ? d : F) * es);   // linear experts: dout_r Wl, then the rows' input gradient
+  p->o_dxr = take(lin ? 0 : S * d * es);
   p->o_xrt = take(d * S8 * es);
   p->o_drt = take(d * S8 * es);
   p->o_abt = take(2 * F * S8 * es);
@@ -1108,24 +1109,34 @@ int swiglu_bwd_launch(void* ab, void* g, const float* row_w, const int32_t* n_ro
 }
 
 template <typename T>
-int bwd_tail(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, cudaStream_t st) {
+int linear_bwd_launch(void* g, const void* xr, void* dr, const float* row_w, const int32_t* n_rows, int64_t rows_cap,
+                      int d, float* dw_row, cudaStream_t st) {
+  if (rows_cap == 0) return SMOE_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>(rows_cap, (int64_t)device_sms() * 16);
+  linear_bwd_kernel<T><<<grid, 256, 0, st>>>((T*)g, (const T*)xr, (T*)dr, row_w, n_rows, rows_cap, d, dw_row);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+template <typename T>
+int bwd_tail(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, const void* dxr_rows, cudaStream_t st) {
   const int64_t T_ = a->tokens, d = a->d_model, k = a->top_k;
   const int E = a->num_experts;
   const int32_t* idx = reinterpret_cast<const int32_t*>(ws + p.o_idx);
   const float* w = reinterpret_cast<const float*>(ws + p.o_w);
-  const bool vec = d % 8 == 0 && aligned16(a->dx) && aligned16(a->gate_w) && aligned16(ws + p.o_dxr);
+  const bool vec = d % 8 == 0 && aligned16(a->dx) && aligned16(a->gate_w) && aligned16(dxr_rows);
   const T* dxs = a->num_shared > 0 ? reinterpret_cast<const T*>(ws + p.o_dxs) : nullptr;
   const int64_t items = T_ * (vec ? d / 8 : d);
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(items, 256), (int64_t)device_sms() * 32));
   if (T_ > 0) {
     if (vec)
       moe_bwd_dx_kernel<T, 8><<<grid, 256, 0, st>>>(
-          reinterpret_cast<const T*>(ws + p.o_dxr), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
+          reinterpret_cast<const T*>(dxr_rows), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
           reinterpret_cast<const float*>(ws + p.o_dwr), (const T*)a->gate_w, dxs, (int)T_, (int)k, (int)d, (T*)a->dx,
           reinterpret_cast<const int32_t*>(ws + p.o_srf), reinterpret_cast<float*>(ws + p.o_dsel));
     else
       moe_bwd_dx_kernel<T, 1><<<grid, 256, 0, st>>>(
-          reinterpret_cast<const T*>(ws + p.o_dxr), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
+          reinterpret_cast<const T*>(dxr_rows), reinterpret_cast<const int32_t*>(ws + p.o_sr), idx, w,
           reinterpret_cast<const float*>(ws + p.o_dwr), (const T*)a->gate_w, dxs, (int)T_, (int)k, (int)d, (T*)a->dx,
           reinterpret_cast<const int32_t*>(ws + p.o_srf), reinterpret_cast<float*>(ws + p.o_dsel));
     SMOE_CK(cudaGetLastError());
@@ -1139,6 +1150,44 @@ int bwd_tail(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, 
 }
 }  // namespace
 
+namespace {
+// Shared expert backward: one group of all T rows with weight 1; its input gradient
+// goes to the dxs slab of the workspace, its weight gradients to dsw13 / dsw2.
+int bwd_shared(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, cudaStream_t st) {
+  const int Fs = a->num_shared ? a->d_ff_shared : 0;
+  if (!Fs) return SMOE_OK;
+  const int T = a->tokens, d = a->d_model, dt = a->dtype;
+  smoe_stream_t stream = (smoe_stream_t)st;
+  int rc;
+  int32_t* soff = reinterpret_cast<int32_t*>(ws + p.o_soff);
+  fill_two_kernel<<<1, 1, 0, st>>>(soff, 0, T);
+  SMOE_CK(cudaGetLastError());
+  void* abs_ = ws + p.o_abs;
+  void* gs = ws + p.o_gs;
+  if ((rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, abs_, dt, dt, SMOE_EPI_GATEUP, soff, nullptr, 1, T, Fs, d, st)))
+    return rc;
+  if ((rc = grouped_gemm_impl(a->dout, a->sw2t, nullptr, gs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, Fs, d, st)))
+    return rc;
+  rc = dt == SMOE_BF16 ? swiglu_bwd_launch<__nv_bfloat16>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st)
+                       : swiglu_bwd_launch<__half>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st);
+  if (rc) return rc;
+  if ((rc = grouped_gemm_impl(abs_, a->sw13t, nullptr, ws + p.o_dxs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, d,
+                              2 * Fs, st)))
+    return rc;
+  // weight gradients of the shared expert: K = the T tokens
+  const int64_t T8 = p.T8;
+  if ((rc = transpose16(a->x, ws + p.o_xt, T, d, T8, st))) return rc;
+  if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, T8, st))) return rc;
+  if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, T8, st))) return rc;
+  if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, T8, st))) return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_abst, T8, ws + p.o_xt, T8, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
+    return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_dot, T8, ws + p.o_gst, T8, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
+  return SMOE_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 size_t smoe_layer_bwd_workspace_size(const smoe_layer_bwd_args* a) {
@@ -1150,15 +1199,18 @@ size_t smoe_layer_bwd_workspace_size(const smoe_layer_bwd_args* a) {
 int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   if (!a) return SMOE_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
-  const int T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = a->d_ff, dt = a->dtype;
-  if (T < 0 || d < 1 || E < 1 || k < 1 || k > E || F < 1) return SMOE_ERR_INVALID;
+  const bool lin = a->expert_type == SMOE_EXPERT_LINEAR;
+  if (!lin && a->expert_type != SMOE_EXPERT_SWIGLU) return SMOE_ERR_INVALID;
+  const int T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = lin ? 0 : a->d_ff, dt = a->dtype;
+  if (T < 0 || d < 1 || E < 1 || k < 1 || k > E || (!lin && F < 1)) return SMOE_ERR_INVALID;
   if (dt != SMOE_BF16 && dt != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
   if (d % 8 != 0 || F % 8 != 0 || E > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
   if (a->num_shared < 0 || a->num_shared > 1) return SMOE_ERR_UNSUPPORTED;
   const int Fs = a->num_shared ? a->d_ff_shared : 0;
   if (a->num_shared && (Fs < 1 || Fs % 8 != 0 || !a->sw1 || !a->sw3 || !a->sw2t || !a->sw13t || !a->dsw13 || !a->dsw2))
     return SMOE_ERR_INVALID;
-  if (!a->gate_w || !a->w1 || !a->w3 || !a->w2t || !a->w13t || !a->dgate || !a->dw13 || !a->dw2)
+  if (!a->gate_w || !a->dgate) return SMOE_ERR_INVALID;
+  if (lin ? (!a->w_lin_t || !a->dw_lin) : (!a->w1 || !a->w3 || !a->w2t || !a->w13t || !a->dw13 || !a->dw2))
     return SMOE_ERR_INVALID;
   if (T > 0 && (!a->x || !a->dout || !a->dx)) return SMOE_ERR_INVALID;
   BwdPlan p;
@@ -1166,8 +1218,12 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   if (!a->workspace || a->workspace_bytes < p.total) return SMOE_ERR_WORKSPACE;
   if (T == 0) {  // no tokens: every gradient is zero
     SMOE_CK(cudaMemsetAsync(a->dgate, 0, (size_t)E * d * 4, st));
-    SMOE_CK(cudaMemsetAsync(a->dw13, 0, (size_t)E * 2 * F * d * 4, st));
-    SMOE_CK(cudaMemsetAsync(a->dw2, 0, (size_t)E * d * F * 4, st));
+    if (lin) {
+      SMOE_CK(cudaMemsetAsync(a->dw_lin, 0, (size_t)E * d * d * 4, st));
+    } else {
+      SMOE_CK(cudaMemsetAsync(a->dw13, 0, (size_t)E * 2 * F * d * 4, st));
+      SMOE_CK(cudaMemsetAsync(a->dw2, 0, (size_t)E * d * F * 4, st));
+    }
     if (Fs) {
       SMOE_CK(cudaMemsetAsync(a->dsw13, 0, (size_t)2 * Fs * d * 4, st));
       SMOE_CK(cudaMemsetAsync(a->dsw2, 0, (size_t)d * Fs * 4, st));
@@ -1206,6 +1262,21 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   slot_weights_to_rows_kernel<<<(unsigned)std::min<int64_t>(cdiv((int64_t)T * k, 256), (int64_t)device_sms() * 8), 256,
                                 0, st>>>(slot_row, w, (int64_t)T * k, row_w);
   SMOE_CK(cudaGetLastError());
+  if (lin) {  // g = dout_r Wl; the element-wise step turns it into the rows' input gradient
+    if ((rc = grouped_gemm_impl(dr, a->w_lin_t, nullptr, g, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, S, d, d, st)))
+      return rc;
+    rc = dt == SMOE_BF16 ? linear_bwd_launch<__nv_bfloat16>(g, xr, dr, row_w, offsets + E, S, d, dw_row, st)
+                         : linear_bwd_launch<__half>(g, xr, dr, row_w, offsets + E, S, d, dw_row, st);
+    if (rc) return rc;
+    if ((rc = bwd_shared(a, p, ws, st))) return rc;
+    rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, g, st) : bwd_tail<__half>(a, p, ws, g, st);
+    if (rc) return rc;
+    if ((rc = transpose16(xr, ws + p.o_xrt, S, d, S8, st))) return rc;
+    if ((rc = transpose16(dr, ws + p.o_drt, S, d, S8, st))) return rc;
+    return a->dw_lin_transposed
+               ? smoe_wgrad_gemm(ws + p.o_xrt, S8, ws + p.o_drt, S8, dt, offsets, E, d, d, S, a->dw_lin, stream)
+               : smoe_wgrad_gemm(ws + p.o_drt, S8, ws + p.o_xrt, S8, dt, offsets, E, d, d, S, a->dw_lin, stream);
+  }
   // recomputed pre-activations, the gradient reaching h, the element-wise backward
   if ((rc = grouped_gemm_impl(xr, a->w1, a->w3, ab, dt, dt, SMOE_EPI_GATEUP, offsets, nullptr, E, S, F, d, st))) return rc;
   if ((rc = grouped_gemm_impl(dr, a->w2t, nullptr, g, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, S, F, d, st))) return rc;
@@ -1215,34 +1286,9 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   // input gradient of the routed rows: [da | db] against [W1 | W3]
   if ((rc = grouped_gemm_impl(ab, a->w13t, nullptr, dxr, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, S, d, 2 * F, st)))
     return rc;
-  if (Fs) {  // shared expert: one group of all T rows, weight 1
-    int32_t* soff = reinterpret_cast<int32_t*>(ws + p.o_soff);
-    fill_two_kernel<<<1, 1, 0, st>>>(soff, 0, T);
-    SMOE_CK(cudaGetLastError());
-    void* abs_ = ws + p.o_abs;
-    void* gs = ws + p.o_gs;
-    if ((rc = grouped_gemm_impl(a->x, a->sw1, a->sw3, abs_, dt, dt, SMOE_EPI_GATEUP, soff, nullptr, 1, T, Fs, d, st)))
-      return rc;
-    if ((rc = grouped_gemm_impl(a->dout, a->sw2t, nullptr, gs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, Fs, d, st)))
-      return rc;
-    rc = dt == SMOE_BF16 ? swiglu_bwd_launch<__nv_bfloat16>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st)
-                         : swiglu_bwd_launch<__half>(abs_, gs, nullptr, nullptr, T, Fs, nullptr, st);
-    if (rc) return rc;
-    if ((rc = grouped_gemm_impl(abs_, a->sw13t, nullptr, ws + p.o_dxs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, d,
-                                2 * Fs, st)))
-      return rc;
-    // weight gradients of the shared expert: K = the T tokens
-    const int64_t T8 = p.T8;
-    if ((rc = transpose16(a->x, ws + p.o_xt, T, d, T8, st))) return rc;
-    if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, T8, st))) return rc;
-    if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, T8, st))) return rc;
-    if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, T8, st))) return rc;
-    if ((rc = smoe_wgrad_gemm(ws + p.o_abst, T8, ws + p.o_xt, T8, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
-      return rc;
-    if ((rc = smoe_wgrad_gemm(ws + p.o_dot, T8, ws + p.o_gst, T8, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
-  }
+  if ((rc = bwd_shared(a, p, ws, st))) return rc;
   // dx (routed rows + shared expert + router) and the gate's gradient
-  rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, st) : bwd_tail<__half>(a, p, ws, st);
+  rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, dxr, st) : bwd_tail<__half>(a, p, ws, dxr, st);
   if (rc) return rc;
   // expert weight gradients: K runs over the routed rows, grouped by expert
   if ((rc = transpose16(xr, ws + p.o_xrt, S, d, S8, st))) return rc;

@@ -128,7 +128,10 @@ class UltimateMoE(MoECore):
 
     def _param_grads(self, g):
         out = [g["gate"].to(self.gate_weight.dtype)]
-        out += [g[n].to(self.compute_dtype) for n in ("w1", "w3", "w2")]
+        if self.expert_type == "swiglu":
+            out += [g[n].to(self.compute_dtype) for n in ("w1", "w3", "w2")]
+        else:
+            out.append(g["expert_w"].to(self.compute_dtype))
         if self.num_shared_experts:
             out += [g[n].to(self.compute_dtype) for n in ("sw1", "sw3", "sw2")]
         return out
@@ -140,6 +143,9 @@ class UltimateMoE(MoECore):
     def _linear_kmajor(self):
         w = self.expert_weights
         return self._cached("lin", [w], lambda: K.transpose_batched(w.detach().contiguous()))
+
+    def _linear_xw(self):
+        return self.expert_weights.detach(), True
 
     def _swiglu(self):
         return self.w1, self.w3, self.w2

@@ -139,10 +139,49 @@ def test_standard_moe_gradients_reach_each_expert(K):
 
 
 @pytest.mark.autograd
-def test_backward_outside_its_scope_raises():
-    """Layers the backward does not cover fail loudly in backward, not with wrong grads."""
+@pytest.mark.parametrize("cls,T,d,E,k,cf", [("UltimateMoE", 300, 256, 8, 2, None), ("StandardMoE", 257, 128, 16, 2, 0.5),
+                                            ("UltimateMoE", 100, 128, 8, 3, None)])
+def test_linear_layer_backward_matches_oracle(K, cls, T, d, E, k, cf):
+    """The reference's own expert type (a bias-free d x d linear): UltimateMoE's x @ W
+    parameter and StandardMoE's per-expert nn.Linear weights, against moe_backward."""
     import swiftmoe_b200 as S
-    m = S.UltimateMoE(8, 64, use_fp16=False, dtype=torch.bfloat16).cuda()       # linear experts
-    out = m(torch.randn(16, 64, device="cuda", dtype=torch.bfloat16))
+    dt = torch.bfloat16
+    W = synth.normal(7, (E, d, d), 0.05)                 # x @ W layout [d_in, d_out]
+    gw = synth.normal(8, (E, d), 0.1)
+    x = rounded(synth.normal(9, (T, d), 1.0), dt)
+    dout = rounded(synth.normal(10, (T, d), 1.0), dt)
+    if cls == "UltimateMoE":
+        m = S.UltimateMoE(E, d, use_fp16=False, dtype=dt, top_k=k, capacity_factor=cf).cuda()
+        with torch.no_grad():
+            m.gate_weight.copy_(torch.from_numpy(gw)); m.expert_weights.copy_(torch.from_numpy(W))
+        gate_p = m.gate_weight
+    else:
+        m = S.StandardMoE(E, d, use_fp16=False, dtype=dt, top_k=k, capacity_factor=cf).cuda()
+        with torch.no_grad():
+            m.gate.weight.copy_(torch.from_numpy(gw))
+            for i in range(E):
+                m.experts[i].weight.copy_(torch.from_numpy(W[i].T.copy()))
+        gate_p = m.gate.weight
+    xt = torch.from_numpy(x).to("cuda", dt).requires_grad_(True)
+    m(xt).backward(torch.from_numpy(dout).to("cuda", dt))
+    idx, w = K.router(xt.detach(), gate_p.detach(), k)
+    p = O.MoEParams(gate=rounded(gw, dt), expert_type="linear", expert_w=rounded(W, dt))
+    ref = O.moe_backward(x, p, dout, k=k, capacity_factor=cf, routing=(idx.cpu().numpy(), w.cpu().numpy()))
+    if cls == "UltimateMoE":
+        dW = m.expert_weights.grad.float().cpu().numpy()
+    else:
+        dW = np.stack([m.experts[i].weight.grad.float().cpu().numpy().T for i in range(E)])
+    assert max_rel_err(xt.grad.float().cpu().numpy(), ref["x"]) <= 2e-2
+    assert max_rel_err(gate_p.grad.float().cpu().numpy(), ref["gate"]) <= 2e-2
+    assert max_rel_err(dW, ref["expert_w"]) <= 2e-2
+    assert K.read_device_error(torch.device("cuda", 0)) == 0
+
+
+@pytest.mark.autograd
+def test_backward_outside_its_scope_raises():
+    """Layers the backward does not cover (fp32) fail loudly in backward, not with wrong grads."""
+    import swiftmoe_b200 as S
+    m = S.UltimateMoE(8, 64, use_fp16=False, expert_type="swiglu", d_ff=128).cuda()      # fp32
+    out = m(torch.randn(16, 64, device="cuda"))
     with pytest.raises(NotImplementedError):
         out.sum().backward()

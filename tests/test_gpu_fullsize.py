@@ -14,24 +14,36 @@ pytestmark = pytest.mark.gpu
 
 
 @torch.no_grad()
-def _fp32_reference_tokens(x, gate, w1, w3, w2, k, tok, bias=None, shared=None):
-    """Layer output of the tokens `tok`, everything in fp32 (torch, on the GPU)."""
+def _fp32_reference_tokens(x, gate, w1, w3, w2, idx, tok, bias=None, shared=None):
+    """Layer output of the tokens `tok` in fp32 (torch matmuls on the GPU) on the routing
+    `idx` the layer chose (weights: softmax of the fp32 logits of those experts), and the
+    fp32 router's own top-k for the routing check."""
     xs = x[tok].float()
     logits = xs @ gate.float().T
     if bias is not None:
         logits = logits + bias.float()
-    v, idx = torch.topk(logits, k, dim=-1)
-    w = torch.softmax(v, dim=-1)
+    k = idx.shape[1]
+    sel = idx[tok].long()
+    w = torch.softmax(logits.gather(1, sel), dim=-1)
     out = torch.zeros_like(xs)
-    for j in range(k):
-        for n in range(xs.shape[0]):
-            e = int(idx[n, j])
-            h = torch.nn.functional.silu(xs[n] @ w1[e].float().T) * (xs[n] @ w3[e].float().T)
-            out[n] += w[n, j] * (h @ w2[e].float().T)
+    for e in torch.unique(sel).tolist():
+        rows, slots = torch.nonzero(sel == e, as_tuple=True)
+        h = torch.nn.functional.silu(xs[rows] @ w1[e].float().T) * (xs[rows] @ w3[e].float().T)
+        out.index_add_(0, rows, (h @ w2[e].float().T) * w[rows, slots].view(-1, 1))
     if shared is not None:
         s1, s3, s2 = (t.float() for t in shared)
         out += (torch.nn.functional.silu(xs @ s1.T) * (xs @ s3.T)) @ s2.T
-    return out, idx
+    return out, torch.topk(logits, k, dim=-1).indices, logits
+
+
+def _check_routing(idx_tok, ridx, logits, rtol=1e-4):
+    """Rows whose expert sets differ from the fp32 top-k must be near-ties of the fp32 logits."""
+    a = torch.sort(idx_tok.long(), 1)[0]
+    b = torch.sort(ridx, 1)[0]
+    for n in torch.nonzero((a != b).any(1)).flatten().tolist():
+        va = torch.sort(logits[n, a[n]])[0]
+        vb = torch.sort(logits[n, b[n]])[0]
+        assert (va - vb).abs().max().item() <= rtol * logits[n].abs().max().item(), n
 
 
 def _layer(E, d, F, k, dev, seed, shared=False):
@@ -43,18 +55,19 @@ def _layer(E, d, F, k, dev, seed, shared=False):
 
 @pytest.mark.parametrize("T", [16384, 1, 8, 64, 256])
 def test_mixtral_shape_token_sample(T):
-    """d 4096, 8 experts, top-2, SwiGLU 14336: the bench layer and the decode sweep."""
+    """d 4096, 8 experts, top-2, SwiGLU 14336: the bench layer and the decode sweep; every
+    sampled token is compared (on the layer's own routing), and the routing itself must
+    match the fp32 top-k except at near-ties."""
     dev = torch.device("cuda", 0)
     m = _layer(8, 4096, 14336, 2, dev, seed=0)
     x = torch.randn(T, 4096, device=dev, dtype=torch.bfloat16, generator=torch.Generator(dev).manual_seed(1))
     out = m(x)
-    tok = torch.randperm(T, generator=torch.Generator().manual_seed(2))[:24].to(dev)
-    ref, ridx = _fp32_reference_tokens(x, m.gate_weight, m.w1, m.w3, m.w2, 2, tok)
+    tok = torch.randperm(T, generator=torch.Generator().manual_seed(2))[:64].to(dev)
     from swiftmoe_b200 import kernels
     idx, _ = kernels.router(x, m.gate_weight, 2)
-    same = (torch.sort(idx[tok].long(), 1)[0] == torch.sort(ridx, 1)[0]).all(1).cpu().numpy()
-    assert same.mean() > 0.9
-    assert max_rel_err(out[tok].float().cpu().numpy()[same], ref.cpu().numpy()[same]) <= 2e-2
+    ref, ridx, logits = _fp32_reference_tokens(x, m.gate_weight, m.w1, m.w3, m.w2, idx, tok)
+    _check_routing(idx[tok], ridx, logits)
+    assert max_rel_err(out[tok].float().cpu().numpy(), ref.cpu().numpy()) <= 2e-2
 
 
 def test_fine_grained_shape_token_sample():
@@ -66,14 +79,13 @@ def test_fine_grained_shape_token_sample():
     m.set_logit_bias(bias)
     x = torch.randn(32768, 2048, device=dev, dtype=torch.bfloat16, generator=torch.Generator(dev).manual_seed(4))
     out = m(x)
-    tok = torch.randperm(32768, generator=torch.Generator().manual_seed(5))[:16].to(dev)
-    ref, ridx = _fp32_reference_tokens(x, m.gate_weight, m.w1, m.w3, m.w2, 8, tok, bias=m.logit_bias,
-                                       shared=(m.shared_w1, m.shared_w3, m.shared_w2))
+    tok = torch.randperm(32768, generator=torch.Generator().manual_seed(5))[:64].to(dev)
     from swiftmoe_b200 import kernels
     idx, _ = kernels.router(x, m.gate_weight, 8, m.logit_bias)
-    same = (torch.sort(idx[tok].long(), 1)[0] == torch.sort(ridx, 1)[0]).all(1).cpu().numpy()
-    assert same.mean() > 0.8
-    assert max_rel_err(out[tok].float().cpu().numpy()[same], ref.cpu().numpy()[same]) <= 2e-2
+    ref, ridx, logits = _fp32_reference_tokens(x, m.gate_weight, m.w1, m.w3, m.w2, idx, tok, bias=m.logit_bias,
+                                               shared=(m.shared_w1, m.shared_w3, m.shared_w2))
+    _check_routing(idx[tok], ridx, logits)
+    assert max_rel_err(out[tok].float().cpu().numpy(), ref.cpu().numpy()) <= 2e-2
 
 
 @pytest.mark.parametrize("T,k,E,cf", [(32768, 8, 128, None), (65536, 2, 64, 1.25)])
