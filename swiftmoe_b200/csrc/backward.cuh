@@ -190,18 +190,22 @@ __global__ void __launch_bounds__(256) moe_bwd_dx_kernel(const T* __restrict__ d
   }
 }
 
-// dwg[e, c] = sum over rows r of expert e in a plan over every slot (offsets [E+1],
-// row_token) of dsel_row[r] * x[row_token[r], c], in row order (deterministic).
-// Grid: (ceil(d / 256), E).
+// Partial gate-weight gradient: part[z][e][c] = sum over the z-th of gridDim.z slices of
+// the rows of expert e in a plan over every slot (offsets [E+1], row_token) of
+// dsel_row[r] * x[row_token[r], c], in row order.  Grid: (ceil(d / 256), E, slices);
+// router_dwg_reduce_kernel adds the slices in order (deterministic).
 template <typename T>
 __global__ void __launch_bounds__(256) router_dwg_kernel(const T* __restrict__ x, const int32_t* __restrict__ row_token,
                                                          const int32_t* __restrict__ offsets,
-                                                         const float* __restrict__ dsel_row, int d,
-                                                         float* __restrict__ dwg) {
+                                                         const float* __restrict__ dsel_row, int d, int E,
+                                                         float* __restrict__ part) {
   const int e = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
-  const int r0 = offsets[e], r1 = offsets[e + 1];
+  const int e0 = offsets[e], e1 = offsets[e + 1];
+  const int len = (e1 - e0 + (int)gridDim.z - 1) / (int)gridDim.z;
+  const int r0 = min(e1, e0 + (int)blockIdx.z * len), r1 = min(e1, r0 + len);
+  float* dwg = part + (size_t)blockIdx.z * E * d;
   float acc = 0.f;
   int r = r0;
   for (; r + 4 <= r1; r += 4) {
@@ -216,6 +220,57 @@ __global__ void __launch_bounds__(256) router_dwg_kernel(const T* __restrict__ x
   }
   for (; r < r1; ++r) acc = fmaf(dsel_row[r], Num<T>::to_f(x[(size_t)row_token[r] * d + c]), acc);
   dwg[(size_t)e * d + c] = acc;
+}
+
+__global__ void __launch_bounds__(256) router_dwg_reduce_kernel(const float* __restrict__ part, int slices,
+                                                                int64_t n, float* __restrict__ dwg) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int z = 0; z < slices; ++z) s += part[(size_t)z * n + i];
+    dwg[i] = s;
+  }
+}
+
+// dst[c * ldd + r] = src[r][c] for 16-bit elements, 64 x 64 tiles, 16-byte loads and
+// stores (C % 8 == 0, ldd % 8 == 0, 16-byte aligned rows); rows past R are skipped and a
+// partial group of 8 output elements at the end of a row is written element by element.
+__global__ void __launch_bounds__(256) transpose16_vec_kernel(const uint16_t* __restrict__ src,
+                                                              uint16_t* __restrict__ dst, int64_t R, int64_t C,
+                                                              int64_t ldd) {
+  __shared__ uint16_t tile[64][64 + 8];
+  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {         // 64 rows x 8 vectors of 8 columns
+    const int v = t + i * 256;
+    const int rr = v >> 3, cv = (v & 7) * 8;
+    const int64_t r = r0 + rr, c = c0 + cv;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (r < R && c < C) u = *reinterpret_cast<const uint4*>(src + r * C + c);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tile[rr][cv + j] = e[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {         // 64 output rows (columns of src) x 8 vectors of 8 rows of src
+    const int v = t + i * 256;
+    const int cc = v >> 3, rv = (v & 7) * 8;
+    const int64_t c = c0 + cc, r = r0 + rv;
+    if (c >= C || r >= R) continue;
+    union {
+      uint4 u;
+      uint16_t e[8];
+    } o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o.e[j] = tile[rv + j][cc];
+    uint16_t* out = dst + c * ldd + r;
+    if (r + 8 <= R) {
+      *reinterpret_cast<uint4*>(out) = o.u;
+    } else {
+      for (int j = 0; j < 8 && r + j < R; ++j) out[j] = o.e[j];
+    }
+  }
 }
 
 // dst[g][c * ldd + r] = src[g][r][c] (r < R, c < C): transpose into rows of length

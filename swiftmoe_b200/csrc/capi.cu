@@ -1021,11 +1021,13 @@ int smoe_wgrad_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int 
 
 // ------------------------------------------------------------------ layer backward
 namespace {
+constexpr int64_t kDwgSlices = 32;  // row slices of the gate-gradient kernel, at most
+
 struct BwdPlan {
   int64_t S, S8, T8, rows_cap_full;
   size_t o_idx, o_w, o_cnt, o_off, o_sr, o_rt, o_pws, o_cntf, o_offf, o_srf, o_rtf, o_rws, o_xr, o_dr, o_roww,
       o_dwr, o_dsel, o_ab, o_g, o_dxr, o_xrt, o_drt, o_abt, o_gt, o_abs, o_gs, o_dxs, o_xt, o_dot, o_abst, o_gst,
-      o_soff, total;
+      o_soff, o_dwgp, total;
   size_t plan_ws, router_ws;
 };
 
@@ -1080,6 +1082,7 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   p->o_abst = take(2 * Fs * T8 * es);
   p->o_gst = take(Fs * T8 * es);
   p->o_soff = take(16);
+  p->o_dwgp = take(kDwgSlices * E * d * 4);
   p->total = o;
   return true;
 }
@@ -1095,6 +1098,13 @@ int transpose_ld(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, 
 }
 
 int transpose16(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, cudaStream_t st) {
+  if (R == 0 || C == 0) return SMOE_OK;
+  if (C % 8 == 0 && ldd % 8 == 0 && aligned16(src) && aligned16(dst) && cdiv(R, 64) <= 65535) {
+    dim3 grid((unsigned)cdiv(C, 64), (unsigned)cdiv(R, 64));
+    transpose16_vec_kernel<<<grid, 256, 0, st>>>((const uint16_t*)src, (uint16_t*)dst, R, C, ldd);
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
   return transpose_ld<unsigned short>(src, dst, R, C, ldd, st);
 }
 
@@ -1141,10 +1151,18 @@ int bwd_tail(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws, 
           reinterpret_cast<const int32_t*>(ws + p.o_srf), reinterpret_cast<float*>(ws + p.o_dsel));
     SMOE_CK(cudaGetLastError());
   }
-  dim3 g2((unsigned)cdiv(d, 256), (unsigned)E);
+  // gate gradient: row slices of every expert in parallel, then an in-order sum of the slices
+  const int64_t cols = cdiv(d, 256);
+  const int slices = (int)std::max<int64_t>(1, std::min<int64_t>(kDwgSlices, cdiv((int64_t)device_sms() * 8, cols * E)));
+  dim3 g2((unsigned)cols, (unsigned)E, (unsigned)slices);
+  float* part = reinterpret_cast<float*>(ws + p.o_dwgp);
   router_dwg_kernel<T><<<g2, 256, 0, st>>>((const T*)a->x, reinterpret_cast<const int32_t*>(ws + p.o_rtf),
                                            reinterpret_cast<const int32_t*>(ws + p.o_offf),
-                                           reinterpret_cast<const float*>(ws + p.o_dsel), (int)d, a->dgate);
+                                           reinterpret_cast<const float*>(ws + p.o_dsel), (int)d, E, part);
+  SMOE_CK(cudaGetLastError());
+  const int64_t n = (int64_t)E * d;
+  router_dwg_reduce_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)device_sms() * 8), 256, 0, st>>>(
+      part, slices, n, a->dgate);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
