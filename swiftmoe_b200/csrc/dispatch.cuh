@@ -188,7 +188,15 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const unsigned char* 
       uint4* d4 = reinterpret_cast<uint4*>(dst);
       if (t >= 0) {
         const uint4* s4 = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
-        for (int i = lane; i < nv; i += 32) d4[i] = s4[i];
+        int i = lane;
+        for (; i + 96 < nv; i += 128) {   // four 16-byte loads in flight per lane
+          const uint4 a = s4[i], b = s4[i + 32], c = s4[i + 64], e = s4[i + 96];
+          d4[i] = a;
+          d4[i + 32] = b;
+          d4[i + 64] = c;
+          d4[i + 96] = e;
+        }
+        for (; i < nv; i += 32) d4[i] = s4[i];
       } else {
         for (int i = lane; i < nv; i += 32) d4[i] = make_uint4(0, 0, 0, 0);
       }

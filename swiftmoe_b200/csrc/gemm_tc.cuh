@@ -414,18 +414,27 @@ __global__ void __launch_bounds__(THREADS, 1)
 // K tiles of a group then never reach into the next group, and every TMA K coordinate is
 // 16-byte aligned.  A start that is not is rounded down (wrong sums, no fault) and
 // reported in the device error word.  A group without rows gets zeros.
-__device__ __forceinline__ void wgrad_tile(int L, int MT, int NB, int& g, int& m0, int& n0) {
+// Tile L -> (group, m0, n0).  n_fast: the n-tiles of one m-tile run back to back, so a
+// group's B rows stay in L2 while A streams once (B the smaller operand); otherwise the
+// m-tiles of one n-tile do, keeping A resident instead.
+__device__ __forceinline__ void wgrad_tile(int L, int MT, int NB, bool n_fast, int& g, int& m0, int& n0) {
   const int per = MT * NB;
   g = L / per;
   const int local = L - g * per;
-  m0 = (local / NB) * BM;
-  n0 = (local % NB) * BN;
+  if (n_fast) {
+    m0 = (local / NB) * BM;
+    n0 = (local % NB) * BN;
+  } else {
+    m0 = (local % MT) * BM;
+    n0 = (local / MT) * BN;
+  }
 }
 
 template <typename OutT>
 __global__ void __launch_bounds__(THREADS, 1)
     wgrad_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      OutT* __restrict__ C, const int32_t* __restrict__ koff, int G, int M, int N, uint32_t idesc) {
+                      OutT* __restrict__ C, const int32_t* __restrict__ koff, int G, int M, int N, uint32_t idesc,
+                      bool n_fast) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -489,7 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
         int g, m0, n0;
-        wgrad_tile(L, MT, NB, g, m0, n0);
+        wgrad_tile(L, MT, NB, n_fast, g, m0, n0);
         for (int kb = s_kb0[g]; kb < s_kb1[g]; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
@@ -517,7 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
         int g, m0, n0;
-        wgrad_tile(L, MT, NB, g, m0, n0);
+        wgrad_tile(L, MT, NB, n_fast, g, m0, n0);
         const int kb0 = s_kb0[g], kb1 = s_kb1[g];
         if (kb1 <= kb0) continue;           // no rows: the epilogue writes zeros
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) break;
@@ -550,7 +559,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
       int g, m0, n0;
-      wgrad_tile(L, MT, NB, g, m0, n0);
+      wgrad_tile(L, MT, NB, n_fast, g, m0, n0);
       const bool row_ok = m0 + r < M;
       OutT* crow = C + ((int64_t)g * M + m0 + (row_ok ? r : 0)) * N;
       if (s_kb1[g] <= s_kb0[g]) {           // empty group: zero tile, no accumulator used

@@ -194,3 +194,92 @@ def test_ep_dedup_plan_and_meta(K, T, k, El, ws, me):
     assert (mw.cpu().numpy()[:n] == mw_r.numpy()[:n]).all()
     assert (oe.cpu().numpy()[:T] == oe_r.numpy()[:T]).all()
     assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("ws,E,cap,seed", [(2, 8, 0, 0), (4, 16, 37, 1), (8, 8, 500, 2), (8, 64, 0, 3), (4, 8, 1, 4)])
+def test_ep_layout_matches_restatement(ws, E, cap, seed):
+    """Device layout of the exchange (send addresses, kept prefixes, receive offsets,
+    return table) from a count matrix, bit for bit against its numpy restatement.  The
+    buffer bases are synthetic: the kernel only computes addresses from them."""
+    import ep_doubles
+    from swiftmoe_b200 import kernels as K
+    rng = np.random.default_rng(seed)
+    G = rng.integers(0, 300, size=(ws, E)).astype(np.int32)
+    G[rng.random((ws, E)) < 0.2] = 0                      # empty segments
+    rb = 8192
+    bases = [(np.arange(ws, dtype=np.int64) + 1) << 34, (np.arange(ws, dtype=np.int64) + 17) << 34]
+    El = E // ws
+    for me in range(ws):
+        outs = []
+        for mod, dev in ((K, "cuda"), (ep_doubles, "cpu")):
+            lay = dict(send_addr=torch.zeros(E, dtype=torch.int64, device=dev),
+                       keep=torch.zeros(E, dtype=torch.int32, device=dev),
+                       recv_offsets=torch.zeros(El + 1, dtype=torch.int32, device=dev),
+                       seg=torch.zeros(2 * El * ws + 1, dtype=torch.int64, device=dev))
+            mod.ep_layout(torch.from_numpy(G).to(dev), me, cap, torch.from_numpy(bases[0]).to(dev),
+                          torch.from_numpy(bases[1]).to(dev), rb, 10 ** 6, lay)
+            outs.append({k_: v.cpu().numpy() for k_, v in lay.items()})
+        for key in outs[0]:
+            assert (outs[0][key] == outs[1][key]).all(), (me, key)
+
+
+def test_ep_layout_overflow_guard():
+    """A receive buffer that would overflow: nothing is addressed, and the error word says so."""
+    from swiftmoe_b200 import kernels as K
+    G = torch.full((2, 4), 100, dtype=torch.int32, device="cuda")
+    base = torch.tensor([1 << 34, 2 << 34], dtype=torch.int64, device="cuda")
+    lay = dict(send_addr=torch.ones(4, dtype=torch.int64, device="cuda"), keep=torch.ones(4, dtype=torch.int32, device="cuda"),
+               recv_offsets=torch.ones(3, dtype=torch.int32, device="cuda"),
+               seg=torch.ones(9, dtype=torch.int64, device="cuda"))
+    K.read_device_error(torch.device("cuda", 0))
+    K.ep_layout(G, 0, 0, base, base, 4096, 150, lay)      # each rank would receive 200 rows
+    assert int(lay["send_addr"].abs().sum()) == 0 and int(lay["keep"].sum()) == 0
+    assert int(lay["recv_offsets"].sum()) == 0
+    assert K.read_device_error(torch.device("cuda", 0)) == 4
+
+
+@pytest.mark.parametrize("cap", [0, 40])
+def test_ep_send_rows_and_drop_slots(cap):
+    """The send kernel stores each routed row of the other ranks' experts at its place in
+    the owner's expert-major receive buffer (here: local buffers standing in for the
+    peers'), rows past the capacity cut are not sent, and drop_slots marks exactly the
+    cut slots -- against the numpy restatement."""
+    import ep_doubles
+    from swiftmoe_b200 import kernels as K
+    ws, E, T, k, d, me = 4, 8, 300, 2, 256, 1
+    El = E // ws
+    rng = np.random.default_rng(11)
+    idx = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    x = torch.randn(T, d, device="cuda").to(torch.bfloat16)
+    plan = K.dispatch_plan(torch.from_numpy(idx).cuda(), E)
+    # every rank's counts: this rank's from the plan, the others' random
+    G = rng.integers(0, 160, size=(ws, E)).astype(np.int32)
+    G[me] = plan["counts"].cpu().numpy()
+    rb = d * 2
+    rows_max = ws * T * k
+    bufs = [torch.zeros(rows_max, d, dtype=torch.bfloat16, device="cuda") for _ in range(ws)]
+    base = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    lay = dict(send_addr=torch.zeros(E, dtype=torch.int64, device="cuda"),
+               keep=torch.zeros(E, dtype=torch.int32, device="cuda"),
+               recv_offsets=torch.zeros(El + 1, dtype=torch.int32, device="cuda"),
+               seg=torch.zeros(2 * El * ws + 1, dtype=torch.int64, device="cuda"))
+    K.ep_layout(torch.from_numpy(G).cuda(), me, cap, base, base, rb, rows_max, lay)
+    K.ep_send_rows(x, plan["row_token"], plan["offsets"], me * El, El, lay["send_addr"], lay["keep"],
+                   plan["rows_cap"])
+    torch.cuda.synchronize()
+    # restatement on the host: the same layout, rows copied into host copies of the buffers
+    hb = [torch.zeros(rows_max, d, dtype=torch.bfloat16) for _ in range(ws)]
+    hbase = torch.tensor([b.data_ptr() for b in hb], dtype=torch.int64)
+    hl = dict(send_addr=torch.zeros(E, dtype=torch.int64), keep=torch.zeros(E, dtype=torch.int32),
+              recv_offsets=torch.zeros(El + 1, dtype=torch.int32), seg=torch.zeros(2 * El * ws + 1, dtype=torch.int64))
+    ep_doubles.ep_layout(torch.from_numpy(G), me, cap, hbase, hbase, rb, rows_max, hl)
+    ep_doubles.ep_send_rows(x.cpu(), plan["row_token"].cpu(), plan["offsets"].cpu(), me * El, El,
+                            hl["send_addr"], hl["keep"], plan["rows_cap"])
+    for r in range(ws):
+        assert torch.equal(bufs[r].cpu(), hb[r]), r
+    sr = plan["slot_row"].clone()
+    K.ep_drop_slots(torch.from_numpy(idx).cuda(), plan["offsets"], lay["keep"], sr)
+    sr_h = plan["slot_row"].cpu().clone()
+    ep_doubles.ep_drop_slots(torch.from_numpy(idx), plan["offsets"].cpu(), hl["keep"], sr_h)
+    assert torch.equal(sr.cpu(), sr_h)
+    assert (sr.cpu() < 0).any() == (cap > 0 and bool((G[:me + 1].sum(0) > cap).any()))
