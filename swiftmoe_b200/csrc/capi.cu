@@ -191,11 +191,11 @@ int launch_wgrad(const CUtensorMap& ma, const CUtensorMap& mb, float* C, const i
                  uint32_t idesc, cudaStream_t st) {
   static SmemGrant done;
   auto kern = tc::wgrad_gemm_kernel<float>;
-  SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES, &done));
+  SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES_ROWS, &done));
   const int64_t tiles = (int64_t)G * cdiv(M, tc::BM) * cdiv(N, tc::BN);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, device_sms()));
   // keep the smaller operand (per group: N rows of B against M rows of A) in L2
-  kern<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, C, koff, G, M, N, idesc, N <= M);
+  kern<<<grid, tc::THREADS, tc::SMEM_BYTES_ROWS, st>>>(ma, mb, C, koff, G, M, N, idesc, N <= M);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

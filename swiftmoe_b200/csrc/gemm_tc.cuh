@@ -430,6 +430,42 @@ __device__ __forceinline__ void wgrad_tile(int L, int MT, int NB, bool n_fast, i
   }
 }
 
+// fp32 tile rows through a 4 KB shared-memory stage per epilogue warp: each thread
+// holds one accumulator row (tcgen05.ld 32x32b), 32 columns (128 bytes) at a time; the
+// 16-byte pieces are XOR-swizzled by row in the stage and leave as warp stores of 4 rows
+// x 128 contiguous bytes.  Rows at or past M and columns at or past N are not written;
+// zero: store zeros instead of reading the accumulator (a group without rows).
+__device__ __forceinline__ void epilogue_f32_staged(uint32_t tbase, float* __restrict__ C, int64_t row_base, int M,
+                                                    int N, int m0_warp, int n0, unsigned char* stage, int lane,
+                                                    bool zero) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t v[32];
+    if (zero) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0u;
+    } else {
+      tmem_ld32(tbase + c * 32, v);
+      tmem_ld_wait();
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    __syncwarp();
+    const int j = lane & 7;
+    const int col = n0 + c * 32 + j * 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = i * 4 + (lane >> 3);
+      const int row = m0_warp + rr;
+      const uint4 u = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((j ^ (rr & 7)) << 4));
+      if (row < M && col < N) *reinterpret_cast<uint4*>(C + (row_base + row) * (int64_t)N + col) = u;
+    }
+    __syncwarp();
+  }
+}
+
 template <typename OutT>
 __global__ void __launch_bounds__(THREADS, 1)
     wgrad_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -445,6 +481,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   int* s_kb0 = reinterpret_cast<int*>(s_tmem + 4);  // first K tile of each group
   int* s_kb1 = s_kb0 + (MAX_GROUPS + 1);            // end K tile of each group
+  // the epilogue warps' output stages (the launch requests SMEM_BYTES_ROWS)
+  unsigned char* s_stage =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_kb1 + 2 * (MAX_GROUPS + 1)) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -553,37 +592,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // --------------------------------------------------------------- epilogue
+    static_assert(sizeof(OutT) == 4, "the weight gradients are stored in fp32");
     const int q = warp & 3;
-    const int r = q * 32 + lane;
+    unsigned char* stage = s_stage + q * ROWS_STAGE_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
       int g, m0, n0;
       wgrad_tile(L, MT, NB, n_fast, g, m0, n0);
-      const bool row_ok = m0 + r < M;
-      OutT* crow = C + ((int64_t)g * M + m0 + (row_ok ? r : 0)) * N;
+      const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16);
       if (s_kb1[g] <= s_kb0[g]) {           // empty group: zero tile, no accumulator used
-        if (row_ok) {
-          float z[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) z[j] = 0.f;
-          for (int c = 0; c < BN / 32; ++c) {
-            if constexpr (sizeof(OutT) == 4) {
-              uint32_t zu[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) zu[j] = 0u;
-              Store<float>::cols32(reinterpret_cast<float*>(crow), n0 + c * 32, N, zu);
-            } else {
-              Store16<OutT>::cols32(crow, n0 + c * 32, N, z);
-            }
-          }
-        }
+        epilogue_f32_staged(tq, reinterpret_cast<float*>(C), (int64_t)g * M, M, N, m0 + q * 32, n0, stage, lane,
+                            true);
         continue;
       }
       if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<SMOE_EPI_STORE, OutT>(tbase, crow, row_ok, n0, N);
+      const uint32_t tbase = tq + (uint32_t)(acc * BN);
+      epilogue_f32_staged(tbase, reinterpret_cast<float*>(C), (int64_t)g * M, M, N, m0 + q * 32, n0, stage, lane,
+                          false);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
