@@ -1025,7 +1025,7 @@ namespace {
 constexpr int64_t kDwgSlices = 32;  // row slices of the gate-gradient kernel, at most
 
 struct BwdPlan {
-  int64_t S, S8, T8, rows_cap_full;
+  int64_t S, Sld, Tld, rows_cap_full;
   size_t o_idx, o_w, o_cnt, o_off, o_sr, o_rt, o_pws, o_cntf, o_offf, o_srf, o_rtf, o_rws, o_xr, o_dr, o_roww,
       o_dwr, o_dsel, o_ab, o_g, o_dxr, o_xrt, o_drt, o_abt, o_gt, o_abs, o_gs, o_dxs, o_xt, o_dot, o_abst, o_gst,
       o_soff, o_dwgp, total;
@@ -1039,8 +1039,11 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = lin ? 0 : a->d_ff;
   const int64_t Fs = a->num_shared > 0 ? a->d_ff_shared : 0;
   p->S = smoe_plan_rows_cap((int)T, (int)k, (int)E, a->capacity, 64);
-  p->S8 = align_up(std::max<int64_t>(p->S, 1), 8);
-  p->T8 = align_up(std::max<int64_t>(T, 1), 8);
+  // row strides of the transposed (K-major) operands: whole 128-byte lines, so that every
+  // 64-element row of a TMA box is one L2 line (a stride off the line splits each row
+  // over two lines and doubles the requests per byte)
+  p->Sld = align_up(std::max<int64_t>(p->S, 1), 64);
+  p->Tld = align_up(std::max<int64_t>(T, 1), 64);
   p->rows_cap_full = smoe_plan_rows_cap((int)T, (int)k, (int)E, 0, 1);
   p->plan_ws = smoe_plan_workspace_size((int)T, (int)k, (int)E);
   p->router_ws = smoe_router_workspace_size((int)T, (int)d, (int)E, a->dtype);
@@ -1050,7 +1053,7 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
     o = align_up(o + bytes, 256);
     return at;
   };
-  const int64_t S = p->S, S8 = p->S8, T8 = p->T8;
+  const int64_t S = p->S, Sld = p->Sld, Tld = p->Tld;
   p->o_idx = take(T * k * 4);
   p->o_w = take(T * k * 4);
   p->o_cnt = take(E * 4);
@@ -1071,17 +1074,17 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   p->o_ab = take(S * 2 * F * es);
   p->o_g = take(S * (lin ? d : F) * es);   // linear experts: dout_r Wl, then the rows' input gradient
   p->o_dxr = take(lin ? 0 : S * d * es);
-  p->o_xrt = take(d * S8 * es);
-  p->o_drt = take(d * S8 * es);
-  p->o_abt = take(2 * F * S8 * es);
-  p->o_gt = take(F * S8 * es);
+  p->o_xrt = take(d * Sld * es);
+  p->o_drt = take(d * Sld * es);
+  p->o_abt = take(2 * F * Sld * es);
+  p->o_gt = take(F * Sld * es);
   p->o_abs = take(T * 2 * Fs * es);
   p->o_gs = take(T * Fs * es);
   p->o_dxs = take(Fs > 0 ? T * d * es : 0);
-  p->o_xt = take(Fs > 0 ? d * T8 * es : 0);
-  p->o_dot = take(Fs > 0 ? d * T8 * es : 0);
-  p->o_abst = take(2 * Fs * T8 * es);
-  p->o_gst = take(Fs * T8 * es);
+  p->o_xt = take(Fs > 0 ? d * Tld * es : 0);
+  p->o_dot = take(Fs > 0 ? d * Tld * es : 0);
+  p->o_abst = take(2 * Fs * Tld * es);
+  p->o_gst = take(Fs * Tld * es);
   p->o_soff = take(16);
   p->o_dwgp = take(kDwgSlices * E * d * 4);
   p->total = o;
@@ -1194,14 +1197,14 @@ int bwd_shared(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws
                               2 * Fs, st)))
     return rc;
   // weight gradients of the shared expert: K = the T tokens
-  const int64_t T8 = p.T8;
-  if ((rc = transpose16(a->x, ws + p.o_xt, T, d, T8, st))) return rc;
-  if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, T8, st))) return rc;
-  if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, T8, st))) return rc;
-  if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, T8, st))) return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_abst, T8, ws + p.o_xt, T8, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
+  const int64_t Tld = p.Tld;
+  if ((rc = transpose16(a->x, ws + p.o_xt, T, d, Tld, st))) return rc;
+  if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, Tld, st))) return rc;
+  if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, Tld, st))) return rc;
+  if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, Tld, st))) return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_abst, Tld, ws + p.o_xt, Tld, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
     return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_dot, T8, ws + p.o_gst, T8, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_dot, Tld, ws + p.o_gst, Tld, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
   return SMOE_OK;
 }
 
@@ -1262,7 +1265,7 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   void* ab = ws + p.o_ab;
   void* g = ws + p.o_g;
   void* dxr = ws + p.o_dxr;
-  const int64_t S = p.S, S8 = p.S8;
+  const int64_t S = p.S, Sld = p.Sld;
   int rc;
   // routing and dispatch, as in the forward (rows padded to 64 per expert for the K groups)
   rc = smoe_router_fwd(a->x, a->gate_w, dt, a->logit_bias, T, d, E, k, idx, w, nullptr, ws + p.o_rws, p.router_ws,
@@ -1290,11 +1293,11 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
     if ((rc = bwd_shared(a, p, ws, st))) return rc;
     rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, g, st) : bwd_tail<__half>(a, p, ws, g, st);
     if (rc) return rc;
-    if ((rc = transpose16(xr, ws + p.o_xrt, S, d, S8, st))) return rc;
-    if ((rc = transpose16(dr, ws + p.o_drt, S, d, S8, st))) return rc;
+    if ((rc = transpose16(xr, ws + p.o_xrt, S, d, Sld, st))) return rc;
+    if ((rc = transpose16(dr, ws + p.o_drt, S, d, Sld, st))) return rc;
     return a->dw_lin_transposed
-               ? smoe_wgrad_gemm(ws + p.o_xrt, S8, ws + p.o_drt, S8, dt, offsets, E, d, d, S, a->dw_lin, stream)
-               : smoe_wgrad_gemm(ws + p.o_drt, S8, ws + p.o_xrt, S8, dt, offsets, E, d, d, S, a->dw_lin, stream);
+               ? smoe_wgrad_gemm(ws + p.o_xrt, Sld, ws + p.o_drt, Sld, dt, offsets, E, d, d, S, a->dw_lin, stream)
+               : smoe_wgrad_gemm(ws + p.o_drt, Sld, ws + p.o_xrt, Sld, dt, offsets, E, d, d, S, a->dw_lin, stream);
   }
   // recomputed pre-activations, the gradient reaching h, the element-wise backward
   if ((rc = grouped_gemm_impl(xr, a->w1, a->w3, ab, dt, dt, SMOE_EPI_GATEUP, offsets, nullptr, E, S, F, d, st))) return rc;
@@ -1310,13 +1313,13 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, dxr, st) : bwd_tail<__half>(a, p, ws, dxr, st);
   if (rc) return rc;
   // expert weight gradients: K runs over the routed rows, grouped by expert
-  if ((rc = transpose16(xr, ws + p.o_xrt, S, d, S8, st))) return rc;
-  if ((rc = transpose16(dr, ws + p.o_drt, S, d, S8, st))) return rc;
-  if ((rc = transpose16(ab, ws + p.o_abt, S, 2 * F, S8, st))) return rc;
-  if ((rc = transpose16(g, ws + p.o_gt, S, F, S8, st))) return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_abt, S8, ws + p.o_xrt, S8, dt, offsets, E, 2 * F, d, S, a->dw13, stream)))
+  if ((rc = transpose16(xr, ws + p.o_xrt, S, d, Sld, st))) return rc;
+  if ((rc = transpose16(dr, ws + p.o_drt, S, d, Sld, st))) return rc;
+  if ((rc = transpose16(ab, ws + p.o_abt, S, 2 * F, Sld, st))) return rc;
+  if ((rc = transpose16(g, ws + p.o_gt, S, F, Sld, st))) return rc;
+  if ((rc = smoe_wgrad_gemm(ws + p.o_abt, Sld, ws + p.o_xrt, Sld, dt, offsets, E, 2 * F, d, S, a->dw13, stream)))
     return rc;
-  return smoe_wgrad_gemm(ws + p.o_drt, S8, ws + p.o_gt, S8, dt, offsets, E, d, F, S, a->dw2, stream);
+  return smoe_wgrad_gemm(ws + p.o_drt, Sld, ws + p.o_gt, Sld, dt, offsets, E, d, F, S, a->dw2, stream);
 }
 
 }  // extern "C"
