@@ -403,6 +403,13 @@ SMOE_API int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream);
 SMOE_API int smoe_wgrad_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int dtype,
                              const int32_t* k_offsets, int G, int M, int N, int64_t K, float* C,
                              smoe_stream_t stream);
+/* The same with the operands given as rows of K: A [K, lda] (its first M columns) and
+ * B [K, ldb] (first N columns), row-major -- e.g. the routed rows themselves, grouped by
+ * expert -- read as MN-major tensor-core tiles, with no transposed copy.  M, N, lda, ldb
+ * multiples of 8; rows from K on read as zeros.                                        */
+SMOE_API int smoe_wgrad_gemm_rows(const void* A, int64_t lda, const void* B, int64_t ldb, int dtype,
+                                  const int32_t* k_offsets, int G, int M, int N, int64_t K, float* C,
+                                  smoe_stream_t stream);
 
 #ifdef __cplusplus
 }

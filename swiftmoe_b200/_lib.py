@@ -94,6 +94,7 @@ SIGNATURES = {
     "smoe_layer_bwd_workspace_size": (_sz, [C.POINTER(LayerBwdArgs)]),
     "smoe_layer_bwd": (_i32, [C.POINTER(LayerBwdArgs), _vp]),
     "smoe_wgrad_gemm": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _i64, _vp, _vp]),
+    "smoe_wgrad_gemm_rows": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -231,67 +231,5 @@ __global__ void __launch_bounds__(256) router_dwg_reduce_kernel(const float* __r
   }
 }
 
-// dst[c * ldd + r] = src[r][c] for 16-bit elements, 64 x 64 tiles, 16-byte loads and
-// stores (C % 8 == 0, ldd % 8 == 0, 16-byte aligned rows); rows past R are skipped and a
-// partial group of 8 output elements at the end of a row is written element by element.
-__global__ void __launch_bounds__(256) transpose16_vec_kernel(const uint16_t* __restrict__ src,
-                                                              uint16_t* __restrict__ dst, int64_t R, int64_t C,
-                                                              int64_t ldd) {
-  __shared__ uint16_t tile[64][64 + 8];
-  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {         // 64 rows x 8 vectors of 8 columns
-    const int v = t + i * 256;
-    const int rr = v >> 3, cv = (v & 7) * 8;
-    const int64_t r = r0 + rr, c = c0 + cv;
-    uint4 u = make_uint4(0u, 0u, 0u, 0u);
-    if (r < R && c < C) u = *reinterpret_cast<const uint4*>(src + r * C + c);
-    const uint16_t* e = reinterpret_cast<const uint16_t*>(&u);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) tile[rr][cv + j] = e[j];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {         // 64 output rows (columns of src) x 8 vectors of 8 rows of src
-    const int v = t + i * 256;
-    const int cc = v >> 3, rv = (v & 7) * 8;
-    const int64_t c = c0 + cc, r = r0 + rv;
-    if (c >= C || r >= R) continue;
-    union {
-      uint4 u;
-      uint16_t e[8];
-    } o;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o.e[j] = tile[rv + j][cc];
-    uint16_t* out = dst + c * ldd + r;
-    if (r + 8 <= R) {
-      *reinterpret_cast<uint4*>(out) = o.u;
-    } else {
-      for (int j = 0; j < 8 && r + j < R; ++j) out[j] = o.e[j];
-    }
-  }
-}
-
-// dst[g][c * ldd + r] = src[g][r][c] (r < R, c < C): transpose into rows of length
-// ldd >= R (the K-major operands of the weight-gradient GEMMs need 16-byte row strides).
-template <typename T>
-__global__ void __launch_bounds__(256) transpose_ld_kernel(const T* __restrict__ src, T* __restrict__ dst, int R,
-                                                           int C, int64_t ldd) {
-  __shared__ T tile[32][33];
-  const int g = blockIdx.z;
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
-  const T* s = src + (size_t)g * R * C;
-  T* o = dst + (size_t)g * C * ldd;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int r = r0 + i, c = c0 + threadIdx.x;
-    if (r < R && c < C) tile[i][threadIdx.x] = s[(size_t)r * C + c];
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int c = c0 + i, r = r0 + threadIdx.x;
-    if (r < R && c < C) o[(size_t)c * ldd + r] = tile[threadIdx.x][i];
-  }
-}
 
 }  // namespace smoe

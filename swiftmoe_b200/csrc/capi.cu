@@ -126,6 +126,22 @@ bool make_map_2d_ld(CUtensorMap* m, const void* base, CUtensorMapDataType dt, in
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over a row-major [rows, ld] 16-bit matrix whose first `cols` columns are used,
+// box = 64 columns x `box_rows` rows, 128 B swizzle (MN-major operand tiles: the columns
+// are the M or N elements, the rows the K index).  Rows from `rows` on read as zeros.
+bool make_map_2d_box(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 3-D map over [G, N, K] weights; box = 64 (K) x 128 (N) x 1 group.
 bool make_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t G, int64_t N, int64_t K) {
   EncodeTiledFn enc = encode_fn();
@@ -187,10 +203,11 @@ int launch_tc_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return SMOE_OK;
 }
 
+template <bool MN>
 int launch_wgrad(const CUtensorMap& ma, const CUtensorMap& mb, float* C, const int32_t* koff, int G, int M, int N,
                  uint32_t idesc, cudaStream_t st) {
   static SmemGrant done;
-  auto kern = tc::wgrad_gemm_kernel<float>;
+  auto kern = tc::wgrad_gemm_kernel<float, MN>;
   SMOE_CK(ensure_smem(kern, tc::SMEM_BYTES_ROWS, &done));
   const int64_t tiles = (int64_t)G * cdiv(M, tc::BM) * cdiv(N, tc::BN);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, device_sms()));
@@ -1015,7 +1032,22 @@ int smoe_wgrad_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int 
   if (!make_map_2d_ld(&ma, A, dt, M, std::max<int64_t>(K, 1), lda)) return SMOE_ERR_CUDA;
   if (!make_map_2d_ld(&mb, B, dt, N, std::max<int64_t>(K, 1), ldb)) return SMOE_ERR_CUDA;
   const uint32_t idesc = umma_idesc_f16(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
-  return launch_wgrad(ma, mb, C, k_offsets, G, M, N, idesc, (cudaStream_t)stream);
+  return launch_wgrad<false>(ma, mb, C, k_offsets, G, M, N, idesc, (cudaStream_t)stream);
+}
+
+int smoe_wgrad_gemm_rows(const void* A, int64_t lda, const void* B, int64_t ldb, int dtype, const int32_t* k_offsets,
+                         int G, int M, int N, int64_t K, float* C, smoe_stream_t stream) {
+  if (!A || !B || !k_offsets || !C || G < 1 || G > tc::MAX_GROUPS || M < 1 || N < 1 || K < 0) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (lda < M || ldb < N || lda % 8 != 0 || ldb % 8 != 0 || M % 8 != 0 || N % 8 != 0) return SMOE_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return SMOE_ERR_UNSUPPORTED;
+  const CUtensorMapDataType dt = dtype == SMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mb;
+  // an empty K range still needs a valid map: one row, never loaded
+  if (!make_map_2d_box(&ma, A, dt, std::max<int64_t>(K, 1), M, lda, tc::BK)) return SMOE_ERR_CUDA;
+  if (!make_map_2d_box(&mb, B, dt, std::max<int64_t>(K, 1), N, ldb, tc::BK)) return SMOE_ERR_CUDA;
+  const uint32_t idesc = umma_idesc_f16_mn(dtype == SMOE_BF16 ? 1u : 0u, tc::BM, tc::BN);
+  return launch_wgrad<true>(ma, mb, C, k_offsets, G, M, N, idesc, (cudaStream_t)stream);
 }
 
 }  // extern "C"
@@ -1025,10 +1057,9 @@ namespace {
 constexpr int64_t kDwgSlices = 32;  // row slices of the gate-gradient kernel, at most
 
 struct BwdPlan {
-  int64_t S, Sld, Tld, rows_cap_full;
+  int64_t S, rows_cap_full;
   size_t o_idx, o_w, o_cnt, o_off, o_sr, o_rt, o_pws, o_cntf, o_offf, o_srf, o_rtf, o_rws, o_xr, o_dr, o_roww,
-      o_dwr, o_dsel, o_ab, o_g, o_dxr, o_xrt, o_drt, o_abt, o_gt, o_abs, o_gs, o_dxs, o_xt, o_dot, o_abst, o_gst,
-      o_soff, o_dwgp, total;
+      o_dwr, o_dsel, o_ab, o_g, o_dxr, o_abs, o_gs, o_dxs, o_soff, o_dwgp, total;
   size_t plan_ws, router_ws;
 };
 
@@ -1039,11 +1070,6 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   const int64_t T = a->tokens, d = a->d_model, E = a->num_experts, k = a->top_k, F = lin ? 0 : a->d_ff;
   const int64_t Fs = a->num_shared > 0 ? a->d_ff_shared : 0;
   p->S = smoe_plan_rows_cap((int)T, (int)k, (int)E, a->capacity, 64);
-  // row strides of the transposed (K-major) operands: whole 128-byte lines, so that every
-  // 64-element row of a TMA box is one L2 line (a stride off the line splits each row
-  // over two lines and doubles the requests per byte)
-  p->Sld = align_up(std::max<int64_t>(p->S, 1), 64);
-  p->Tld = align_up(std::max<int64_t>(T, 1), 64);
   p->rows_cap_full = smoe_plan_rows_cap((int)T, (int)k, (int)E, 0, 1);
   p->plan_ws = smoe_plan_workspace_size((int)T, (int)k, (int)E);
   p->router_ws = smoe_router_workspace_size((int)T, (int)d, (int)E, a->dtype);
@@ -1053,7 +1079,7 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
     o = align_up(o + bytes, 256);
     return at;
   };
-  const int64_t S = p->S, Sld = p->Sld, Tld = p->Tld;
+  const int64_t S = p->S;
   p->o_idx = take(T * k * 4);
   p->o_w = take(T * k * 4);
   p->o_cnt = take(E * 4);
@@ -1074,42 +1100,13 @@ bool bwd_plan(const smoe_layer_bwd_args* a, BwdPlan* p) {
   p->o_ab = take(S * 2 * F * es);
   p->o_g = take(S * (lin ? d : F) * es);   // linear experts: dout_r Wl, then the rows' input gradient
   p->o_dxr = take(lin ? 0 : S * d * es);
-  p->o_xrt = take(d * Sld * es);
-  p->o_drt = take(d * Sld * es);
-  p->o_abt = take(2 * F * Sld * es);
-  p->o_gt = take(F * Sld * es);
   p->o_abs = take(T * 2 * Fs * es);
   p->o_gs = take(T * Fs * es);
   p->o_dxs = take(Fs > 0 ? T * d * es : 0);
-  p->o_xt = take(Fs > 0 ? d * Tld * es : 0);
-  p->o_dot = take(Fs > 0 ? d * Tld * es : 0);
-  p->o_abst = take(2 * Fs * Tld * es);
-  p->o_gst = take(Fs * Tld * es);
   p->o_soff = take(16);
   p->o_dwgp = take(kDwgSlices * E * d * 4);
   p->total = o;
   return true;
-}
-
-template <typename T>
-int transpose_ld(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, cudaStream_t st) {
-  if (R == 0 || C == 0) return SMOE_OK;
-  if (R > INT32_MAX || C > INT32_MAX || cdiv(R, 32) > 65535) return SMOE_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(R, 32), 1), block(32, 8);
-  transpose_ld_kernel<T><<<grid, block, 0, st>>>((const T*)src, (T*)dst, (int)R, (int)C, ldd);
-  SMOE_CK(cudaGetLastError());
-  return SMOE_OK;
-}
-
-int transpose16(const void* src, void* dst, int64_t R, int64_t C, int64_t ldd, cudaStream_t st) {
-  if (R == 0 || C == 0) return SMOE_OK;
-  if (C % 8 == 0 && ldd % 8 == 0 && aligned16(src) && aligned16(dst) && cdiv(R, 64) <= 65535) {
-    dim3 grid((unsigned)cdiv(C, 64), (unsigned)cdiv(R, 64));
-    transpose16_vec_kernel<<<grid, 256, 0, st>>>((const uint16_t*)src, (uint16_t*)dst, R, C, ldd);
-    SMOE_CK(cudaGetLastError());
-    return SMOE_OK;
-  }
-  return transpose_ld<unsigned short>(src, dst, R, C, ldd, st);
 }
 
 template <typename T>
@@ -1196,15 +1193,9 @@ int bwd_shared(const smoe_layer_bwd_args* a, const BwdPlan& p, unsigned char* ws
   if ((rc = grouped_gemm_impl(abs_, a->sw13t, nullptr, ws + p.o_dxs, dt, dt, SMOE_EPI_STORE, soff, nullptr, 1, T, d,
                               2 * Fs, st)))
     return rc;
-  // weight gradients of the shared expert: K = the T tokens
-  const int64_t Tld = p.Tld;
-  if ((rc = transpose16(a->x, ws + p.o_xt, T, d, Tld, st))) return rc;
-  if ((rc = transpose16(a->dout, ws + p.o_dot, T, d, Tld, st))) return rc;
-  if ((rc = transpose16(abs_, ws + p.o_abst, T, 2 * Fs, Tld, st))) return rc;
-  if ((rc = transpose16(gs, ws + p.o_gst, T, Fs, Tld, st))) return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_abst, Tld, ws + p.o_xt, Tld, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream)))
-    return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_dot, Tld, ws + p.o_gst, Tld, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
+  // weight gradients of the shared expert: K = the T tokens, rows read as they are
+  if ((rc = smoe_wgrad_gemm_rows(abs_, 2 * Fs, a->x, d, dt, soff, 1, 2 * Fs, d, T, a->dsw13, stream))) return rc;
+  if ((rc = smoe_wgrad_gemm_rows(a->dout, d, gs, Fs, dt, soff, 1, d, Fs, T, a->dsw2, stream))) return rc;
   return SMOE_OK;
 }
 
@@ -1265,7 +1256,7 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   void* ab = ws + p.o_ab;
   void* g = ws + p.o_g;
   void* dxr = ws + p.o_dxr;
-  const int64_t S = p.S, Sld = p.Sld;
+  const int64_t S = p.S;
   int rc;
   // routing and dispatch, as in the forward (rows padded to 64 per expert for the K groups)
   rc = smoe_router_fwd(a->x, a->gate_w, dt, a->logit_bias, T, d, E, k, idx, w, nullptr, ws + p.o_rws, p.router_ws,
@@ -1293,11 +1284,8 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
     if ((rc = bwd_shared(a, p, ws, st))) return rc;
     rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, g, st) : bwd_tail<__half>(a, p, ws, g, st);
     if (rc) return rc;
-    if ((rc = transpose16(xr, ws + p.o_xrt, S, d, Sld, st))) return rc;
-    if ((rc = transpose16(dr, ws + p.o_drt, S, d, Sld, st))) return rc;
-    return a->dw_lin_transposed
-               ? smoe_wgrad_gemm(ws + p.o_xrt, Sld, ws + p.o_drt, Sld, dt, offsets, E, d, d, S, a->dw_lin, stream)
-               : smoe_wgrad_gemm(ws + p.o_drt, Sld, ws + p.o_xrt, Sld, dt, offsets, E, d, d, S, a->dw_lin, stream);
+    return a->dw_lin_transposed ? smoe_wgrad_gemm_rows(xr, d, dr, d, dt, offsets, E, d, d, S, a->dw_lin, stream)
+                                : smoe_wgrad_gemm_rows(dr, d, xr, d, dt, offsets, E, d, d, S, a->dw_lin, stream);
   }
   // recomputed pre-activations, the gradient reaching h, the element-wise backward
   if ((rc = grouped_gemm_impl(xr, a->w1, a->w3, ab, dt, dt, SMOE_EPI_GATEUP, offsets, nullptr, E, S, F, d, st))) return rc;
@@ -1312,14 +1300,10 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   // dx (routed rows + shared expert + router) and the gate's gradient
   rc = dt == SMOE_BF16 ? bwd_tail<__nv_bfloat16>(a, p, ws, dxr, st) : bwd_tail<__half>(a, p, ws, dxr, st);
   if (rc) return rc;
-  // expert weight gradients: K runs over the routed rows, grouped by expert
-  if ((rc = transpose16(xr, ws + p.o_xrt, S, d, Sld, st))) return rc;
-  if ((rc = transpose16(dr, ws + p.o_drt, S, d, Sld, st))) return rc;
-  if ((rc = transpose16(ab, ws + p.o_abt, S, 2 * F, Sld, st))) return rc;
-  if ((rc = transpose16(g, ws + p.o_gt, S, F, Sld, st))) return rc;
-  if ((rc = smoe_wgrad_gemm(ws + p.o_abt, Sld, ws + p.o_xrt, Sld, dt, offsets, E, 2 * F, d, S, a->dw13, stream)))
-    return rc;
-  return smoe_wgrad_gemm(ws + p.o_drt, Sld, ws + p.o_gt, Sld, dt, offsets, E, d, F, S, a->dw2, stream);
+  // expert weight gradients: K runs over the routed rows, grouped by expert (rows read as
+  // they are, as MN-major tiles)
+  if ((rc = smoe_wgrad_gemm_rows(ab, 2 * F, xr, d, dt, offsets, E, 2 * F, d, S, a->dw13, stream))) return rc;
+  return smoe_wgrad_gemm_rows(dr, d, g, F, dt, offsets, E, d, F, S, a->dw2, stream);
 }
 
 }  // extern "C"

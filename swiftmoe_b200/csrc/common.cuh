@@ -271,9 +271,26 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand tile stored with the 128-byte swizzle:
+// atoms of 64 MN-elements (128 bytes) x 8 K-rows (1024 bytes); lbo = bytes between atoms
+// along MN, sbo = bytes between atoms along K.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);        // start address
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;     // leading (MN) byte offset
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;     // stride (K) byte offset
+  d |= static_cast<uint64_t>(1u) << 46;                       // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                       // layout: 128-byte swizzle
+  return d;
+}
+
 // Instruction descriptor: D fp32, A/B 16-bit (ab_fmt 0 = fp16, 1 = bf16), both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_fmt, uint32_t M, uint32_t N) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+// The same with both operands MN-major (the transpose-A and transpose-B bits).
+__host__ __device__ constexpr uint32_t umma_idesc_f16_mn(uint32_t ab_fmt, uint32_t M, uint32_t N) {
+  return umma_idesc_f16(ab_fmt, M, N) | (1u << 15) | (1u << 16);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, single CTA, issued by one thread.

@@ -417,6 +417,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Tile L -> (group, m0, n0).  n_fast: the n-tiles of one m-tile run back to back, so a
 // group's B rows stay in L2 while A streams once (B the smaller operand); otherwise the
 // m-tiles of one n-tile do, keeping A resident instead.
+constexpr uint32_t kMnBox = 64 * BK * 2;  // one 64 x 64 MN-major box: 8 KB
+
 __device__ __forceinline__ void wgrad_tile(int L, int MT, int NB, bool n_fast, int& g, int& m0, int& n0) {
   const int per = MT * NB;
   g = L / per;
@@ -466,7 +468,12 @@ __device__ __forceinline__ void epilogue_f32_staged(uint32_t tbase, float* __res
   }
 }
 
-template <typename OutT>
+// MN = true: A and B are given as rows of K ([K, M] and [K, N], M / N contiguous: the
+// routed rows as they are) and are read as MN-major tiles -- TMA boxes of 64 MN-elements x
+// 64 K-rows, two for the 128 A columns and four for the 256 B columns of a tile, each box
+// one 8 KB region of 8 swizzle atoms along K -- instead of K-major boxes of transposed
+// copies.  MN = false: A [M, K] and B [N, K], K-major.
+template <typename OutT, bool MN>
 __global__ void __launch_bounds__(THREADS, 1)
     wgrad_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       OutT* __restrict__ C, const int32_t* __restrict__ koff, int G, int M, int N, uint32_t idesc,
@@ -542,10 +549,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
-          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, m0);
-          tma_load_2d(b_dst, &tmB, fb, kb * BK, n0);
-          tma_load_2d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128);
+          if constexpr (MN) {
+            tma_load_2d(a_dst, &tmA, fb, m0, kb * BK);
+            tma_load_2d(a_dst + kMnBox, &tmA, fb, m0 + 64, kb * BK);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tma_load_2d(b_dst + i * kMnBox, &tmB, fb, n0 + 64 * i, kb * BK);
+          } else {
+            tma_load_2d(a_dst, &tmA, fb, kb * BK, m0);
+            tma_load_2d(b_dst, &tmB, fb, kb * BK, n0);
+            tma_load_2d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -574,11 +589,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, s_abort)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
-          const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > kb0 || kk != 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t a_desc, b_desc;
+            if constexpr (MN) {   // K step of 16 rows = two 1 KB atoms along K
+              a_desc = umma_desc_mn_sw128(smem_u32(sA + stage * A_BYTES) + kk * 2048, kMnBox, 1024);
+              b_desc = umma_desc_mn_sw128(smem_u32(sB + stage * B_BYTES) + kk * 2048, kMnBox, 1024);
+            } else {              // K step of 16 elements = 32 bytes inside the 128-byte rows
+              a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES)) + 2 * kk;
+              b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES)) + 2 * kk;
+            }
+            umma_f16(d_tmem, a_desc, b_desc, idesc, (kb > kb0 || kk != 0) ? 1u : 0u);
+          }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }

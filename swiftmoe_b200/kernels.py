@@ -157,6 +157,24 @@ def wgrad_gemm(A: torch.Tensor, B: torch.Tensor, k_offsets: torch.Tensor, K: Opt
     return out
 
 
+def wgrad_gemm_rows(A: torch.Tensor, B: torch.Tensor, k_offsets: torch.Tensor, M: Optional[int] = None,
+                    N: Optional[int] = None, out: Optional[torch.Tensor] = None):
+    """C[g] = A[K_g, :M]^T @ B[K_g, :N] (fp32 [G, M, N]) for the row ranges K_g =
+    [k_offsets[g], k_offsets[g+1]) of the row-major 16-bit operands A [K, lda], B [K, ldb]."""
+    _need_cuda(A, B, k_offsets)
+    K, lda = A.shape
+    K2, ldb = B.shape
+    M = lda if M is None else M
+    N = ldb if N is None else N
+    G = k_offsets.numel() - 1
+    if out is None:
+        out = torch.empty((G, M, N), dtype=torch.float32, device=A.device)
+    L.check(L.load().smoe_wgrad_gemm_rows(L.ptr(A), lda, L.ptr(B), ldb, L.dtype_code(A.dtype), L.ptr(k_offsets), G,
+                                          M, N, min(K, K2), L.ptr(out), L.stream_handle(A.device)),
+            "smoe_wgrad_gemm_rows")
+    return out
+
+
 def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
     """[G, R, C] -> [G, C, R]."""
     _need_cuda(src)

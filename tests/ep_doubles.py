@@ -191,6 +191,8 @@ def ep_send_rows(x, row_token, offsets, own_first, own_count, send_addr, keep, r
     off = offsets.numpy().astype(np.int64)
     E = off.size - 1
     rt, sa, kp = row_token.numpy(), send_addr.numpy(), keep.numpy()
+    if x.shape[0] == 0:
+        return
     xr = np.ascontiguousarray(x.contiguous().view(torch.uint8).numpy().reshape(x.shape[0], -1))   # rows as bytes
     rb = xr.shape[1]
     for i in range(int(off[E])):

@@ -41,6 +41,29 @@ def test_wgrad_gemm_matches_torch(K, koff, M, N, K_, ld):
     assert K.read_device_error(torch.device("cuda", 0)) == 0
 
 
+@pytest.mark.parametrize("koff,M,N,K_,lda,ldb", [
+    ([0, 128, 128, 320], 200, 264, 320, 200, 264),   # an empty group, ragged M and N
+    ([0, 64, 448], 384, 512, 448, 392, 520),          # row strides wider than M / N
+    ([0, 300], 256, 256, 300, 256, 256),              # one group ending off a 64-row boundary (rows past K read zeros)
+    ([0, 4096, 8192], 1024, 512, 8192, 1024, 512)])   # long K ranges
+def test_wgrad_gemm_rows_matches_torch(K, koff, M, N, K_, lda, ldb):
+    """The weight-gradient GEMM on operands given as rows of K (the routed rows as they
+    are, read as MN-major tensor-core tiles): C[g] = A[K_g, :M]^T B[K_g, :N]."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.randn(K_ + 5, lda, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(K_ + 5, ldb, device="cuda", generator=g).to(torch.bfloat16)
+    ko = torch.tensor(koff, dtype=torch.int32, device="cuda")
+    C = K.wgrad_gemm_rows(A[:K_].contiguous(), B[:K_].contiguous(), ko, M=M, N=N)
+    for i in range(len(koff) - 1):
+        a, b = koff[i], koff[i + 1]
+        ref = A[a:b, :M].float().T @ B[a:b, :N].float()
+        if b == a:
+            assert (C[i] == 0).all()
+        else:
+            assert (C[i] - ref).abs().max().item() <= 1e-4 * max(ref.abs().max().item(), 1.0), i
+    assert K.read_device_error(torch.device("cuda", 0)) == 0
+
+
 def test_gateup_epilogue_matches_torch(K):
     from swiftmoe_b200 import _lib as L
     g = torch.Generator(device="cuda").manual_seed(6)
