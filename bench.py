@@ -79,6 +79,8 @@ def parse():
     ap.add_argument("--extras", default="auto", choices=["auto", "none"],
                     help="auto: also measure the other layer shapes and the decode sweep")
     ap.add_argument("--parity-sample", type=int, default=64, help="tokens per rank checked after timing")
+    ap.add_argument("--mode", default="forward", choices=["forward", "backward"],
+                    help="backward: time the layer's backward pass alone (one GPU; profiling cases)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="token chunks of the EP exchange")
     ap.add_argument("--ep-transport", default=None, choices=["p2p", "collective"])
     ap.add_argument("--ep-schedule", default=None, choices=["device", "local_first", "chunked"],
@@ -505,6 +507,22 @@ def release(model, R: Ranks):
     torch.cuda.empty_cache()
 
 
+def backward_timing(model, T: int, R: Ranks, pk, steps: int, warmup: int):
+    """The layer's backward (``smoe_layer_bwd``: gradients of x, the gate and every expert
+    weight) for a seeded upstream gradient, CUDA-event timed; FLOPs counted as the GEMMs
+    it runs (gate/up recompute, dout W2, dgrad, two weight gradients)."""
+    import torch
+    d, F = model.d_model, model.d_ff
+    x = torch.randn((T, d), device=R.dev, dtype=torch.bfloat16, generator=torch.Generator(R.dev).manual_seed(300))
+    dout = torch.randn((T, d), device=R.dev, dtype=torch.bfloat16, generator=torch.Generator(R.dev).manual_seed(301))
+    ms = time_steps(lambda i=None: model._backward_fused(x, dout), steps, warmup, R)
+    S = T * model.top_k
+    flops = 2.0 * S * d * 2 * F * 3 + 2.0 * S * d * F * 2
+    return {"ms_per_backward": ms, "tokens_per_gpu": T, "gemm_tflops": flops / (ms / 1e3) / 1e12,
+            "frac_of_burst_peak": flops / (ms / 1e3) / 1e12 / pk["burst"], "gemm_flops": flops,
+            "what": "gradients of x, gate, w1, w3, w2 (bf16 layer, fp32 weight gradients), one GPU"}
+
+
 def extra_workloads(R: Ranks, pk, steps: int, warmup: int, decode_model=None, sample: int = 32):
     """The other layer shapes of the benchmark set, a few seconds each: the fp32 layer
     (one GPU), the capacity-limited and fine-grained expert-parallel layers (every N),
@@ -540,6 +558,8 @@ def extra_workloads(R: Ranks, pk, steps: int, warmup: int, decode_model=None, sa
         ent["parity"] = parity_check(model, x, out, wl, R, sample)
         res[name] = ent
         release(model, R)
+    if decode_model is not None and R.ws == 1:
+        res["backward"] = backward_timing(decode_model, WORKLOADS["mixtral"]["T"], R, pk, steps=5, warmup=2)
     if decode_model is not None and R.ws in (1, 8):
         wl = WORKLOADS["mixtral"]
         for T in DECODE_TOKENS:
@@ -584,6 +604,13 @@ def _main():
         return
     import torch
     import torch.distributed as dist
+    if args.mode == "backward":
+        torch.cuda.set_device(0)
+        R = Ranks(1, 0, 0, torch.device("cuda", 0))
+        model, _ = make_layer(wl, R, 1, profiling=False)
+        res = backward_timing(model, args.tokens, R, peaks(), args.steps, args.warmup)
+        print(json.dumps({"mode": "backward", "workload": WORKLOAD, **res}), flush=True)
+        return
 
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
