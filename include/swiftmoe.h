@@ -244,11 +244,27 @@ SMOE_API int smoe_ep_regroup_plan(const int32_t* recv_counts, int ws, int E_l, i
  * rows of the layout (expert_offsets[E] <= rows_cap).  Order the receivers after it
  * with a collective on the same stream.
  * smoe_ep_drop_slots: slot_row[s] = -1 for the slots the cut dropped (row position in
- * its expert's segment >= keep[e]), so that smoe_combine skips them.                 */
+ * its expert's segment >= keep[e]), so that smoe_combine skips them.
+ * flags SMOE_EP_LAYOUT_ROTATED (token dedup; E == ws "experts" = ranks, no capacity):
+ * every source s lays out its rows in its rotated rank order (destination (s + g) % ws
+ * for group g, its own rank first) and counts_all holds those groups' counts; send_addr
+ * and keep come out in this rank's rotated group order, the return table in rank order.
+ * smoe_ep_clear_tail: idx [rows_cap, k] slots of rows r >= *n_rows set to -1 (received
+ * rows past this step's count).  smoe_store_rows: src row r (r < n_rows) to the address
+ * row_ptrs[r] (0 = skip; 16-byte aligned, possibly another GPU's memory).
+ * smoe_copy_rows_count: dst rows [0, *n_rows) = src rows, n_rows in device memory.
+ * Replace, for token dedup: the host-side sizing and per-peer copies of the
+ * (token, rank) rows and their slot metadata (models/ultimate_moe.py:128-141).       */
+SMOE_API int smoe_ep_clear_tail(int32_t* idx, const int32_t* n_rows, int64_t rows_cap, int k, smoe_stream_t stream);
+SMOE_API int smoe_store_rows(const void* src, int64_t row_bytes, const uint64_t* row_ptrs, int64_t n_rows,
+                             smoe_stream_t stream);
+SMOE_API int smoe_copy_rows_count(void* dst, const void* src, int64_t row_bytes, const int32_t* n_rows,
+                                  int64_t rows_cap, smoe_stream_t stream);
+#define SMOE_EP_LAYOUT_ROTATED 1 /* flags of smoe_ep_layout: token dedup's rotated layouts */
 SMOE_API int smoe_ep_layout(const int32_t* counts_all, int ws, int E, int rank, int capacity,
                             const uint64_t* recv_base, const uint64_t* ret_base, int64_t row_bytes,
                             int64_t recv_rows_max, uint64_t* send_addr, int32_t* keep, int32_t* recv_offsets,
-                            int64_t* seg_table, smoe_stream_t stream);
+                            int64_t* seg_table, int flags, smoe_stream_t stream);
 SMOE_API int smoe_ep_send_rows(const void* x, int64_t row_bytes, const int32_t* row_token,
                                const int32_t* expert_offsets, int E, int own_first, int own_count,
                                const uint64_t* send_addr, const int32_t* keep, int64_t rows_cap,

@@ -77,7 +77,10 @@ SIGNATURES = {
     "smoe_ep_return_rows": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i32, _i64, _vp, _i64, _vp]),
     "smoe_ep_dedup_ranks": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp]),
     "smoe_ep_dedup_meta": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
-    "smoe_ep_layout": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "smoe_ep_layout": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "smoe_ep_clear_tail": (_i32, [_vp, _vp, _i64, _i32, _vp]),
+    "smoe_store_rows": (_i32, [_vp, _i64, _vp, _i64, _vp]),
+    "smoe_copy_rows_count": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "smoe_ep_send_rows": (_i32, [_vp, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
     "smoe_ep_drop_slots": (_i32, [_vp, _i64, _vp, _i32, _vp, _vp, _vp]),
     "smoe_ep_buffer_create": (_i32, [_sz, C.POINTER(_vp), _vp]),

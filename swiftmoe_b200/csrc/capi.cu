@@ -776,8 +776,10 @@ int smoe_ep_return_rows(const int32_t* row_src, const int32_t* expert_offsets, i
 
 int smoe_ep_layout(const int32_t* counts_all, int ws, int E, int rank, int capacity, const uint64_t* recv_base,
                    const uint64_t* ret_base, int64_t row_bytes, int64_t recv_rows_max, uint64_t* send_addr,
-                   int32_t* keep, int32_t* recv_offsets, int64_t* seg_table, smoe_stream_t stream) {
+                   int32_t* keep, int32_t* recv_offsets, int64_t* seg_table, int flags, smoe_stream_t stream) {
   if (ws < 1 || E < 1 || E % ws != 0 || rank < 0 || rank >= ws || capacity < 0) return SMOE_ERR_INVALID;
+  if (flags & ~SMOE_EP_LAYOUT_ROTATED) return SMOE_ERR_INVALID;
+  if ((flags & SMOE_EP_LAYOUT_ROTATED) && (E != ws || capacity != 0)) return SMOE_ERR_INVALID;
   if (row_bytes <= 0 || row_bytes % 16 != 0 || recv_rows_max < 0 || recv_rows_max > INT32_MAX) return SMOE_ERR_INVALID;
   if (!counts_all || !recv_base || !ret_base || !send_addr || !keep || !recv_offsets || !seg_table)
     return SMOE_ERR_INVALID;
@@ -787,7 +789,7 @@ int smoe_ep_layout(const int32_t* counts_all, int ws, int E, int rank, int capac
   SMOE_CK(ensure_smem(ep_layout_kernel, smem, &done));
   ep_layout_kernel<<<1, 256, smem, (cudaStream_t)stream>>>(counts_all, ws, E, rank, capacity, recv_base, ret_base,
                                                            row_bytes, recv_rows_max, send_addr, keep, recv_offsets,
-                                                           seg_table);
+                                                           seg_table, flags & SMOE_EP_LAYOUT_ROTATED);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
@@ -804,6 +806,41 @@ int smoe_ep_send_rows(const void* x, int64_t row_bytes, const int32_t* row_token
   ep_send_rows_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
       static_cast<const unsigned char*>(x), row_bytes, row_token, expert_offsets, E, own_first,
       own_first + own_count, send_addr, keep);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_ep_clear_tail(int32_t* idx, const int32_t* n_rows, int64_t rows_cap, int k, smoe_stream_t stream) {
+  if (rows_cap < 0 || k < 1) return SMOE_ERR_INVALID;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!idx || !n_rows) return SMOE_ERR_INVALID;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows_cap * k, 256), (int64_t)device_sms() * 8);
+  ep_clear_tail_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, n_rows, rows_cap, k);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_store_rows(const void* src, int64_t row_bytes, const uint64_t* row_ptrs, int64_t n_rows,
+                    smoe_stream_t stream) {
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || n_rows < 0) return SMOE_ERR_INVALID;
+  if (n_rows == 0) return SMOE_OK;
+  if (!src || !row_ptrs || !aligned16(src)) return SMOE_ERR_INVALID;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(cdiv(n_rows, 8), (int64_t)device_sms() * 4));
+  store_rows_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(static_cast<const unsigned char*>(src),
+                                                                         row_bytes, row_ptrs, n_rows);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+int smoe_copy_rows_count(void* dst, const void* src, int64_t row_bytes, const int32_t* n_rows, int64_t rows_cap,
+                         smoe_stream_t stream) {
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || rows_cap < 0) return SMOE_ERR_INVALID;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!dst || !src || !n_rows || !aligned16(dst) || !aligned16(src)) return SMOE_ERR_INVALID;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows_cap * (row_bytes >> 4), 256), (int64_t)device_sms() * 8);
+  copy_rows_count_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<unsigned char*>(dst),
+                                                                 static_cast<const unsigned char*>(src), row_bytes,
+                                                                 n_rows, rows_cap);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

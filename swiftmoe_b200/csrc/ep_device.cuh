@@ -35,24 +35,34 @@ constexpr int kLayoutMaxCells = 8192;    // ws * E handled by the one-block layo
 //   seg[2*El*ws+1] return table of the received segments in (local expert, source) order:
 //                  first receive row of each segment, the row total, then the byte
 //                  address of each segment's first row in the source's return buffer
+//
+// rotated != 0 (token dedup: one "expert" per rank, E == ws): every source lays its rows
+// out in ITS rotated rank order (its own rank first), G[s][g] counts source s's group g
+// = destination (s + g) % ws, and send_addr / keep are written in this rank's rotated
+// group order; everything else is in rank order.
+__device__ __forceinline__ int layout_count(const int32_t* G, int ws, int E, bool rotated, int s, int e) {
+  return rotated ? G[s * E + (e - s + ws) % ws] : G[s * E + e];
+}
+
 __global__ void __launch_bounds__(256) ep_layout_kernel(const int32_t* __restrict__ G, int ws, int E, int me,
                                                         int capacity, const uint64_t* __restrict__ recv_base,
                                                         const uint64_t* __restrict__ ret_base, int64_t row_bytes,
                                                         int64_t recv_rows_max, uint64_t* __restrict__ send_addr,
                                                         int32_t* __restrict__ keep, int32_t* __restrict__ recv_off,
-                                                        int64_t* __restrict__ seg) {
+                                                        int64_t* __restrict__ seg, int rotated) {
   extern __shared__ int lay_sh[];
   int* Kp = lay_sh;                  // [ws][E] kept rows of each (source, expert) segment
   int* per_exp = Kp + ws * E;        // [E] rows expert e receives from other ranks
   int* eo = per_exp + E;             // [E] start of expert e's region in its owner's buffer
   __shared__ int s_overflow;
   const int El = E / ws;
+  const bool rot = rotated != 0 && El == 1;
   if (threadIdx.x == 0) s_overflow = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int owner = e / El;
     int before = 0, recv = 0;
     for (int s = 0; s < ws; ++s) {
-      const int c = G[s * E + e];
+      const int c = layout_count(G, ws, E, rot, s, e);
       const int kp = capacity > 0 ? max(0, min(c, capacity - before)) : c;
       Kp[s * E + e] = kp;
       before += c;
@@ -78,8 +88,9 @@ __global__ void __launch_bounds__(256) ep_layout_kernel(const int32_t* __restric
     for (int s = 0; s < me; ++s)
       if (s != owner) so += Kp[s * E + e];
     const int64_t row = (int64_t)eo[e] + so;
-    send_addr[e] = (owner == me || overflow) ? 0ull : recv_base[owner] + (uint64_t)(row * row_bytes);
-    keep[e] = overflow ? 0 : Kp[me * E + e];
+    const int o = rot ? (e - me + ws) % ws : e;        // output slot: this rank's send layout order
+    send_addr[o] = (owner == me || overflow) ? 0ull : recv_base[owner] + (uint64_t)(row * row_bytes);
+    keep[o] = overflow ? 0 : Kp[me * E + e];
   }
   const int nseg = El * ws;
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
@@ -90,7 +101,8 @@ __global__ void __launch_bounds__(256) ep_layout_kernel(const int32_t* __restric
       if (q != me) so += Kp[q * E + e];
     seg[i] = overflow ? 0 : (int64_t)eo[e] + so;
     int64_t src_off = 0;              // the segment's first row in source s's send layout
-    for (int f = 0; f < e; ++f) src_off += G[s * E + f];
+    const int pos = rot ? (e - s + ws) % ws : e;
+    for (int f = 0; f < pos; ++f) src_off += G[s * E + f];
     seg[nseg + 1 + i] = (int64_t)(ret_base[s] + (uint64_t)(src_off * row_bytes));
   }
   for (int le = threadIdx.x; le < El; le += blockDim.x) recv_off[le] = overflow ? 0 : eo[me * El + le];
@@ -145,6 +157,45 @@ __global__ void __launch_bounds__(256) ep_send_rows_kernel(const unsigned char* 
     wrote = true;
   }
   if (wrote) __threadfence_system();
+}
+
+// idx[r][j] = -1 for the received rows r >= *n_rows (their slots hold stale metadata).
+__global__ void __launch_bounds__(256) ep_clear_tail_kernel(int32_t* __restrict__ idx, const int32_t* __restrict__ n_rows,
+                                                            int64_t rows_cap, int k) {
+  const int64_t first = (int64_t)(*n_rows) * k;
+  for (int64_t i = first + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows_cap * k;
+       i += (int64_t)gridDim.x * blockDim.x)
+    idx[i] = -1;
+}
+
+// Row r of src (r < n_rows) to the address row_ptrs[r] (0: skipped); one warp per row,
+// 16-byte vectors (row_bytes % 16 == 0).  The addresses may be in other GPUs' memory.
+__global__ void __launch_bounds__(256) store_rows_kernel(const unsigned char* __restrict__ src, int64_t row_bytes,
+                                                         const uint64_t* __restrict__ row_ptrs, int64_t n_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nv = (int)(row_bytes >> 4);
+  bool wrote = false;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows; r += warps) {
+    const uint64_t p = row_ptrs[r];
+    if (p == 0 || (p & 15)) continue;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + r * row_bytes);
+    uint4* d4 = reinterpret_cast<uint4*>(p);
+    for (int j = lane; j < nv; j += 32) d4[j] = s4[j];
+    wrote = true;
+  }
+  if (wrote) __threadfence_system();
+}
+
+// dst rows [0, *n_rows) = src rows [0, *n_rows) (n_rows in device memory, <= rows_cap).
+__global__ void __launch_bounds__(256) copy_rows_count_kernel(unsigned char* __restrict__ dst,
+                                                              const unsigned char* __restrict__ src, int64_t row_bytes,
+                                                              const int32_t* __restrict__ n_rows, int64_t rows_cap) {
+  const int64_t n = min((int64_t)(*n_rows), rows_cap) * (row_bytes >> 4);
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    d4[i] = s4[i];
 }
 
 // slot_row[s] = -1 for every slot whose row lies past the kept prefix of its expert's

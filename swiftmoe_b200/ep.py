@@ -205,7 +205,10 @@ class ExpertParallelExchange:
         CUDA tensors use the peer-copy transport (``_forward_p2p``) unless
         ``transport="collective"``; CPU tensors (gloo) use all_to_all_single."""
         use_p2p = self.transport == "p2p" or (self.transport == "auto" and x.is_cuda)
-        if use_p2p and self.schedule in ("device", "local_first") and capacity <= 0 and self._use_dedup(idx.shape[1]):
+        dedup = capacity <= 0 and self._use_dedup(idx.shape[1])
+        if use_p2p and self.schedule == "device" and dedup and (idx.shape[1] * 4) % 16 == 0:
+            return self._forward_p2p_device_dedup(x, idx, w, experts, shared, timer)
+        if use_p2p and self.schedule in ("device", "local_first") and dedup:
             return self._forward_p2p_dedup(x, idx, w, experts, shared, timer)
         if use_p2p and self.schedule == "device":
             return self._forward_p2p_device(x, idx, w, capacity, experts, shared, timer)
@@ -725,6 +728,128 @@ class ExpertParallelExchange:
         rt.wait(comp, ev_ret)
         mark("wait_ret0_after")
         return self.k.combine(ret_local[:max(T * k, 1)], plan["slot_row"], w, T, k, shared=shared)
+
+    def _forward_p2p_device_dedup(self, x, idx, w, experts, shared=None, timer=None):
+        """Token dedup on the device schedule: no host wait.  The rows and their slot
+        metadata are those of ``_forward_p2p_dedup`` (one row per (token, rank), this
+        rank's rotated rank order with its own rank first, each sent row carrying the
+        local expert and gate weight of the token's k slots); their layout in the
+        receivers' buffers comes from ``ep_layout`` in its rotated mode (rows, then
+        expert ids, then weights, one call each), the send kernel stores all three into
+        the peers, the receiver marks its unfilled rows, expands, runs the experts and
+        stores one weighted partial row per received row straight back into its
+        source's return buffer; the own rows' partial sums are copied into the own
+        segment.  Buffers are sized for ``max_tokens`` tokens per rank."""
+        rt = self.rt
+        ws, El, E, me = self.world_size, self.exp_per_rank, self.num_experts, self.rank
+        T, k = idx.shape
+        d = x.shape[1]
+        dev = x.device
+        rb = d * x.element_size()
+        if self.max_tokens is None or getattr(self, "_reserved_k", k) != k:
+            self.reserve(T, k, dev)
+        if T > self.max_tokens:
+            from ._lib import SwiftMoEError
+            raise SwiftMoEError(f"batch of {T} tokens exceeds the exchange's max_tokens={self.max_tokens}; "
+                                f"call reserve() with the largest batch on every rank first")
+        comp, comm = rt.compute(dev), rt.comm(dev)
+
+        def mark(name):
+            if timer is not None:
+                timer(name)
+
+        st, recv_buf, ret_buf = self._dedup_state(k, rb, dev)
+        R = st["recv_rows"]
+        ridx = self.k.ep_dedup_ranks(idx, El, ws, me)
+        rplan = self.k.dispatch_plan(ridx, ws)                    # one row per (token, rank), own rank first
+        rows_cap = rplan["rows_cap"]
+        meta_e, meta_w, own_e = self.k.ep_dedup_meta(idx, w, ridx, rplan["slot_row"], rplan["counts"][0:1], El, ws,
+                                                     rows_cap)
+        ident = st["ident"][:max(rows_cap, 1)]
+        G = st["G"]
+        mark("counts_start")
+        rt.join(comm, comp)
+        for t in (x, rplan["row_token"], rplan["offsets"], rplan["counts"], meta_e, meta_w):
+            rt.keep(t, comm)
+        with rt.on(comm):
+            dist.all_gather_into_tensor(G.view(-1), rplan["counts"], group=self.group)
+            for lay, base, nb in ((st["lay_x"], st["recv_base"], rb), (st["lay_e"], st["recv_base_e"], 4 * k),
+                                  (st["lay_w"], st["recv_base_w"], 4 * k)):
+                self.k.ep_layout(G, me, 0, base, st["ret_base"], nb, R, lay, rotated=True)
+            self.k.ep_send_rows(x, rplan["row_token"], rplan["offsets"], 0, 1, st["lay_x"]["send_addr"],
+                                st["lay_x"]["keep"], rows_cap)
+            self.k.ep_send_rows(meta_e, ident, rplan["offsets"], 0, 1, st["lay_e"]["send_addr"], st["lay_e"]["keep"],
+                                rows_cap)
+            self.k.ep_send_rows(meta_w, ident, rplan["offsets"], 0, 1, st["lay_w"]["send_addr"], st["lay_w"]["keep"],
+                                rows_cap)
+        self._barrier(comm, dev)
+        ev_sent = rt.record(comm)
+        mark("counts_done")
+        # own rows: expand, compute, weighted partial sums into the own segment of the
+        # return buffer (rows [0, own count) of the send layout)
+        send = self.k.permute_rows(x, rplan["row_token"], rplan["offsets"][0:2], rows_cap)
+        oplan = self.k.dispatch_plan(own_e[:T], El)
+        xo = self.k.permute_rows(send, oplan["row_token"], oplan["offsets"], oplan["rows_cap"])
+        mark("experts_self_start")
+        yo = experts(xo, oplan["offsets"])
+        mark("experts_self_end")
+        part_own = self.k.combine(yo, oplan["slot_row"], meta_w[:T], T, k)
+        ret_local = rt.view(ret_buf.local, (st["ret_rows"], d), x.dtype, dev)
+        self.k.copy_rows_count(ret_local, part_own, rplan["counts"][0:1])
+        mark("wait_sent0_before")
+        rt.wait(comp, ev_sent)
+        mark("wait_sent0_after")
+        n_recv = st["lay_x"]["recv_offsets"][1:2]
+        xr = rt.view(recv_buf.local, (R, d), x.dtype, dev)
+        er = rt.view(recv_buf.local + st["off_e"], (R, k), torch.int32, dev)
+        wr = rt.view(recv_buf.local + st["off_w"], (R, k), torch.float32, dev)
+        self.k.ep_clear_tail(er, n_recv)
+        rp = self.k.dispatch_plan(er, El)
+        xe = self.k.permute_rows(xr, rp["row_token"], rp["offsets"], rp["rows_cap"])
+        mark("experts0_start")
+        y = experts(xe, rp["offsets"])
+        mark("experts0_end")
+        part = self.k.combine(y, rp["slot_row"], wr, R, k)
+        row_ptrs = self.k.ep_return_rows(None, st["lay_x"]["recv_offsets"], None, R, st["lay_x"]["seg"], rb, R)
+        self.k.store_rows(part, row_ptrs, R)
+        self._rows_dev = (oplan["offsets"][El:], rp["offsets"][El:])
+        rt.join(comm, comp)
+        self._barrier(comm, dev)
+        ev_ret = rt.record(comm)
+        mark("combine_start")
+        mark("wait_ret0_before")
+        rt.wait(comp, ev_ret)
+        mark("wait_ret0_after")
+        if self._ones is None or self._ones.shape != (T, k) or self._ones.device != dev:
+            self._ones = torch.ones((T, k), dtype=torch.float32, device=dev)
+        return self.k.combine(ret_local[:max(rows_cap, 1)], rplan["slot_row"], self._ones, T, k, shared=shared)
+
+    def _dedup_state(self, k: int, row_bytes: int, dev):
+        """Peer buffers of the dedup device schedule (rows, then per-slot expert ids, then
+        weights, in one receive buffer) and its persistent layout tensors."""
+        ws = self.world_size
+        R = max((ws - 1) * self.max_tokens, 1)               # rows one rank can receive at most
+        ret_rows = self.max_tokens * min(k, ws)               # (token, rank) rows of the send layout
+        al = lambda v: (v + 255) // 256 * 256
+        off_e = al(R * row_bytes)
+        off_w = off_e + al(R * k * 4)
+        recv_buf, ret_buf = self._peer_buffers(dev)
+        recv_buf.ensure(off_w + R * k * 4)
+        ret_buf.ensure(ret_rows * row_bytes)
+        key = ("dedup", recv_buf.local, ret_buf.local, k, row_bytes, str(dev))
+        if self._dev is None or self._dev.get("key") != key:
+            i64 = dict(dtype=torch.int64, device=dev)
+            i32 = dict(dtype=torch.int32, device=dev)
+            lay = lambda: dict(send_addr=torch.zeros(ws, **i64), keep=torch.zeros(ws, **i32),
+                               recv_offsets=torch.zeros(2, **i32), seg=torch.zeros(2 * ws + 1, **i64))
+            self._dev = dict(
+                key=key, recv_rows=R, ret_rows=ret_rows, off_e=off_e, off_w=off_w,
+                recv_base=torch.tensor(recv_buf.ptrs, **i64), ret_base=torch.tensor(ret_buf.ptrs, **i64),
+                recv_base_e=torch.tensor([p_ + off_e for p_ in recv_buf.ptrs], **i64),
+                recv_base_w=torch.tensor([p_ + off_w for p_ in recv_buf.ptrs], **i64),
+                G=torch.zeros((ws, ws), **i32), lay_x=lay(), lay_e=lay(), lay_w=lay(),
+                ident=torch.arange(max(self.max_tokens * min(k, ws), 1), **i32))
+        return self._dev, recv_buf, ret_buf
 
     def _forward_p2p_dedup(self, x, idx, w, experts, shared=None, timer=None):
         """Local-first schedule with token dedup, for top-k routing with several experts

@@ -227,7 +227,7 @@ def ep_return_rows(row_src: torch.Tensor, offsets: torch.Tensor, recv_dst: torch
 
 
 def ep_layout(counts_all: torch.Tensor, rank: int, capacity: int, recv_base: torch.Tensor, ret_base: torch.Tensor,
-              row_bytes: int, recv_rows_max: int, out: dict):
+              row_bytes: int, recv_rows_max: int, out: dict, rotated: bool = False):
     """Device-side layout of the exchange from the all-gathered counts [ws, E] (see
     smoe_ep_layout).  ``out`` holds the preallocated outputs: send_addr [E] int64, keep [E]
     int32, recv_offsets [E_l+1] int32, seg [2*E_l*ws+1] int64; returns it."""
@@ -235,9 +235,32 @@ def ep_layout(counts_all: torch.Tensor, rank: int, capacity: int, recv_base: tor
     ws_, E = counts_all.shape
     L.check(L.load().smoe_ep_layout(L.ptr(counts_all), ws_, E, rank, capacity, L.ptr(recv_base), L.ptr(ret_base),
                                     row_bytes, recv_rows_max, L.ptr(out["send_addr"]), L.ptr(out["keep"]),
-                                    L.ptr(out["recv_offsets"]), L.ptr(out["seg"]),
+                                    L.ptr(out["recv_offsets"]), L.ptr(out["seg"]), 1 if rotated else 0,
                                     L.stream_handle(counts_all.device)), "smoe_ep_layout")
     return out
+
+
+def ep_clear_tail(idx: torch.Tensor, n_rows: torch.Tensor) -> None:
+    """idx [rows_cap, k] slots of the rows r >= n_rows[0] (device) set to -1, in place."""
+    _need_cuda(idx, n_rows)
+    rows_cap, k = idx.shape
+    L.check(L.load().smoe_ep_clear_tail(L.ptr(idx), L.ptr(n_rows), rows_cap, k, L.stream_handle(idx.device)),
+            "smoe_ep_clear_tail")
+
+
+def store_rows(src: torch.Tensor, row_ptrs: torch.Tensor, n_rows: int) -> None:
+    """Row r of src (r < n_rows) to the address row_ptrs[r] (0 = skip)."""
+    _need_cuda(src, row_ptrs)
+    L.check(L.load().smoe_store_rows(L.ptr(src), src.shape[1] * src.element_size(), L.ptr(row_ptrs), n_rows,
+                                     L.stream_handle(src.device)), "smoe_store_rows")
+
+
+def copy_rows_count(dst: torch.Tensor, src: torch.Tensor, n_rows: torch.Tensor) -> None:
+    """dst rows [0, n_rows[0]) = src rows (n_rows in device memory)."""
+    _need_cuda(dst, src, n_rows)
+    rows_cap = min(dst.shape[0], src.shape[0])
+    L.check(L.load().smoe_copy_rows_count(L.ptr(dst), L.ptr(src), src.shape[1] * src.element_size(), L.ptr(n_rows),
+                                          rows_cap, L.stream_handle(src.device)), "smoe_copy_rows_count")
 
 
 def ep_send_rows(x: torch.Tensor, row_token: torch.Tensor, offsets: torch.Tensor, own_first: int, own_count: int,

@@ -147,10 +147,13 @@ def ep_dedup_meta(idx, w, ridx, slot_row, own_count, El, ws, rows_cap):
     return torch.from_numpy(meta_e), torch.from_numpy(meta_w), torch.from_numpy(own_e)
 
 
-def ep_layout(counts_all, rank, capacity, recv_base, ret_base, row_bytes, recv_rows_max, out):
-    G = counts_all.numpy().astype(np.int64)
-    ws, E = G.shape
+def ep_layout(counts_all, rank, capacity, recv_base, ret_base, row_bytes, recv_rows_max, out, rotated=False):
+    Gin = counts_all.numpy().astype(np.int64)
+    ws, E = Gin.shape
     El, me = E // ws, rank
+    rot = rotated and El == 1
+    # rotated: row s of the input counts source s's groups g = destination (s + g) % ws
+    G = np.stack([np.roll(Gin[s_], s_) for s_ in range(ws)]) if rot else Gin
     before = np.cumsum(G, 0) - G
     Kp = np.clip(capacity - before, 0, G) if capacity > 0 else G.copy()
     owner = np.arange(E) // El
@@ -167,9 +170,10 @@ def ep_layout(counts_all, rank, capacity, recv_base, ret_base, row_bytes, recv_r
     keep = np.zeros(E, np.int32)
     for e in range(E):
         so = sum(int(Kp[s, e]) for s in range(me) if s != owner[e])
+        o = (e - me) % ws if rot else e
         if owner[e] != me and not overflow:
-            send_addr[e] = int(rbase[owner[e]]) + int(eo[e] + so) * row_bytes
-        keep[e] = 0 if overflow else Kp[me, e]
+            send_addr[o] = int(rbase[owner[e]]) + int(eo[e] + so) * row_bytes
+        keep[o] = 0 if overflow else Kp[me, e]
     nseg = El * ws
     seg = np.zeros(2 * nseg + 1, np.int64)
     for i in range(nseg):
@@ -177,7 +181,8 @@ def ep_layout(counts_all, rank, capacity, recv_base, ret_base, row_bytes, recv_r
         e = me * El + le
         so = sum(int(Kp[q, e]) for q in range(s) if q != me)
         seg[i] = 0 if overflow else eo[e] + so
-        seg[nseg + 1 + i] = int(tbase[s]) + int(G[s, :e].sum()) * row_bytes
+        pos = (e - s) % ws if rot else e
+        seg[nseg + 1 + i] = int(tbase[s]) + int(Gin[s, :pos].sum() if rot else G[s, :e].sum()) * row_bytes
     seg[nseg] = 0 if overflow else n_recv[me]
     roff = np.concatenate([eo[me * El:(me + 1) * El], [n_recv[me]]]) if not overflow else np.zeros(El + 1)
     out["send_addr"].copy_(torch.from_numpy(send_addr))
@@ -212,3 +217,21 @@ def ep_drop_slots(idx, offsets, keep, slot_row):
         e, r = int(it[s]), int(sr[s])
         if 0 <= e < kp.size and r >= 0 and r - off[e] >= kp[e]:
             sr[s] = -1
+
+
+def ep_clear_tail(idx, n_rows):
+    n = int(n_rows.numpy().reshape(-1)[0])
+    idx.numpy()[n:] = -1
+
+
+def store_rows(src, row_ptrs, n_rows):
+    sb = np.ascontiguousarray(src.contiguous().view(torch.uint8).numpy().reshape(src.shape[0], -1))
+    ptr = row_ptrs.numpy()
+    for r in range(n_rows):
+        if ptr[r]:
+            ctypes.memmove(int(ptr[r]), sb[r].ctypes.data, sb.shape[1])
+
+
+def copy_rows_count(dst, src, n_rows):
+    n = int(n_rows.numpy().reshape(-1)[0])
+    dst[:n] = src[:n]

@@ -109,7 +109,9 @@ def _worker(rank, ws, rdzv, E, d, T, k, cap_factor, schedule, with_shared, resul
     # device schedule (layout on the device, rows stored into the peers by the send kernel)
     (2, 8, 2, None, "device", False), (2, 8, 2, 1.0, "device", True), (4, 8, 3, None, "device", False),
     (4, 16, 2, 0.5, "device", False), (8, 8, 2, 0.7, "device", False), (8, 16, 2, None, "device", True),
-    (4, 16, 5, 0.5, "device", False), (2, 16, 4, None, "device+nodedup", True)])
+    (4, 16, 5, 0.5, "device", False), (2, 16, 4, None, "device+nodedup", True),
+    # device schedule with token dedup (top-k a multiple of 4 with several experts per rank)
+    (2, 16, 4, None, "device", True), (4, 16, 8, None, "device", False), (8, 16, 8, None, "device", True)])
 def test_p2p_schedules_match_oracle(tmp_path, ws, E, k, cf, schedule, shared):
     T, d = 23, 12
     mp.spawn(_worker, args=(ws, _rdzv(tmp_path), E, d, T, k, cf, schedule, shared, str(tmp_path)), nprocs=ws, join=True)
@@ -121,7 +123,8 @@ def test_p2p_schedules_match_oracle(tmp_path, ws, E, k, cf, schedule, shared):
     ((0, 17), 16, 4, None, "local_first"), ((5, 0, 23, 1), 16, 6, None, "local_first"),
     ((0, 23), 8, 2, 1.0, "local_first"), ((5, 0, 23, 1), 8, 2, 0.5, "chunked"),
     ((0, 23), 8, 2, None, "device"), ((5, 0, 23, 1), 8, 2, 0.5, "device"),
-    ((5, 0, 23, 1), 16, 6, None, "device+nodedup")])
+    ((5, 0, 23, 1), 16, 6, None, "device+nodedup"), ((0, 17), 16, 4, None, "device"),
+    ((5, 0, 23, 1), 16, 8, None, "device")])
 def test_p2p_schedules_ragged_and_empty_batches(tmp_path, Ts, E, k, cf, schedule):
     """Ranks with different token counts, some with none: every rank still takes part in
     every collective step, and the ranks with tokens match the oracle."""
@@ -144,7 +147,7 @@ def _check(tmp_path, ws):
     (4, 16, 4, None, "local_first", 50.0), (4, 8, 8, None, "local_first", 0.0),
     (2, 8, 8, 1.0, "local_first", 0.0), (4, 8, 2, None, "chunked", 50.0),
     (2, 8, 2, None, "device", 50.0), (4, 8, 2, 0.5, "device", 50.0), (4, 8, 8, None, "device+nodedup", 0.0),
-    (2, 8, 8, 1.0, "device", 0.0)])
+    (2, 8, 8, 1.0, "device", 0.0), (4, 16, 4, None, "device", 50.0), (4, 8, 8, None, "device", 0.0)])
 def test_p2p_schedules_extreme_routing(tmp_path, ws, E, k, cf, schedule, skew):
     """All tokens routed to one rank's experts (the others compute nothing and receive
     nothing), and k = E (every token to every expert, every rank once with dedup)."""
