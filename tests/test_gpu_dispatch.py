@@ -283,3 +283,47 @@ def test_ep_send_rows_and_drop_slots(cap):
     ep_doubles.ep_drop_slots(torch.from_numpy(idx), plan["offsets"].cpu(), hl["keep"], sr_h)
     assert torch.equal(sr.cpu(), sr_h)
     assert (sr.cpu() < 0).any() == (cap > 0 and bool((G[:me + 1].sum(0) > cap).any()))
+
+
+@pytest.mark.parametrize("ws,seed", [(2, 5), (4, 6), (8, 7)])
+def test_ep_layout_rotated_matches_restatement(ws, seed):
+    """The token-dedup layout: every source's groups in its own rotated rank order."""
+    import ep_doubles
+    from swiftmoe_b200 import kernels as K
+    rng = np.random.default_rng(seed)
+    G = rng.integers(0, 500, size=(ws, ws)).astype(np.int32)
+    bases = [(np.arange(ws, dtype=np.int64) + 3) << 34, (np.arange(ws, dtype=np.int64) + 29) << 34]
+    for me in range(ws):
+        outs = []
+        for mod, dev in ((K, "cuda"), (ep_doubles, "cpu")):
+            lay = dict(send_addr=torch.zeros(ws, dtype=torch.int64, device=dev),
+                       keep=torch.zeros(ws, dtype=torch.int32, device=dev),
+                       recv_offsets=torch.zeros(2, dtype=torch.int32, device=dev),
+                       seg=torch.zeros(2 * ws + 1, dtype=torch.int64, device=dev))
+            mod.ep_layout(torch.from_numpy(G).to(dev), me, 0, torch.from_numpy(bases[0]).to(dev),
+                          torch.from_numpy(bases[1]).to(dev), 4096, 10 ** 6, lay, rotated=True)
+            outs.append({k_: v.cpu().numpy() for k_, v in lay.items()})
+        for key in outs[0]:
+            assert (outs[0][key] == outs[1][key]).all(), (me, key)
+
+
+def test_clear_tail_store_rows_copy_rows_count():
+    """The dedup schedule's small kernels: unfilled receive rows marked -1, rows stored at
+    per-row addresses (0 = skipped), and a copy of a device-counted prefix of rows."""
+    from swiftmoe_b200 import kernels as K
+    idx = torch.arange(40, dtype=torch.int32, device="cuda").view(10, 4)
+    K.ep_clear_tail(idx, torch.tensor([6], dtype=torch.int32, device="cuda"))
+    assert (idx[:6].cpu() == torch.arange(24, dtype=torch.int32).view(6, 4)).all() and (idx[6:] == -1).all()
+    src = torch.randn(9, 64, device="cuda").to(torch.bfloat16)
+    dst = torch.zeros(20, 64, device="cuda", dtype=torch.bfloat16)
+    order = [4, 0, 17, 9, -1, 3, 12, 19, 7]          # -1: row not stored
+    ptrs = torch.tensor([0 if o < 0 else dst[o].data_ptr() for o in order], dtype=torch.int64, device="cuda")
+    K.store_rows(src, ptrs, 9)
+    torch.cuda.synchronize()
+    for r, o in enumerate(order):
+        if o >= 0:
+            assert torch.equal(dst[o], src[r])
+    assert int((dst.float().abs().sum(1) > 0).sum()) == 8
+    out = torch.zeros(9, 64, device="cuda", dtype=torch.bfloat16)
+    K.copy_rows_count(out, src, torch.tensor([5], dtype=torch.int32, device="cuda"))
+    assert torch.equal(out[:5], src[:5]) and (out[5:] == 0).all()
