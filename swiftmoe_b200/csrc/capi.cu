@@ -220,34 +220,45 @@ int launch_wgrad(const CUtensorMap& ma, const CUtensorMap& mb, float* C, const i
 template <int EPI, typename T, typename OutT>
 int launch_gemv_t(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs,
                   const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
-                  cudaStream_t st) {
-  const int64_t warps = (int64_t)G * N;
+                  cudaStream_t st, const int32_t* a_index, int a_rows) {
+  // one warp per (group with rows, column); at most min(G, rows_cap) groups have rows
+  const int64_t warps = std::min<int64_t>(G, std::max<int64_t>(rows_cap, 1)) * N;
   const unsigned grid = (unsigned)std::max<int64_t>(
       1, std::min<int64_t>(cdiv(warps * 32, gemv::THREADS), (int64_t)device_sms() * 8));
   gemv::grouped_gemv_kernel<EPI, T, OutT><<<grid, gemv::THREADS, 0, st>>>(
-      (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap);
+      (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap, a_index,
+      a_rows);
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
 
 int launch_gemv(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs, int dtype,
                 int out_dtype, int epi, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N,
-                int K, cudaStream_t st) {
+                int K, cudaStream_t st, const int32_t* a_index = nullptr, int a_rows = -1) {
   const bool bf = dtype == SMOE_BF16;
+  if (a_index == nullptr) a_rows = (int)rows_cap;
   if (epi == SMOE_EPI_SWIGLU)
     return bf ? launch_gemv_t<SMOE_EPI_SWIGLU, __nv_bfloat16, __nv_bfloat16>(A, B, B3, C, row_ptrs, offsets, ends,
-                                                                             G, rows_cap, N, K, st)
+                                                                             G, rows_cap, N, K, st, a_index, a_rows)
               : launch_gemv_t<SMOE_EPI_SWIGLU, __half, __half>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N,
-                                                               K, st);
+                                                               K, st, a_index, a_rows);
   if (out_dtype == SMOE_F32)
     return bf ? launch_gemv_t<SMOE_EPI_STORE, __nv_bfloat16, float>(A, B, B3, C, row_ptrs, offsets, ends, G,
-                                                                    rows_cap, N, K, st)
+                                                                    rows_cap, N, K, st, a_index, a_rows)
               : launch_gemv_t<SMOE_EPI_STORE, __half, float>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N, K,
-                                                             st);
+                                                             st, a_index, a_rows);
   return bf ? launch_gemv_t<SMOE_EPI_STORE, __nv_bfloat16, __nv_bfloat16>(A, B, B3, C, row_ptrs, offsets, ends, G,
-                                                                          rows_cap, N, K, st)
+                                                                          rows_cap, N, K, st, a_index, a_rows)
             : launch_gemv_t<SMOE_EPI_STORE, __half, __half>(A, B, B3, C, row_ptrs, offsets, ends, G, rows_cap, N, K,
-                                                            st);
+                                                            st, a_index, a_rows);
+}
+
+// A 16-bit grouped GEMM that the decode kernels take: at most gemv::DISPATCH_ROWS rows.
+bool gemv_eligible(const void* A, const void* B, const void* B3, int dtype, int out_dtype, int epi, int G,
+                   int64_t rows_cap, int K) {
+  return dtype != SMOE_F32 && epi != SMOE_EPI_GATEUP && rows_cap <= gemv::DISPATCH_ROWS && G <= gemv::MAX_GROUPS &&
+         K % 8 == 0 && aligned16(A) && aligned16(B) && (!B3 || aligned16(B3)) &&
+         (epi == SMOE_EPI_STORE || out_dtype == dtype) && (out_dtype == SMOE_F32 || out_dtype == dtype);
 }
 
 // Which tensor-core kernel runs a grouped GEMM.  Measured on the Mixtral-shaped layer
@@ -291,10 +302,7 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   }
   // 16-bit inputs: decode-sized batches stream the weights on the SIMT pipes, the rest
   // runs on tensor cores
-  if (epi != SMOE_EPI_GATEUP && rows_cap <= gemv::DISPATCH_ROWS && G <= gemv::MAX_GROUPS && K % 8 == 0 &&
-      aligned16(A) && aligned16(B) &&
-      (!B3 || aligned16(B3)) && (epi == SMOE_EPI_STORE || out_dtype == dtype) &&
-      (out_dtype == SMOE_F32 || out_dtype == dtype))
+  if (gemv_eligible(A, B, B3, dtype, out_dtype, epi, G, rows_cap, K))
     return launch_gemv(A, B, B3, C, row_ptrs, dtype, out_dtype, epi, offsets, ends, G, rows_cap, N, K, st);
   if (G > tc::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
   if (K % 8 != 0 || N % 8 != 0) return SMOE_ERR_UNSUPPORTED;
@@ -596,6 +604,15 @@ int smoe_dispatch_plan(const int32_t* idx, int T, int k, int E, int capacity, in
   int32_t* base = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) +
                                              align_up((size_t)nb * E * sizeof(int32_t), 256));
   const int smem_w = kPlanWarps * E * (int)sizeof(int);
+  if (nb == 1) {  // one block: count, scan and scatter in one launch
+    static SmemGrant done_1;
+    const int smem_1 = smem_w + (E + 1) * (int)sizeof(int);
+    SMOE_CK(ensure_smem(plan_small_kernel, smem_1, &done_1));
+    plan_small_kernel<<<1, kPlanThreads, smem_1, st>>>(idx, n_slots, k, E, capacity, row_align, expert_counts,
+                                                       expert_offsets, slot_row, row_token);
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
   static SmemGrant done_c, done_s;
   SMOE_CK(ensure_smem(plan_count_kernel, smem_w, &done_c));
   SMOE_CK(ensure_smem(plan_scatter_kernel, smem_w, &done_s));
@@ -637,6 +654,19 @@ int smoe_combine(const void* y, int dtype, const int32_t* slot_row, const float*
   cudaStream_t st = (cudaStream_t)stream;
   const int V = 16 / es;
   const bool vec = d % V == 0 && aligned16(y) && aligned16(out) && (!shared || aligned16(shared));
+  if (vec && k <= 32) {  // one warp per token
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T, 8), (int64_t)device_sms() * 8);
+#define SMOE_COMBINE_W(TY, VV)                                                                                 \
+  combine_warp_kernel<TY, VV><<<grid, 256, 0, st>>>((const TY*)y, slot_row, w, T, k, d, (const TY*)shared, (TY*)out)
+    switch (dtype) {
+      case SMOE_F32: SMOE_COMBINE_W(float, 4); break;
+      case SMOE_F16: SMOE_COMBINE_W(__half, 8); break;
+      default: SMOE_COMBINE_W(__nv_bfloat16, 8);
+    }
+#undef SMOE_COMBINE_W
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
   const int64_t items = (int64_t)T * (vec ? d / V : d);
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(items, 256), (int64_t)device_sms() * 32);
 #define SMOE_COMBINE(TY, VV)                                                                                  \
@@ -1025,11 +1055,28 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
   rc = smoe_dispatch_plan(idx, T, k, E, a->capacity, 1, counts, offsets, slot_row, row_token, p.rows_cap,
                           ws + p.off_plan_ws, p.plan_ws, stream);
   if (rc) return rc;
-  rc = smoe_permute_rows(a->x, dt, T, d, row_token, offsets, E, p.rows_cap, xrows, stream);
-  if (rc) return rc;
+  // decode-sized SwiGLU layers: the first GEMM reads the token rows through row_token
+  const bool gather = a->expert_type == SMOE_EXPERT_SWIGLU &&
+                      gemv_eligible(a->x, a->w1, a->w3, dt, dt, SMOE_EPI_SWIGLU, E, p.rows_cap, d);
+  if (!gather) {
+    const int64_t row_bytes = (int64_t)d * elt_size(dt);
+    if (row_bytes % 16 == 0 && aligned16(a->x) && aligned16(xrows) && k <= 32) {
+      // token by token: each x row is read once for its k rows
+      const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T, 8), (int64_t)device_sms() * 8);
+      permute_tokens_kernel<<<grid, 256, 0, st>>>(static_cast<const unsigned char*>(a->x), row_bytes, slot_row, T, k,
+                                                  static_cast<unsigned char*>(xrows));
+      SMOE_CK(cudaGetLastError());
+    } else {
+      rc = smoe_permute_rows(a->x, dt, T, d, row_token, offsets, E, p.rows_cap, xrows, stream);
+      if (rc) return rc;
+    }
+  }
   if ((rc = mark(2))) return rc;
   if (a->expert_type == SMOE_EXPERT_SWIGLU) {
-    rc = grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E, p.rows_cap, F, d, st);
+    rc = gather ? launch_gemv(a->x, a->w1, a->w3, h, nullptr, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E,
+                              p.rows_cap, F, d, st, row_token, T)
+                : grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E, p.rows_cap,
+                                    F, d, st);
     if (rc) return rc;
     if ((rc = mark(3))) return rc;
     rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, F, st);

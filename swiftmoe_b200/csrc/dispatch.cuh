@@ -169,6 +169,98 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(const int32_
   }
 }
 
+// The three plan kernels in one launch for plans of one block (n_slots <= kPlanChunk,
+// decode-sized batches): the single block's base is 0 for every expert, so counting,
+// the capacity cut, the scan and the stable scatter run back to back in shared memory
+// and give the same arrays as plan_count -> plan_scan -> plan_scatter.
+__global__ void __launch_bounds__(kPlanThreads) plan_small_kernel(const int32_t* __restrict__ idx, int64_t n_slots,
+                                                                  int k, int E, int capacity, int row_align,
+                                                                  int32_t* __restrict__ counts,
+                                                                  int32_t* __restrict__ offsets,
+                                                                  int32_t* __restrict__ slot_row,
+                                                                  int32_t* __restrict__ row_token) {
+  extern __shared__ int sm_plan[];
+  int* cnt = sm_plan;                    // [kPlanWarps][E]: counts, then running positions
+  int* s_off = cnt + kPlanWarps * E;     // [E + 1]: aligned kept rows, then their exclusive scan
+  __shared__ int s_warp[kPlanWarps];
+  for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  plan_warp_counts(idx, n_slots, E, 0, cnt);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kPlanWarps; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;              // warp w's first position among expert e's slots
+      run += c;
+    }
+    counts[e] = run;
+    const int kept = capacity > 0 ? min(run, capacity) : run;
+    s_off[e] = ((kept + row_align - 1) / row_align) * row_align;
+  }
+  __syncthreads();
+  // exclusive scan of s_off[0..E) over contiguous per-thread strips
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int lo = min(E, (int)threadIdx.x * per), hi = min(E, lo + per);
+  int local = 0;
+  for (int e = lo; e < hi; ++e) local += s_off[e];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_warp[w];
+  __syncthreads();                       // every strip has read its s_off entries
+  for (int e = lo; e < hi; ++e) {
+    const int a = s_off[e];
+    s_off[e] = run;
+    offsets[e] = run;
+    run += a;
+  }
+  if (threadIdx.x == blockDim.x - 1) {   // the last strip ends at the total
+    s_off[E] = run;
+    offsets[E] = run;
+  }
+  __syncthreads();
+  if (row_align > 1) {                   // alignment padding rows carry token -1
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int c = counts[e];           // written by this thread above
+      const int kept = capacity > 0 ? min(c, capacity) : c;
+      for (int r = s_off[e] + kept; r < s_off[e + 1]; ++r) row_token[r] = -1;
+    }
+  }
+  int* pos = cnt + warp * E;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int step = 0; step < kPlanSlotsPerWarp / 32; ++step) {
+    const int64_t s = warp * kPlanSlotsPerWarp + step * 32 + lane;
+    int e = -1;
+    if (s < n_slots) {
+      e = idx[s];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int p = 0;
+    if (e >= 0) p = pos[e] + __popc(peers & lt);
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) pos[e] += __popc(peers);
+    __syncwarp();
+    if (s < n_slots) {
+      if (e < 0 || (capacity > 0 && p >= capacity)) {
+        slot_row[s] = -1;
+      } else {
+        const int row = s_off[e] + p;
+        slot_row[s] = row;
+        row_token[row] = (int32_t)(s / k);
+      }
+    }
+  }
+}
+
 // rows[r,:] = x[row_token[r],:] for offsets[0] <= r < offsets[E] (a plan's offsets start
 // at 0; a slice of them selects a range of experts); one warp per row, 16-byte vectors
 // when every row starts on a 16-byte boundary.
@@ -249,6 +341,109 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, c
 #pragma unroll
       for (int q = 0; q < VEC; ++q) o.e[q] = Num<T>::from_f(acc[q]);
       *reinterpret_cast<uint4*>(out + (size_t)t * d + c) = o.u;
+    }
+  }
+}
+
+// combine_kernel for 16-byte-aligned rows, one warp per token: the token's k row indices
+// and weights are read once (lane j holds slot j) and shared by shuffles, and each lane
+// keeps 4 column pieces x 2 slots = 8 16-byte loads in flight.  Same arithmetic, in the
+// same order, as combine_kernel: acc = fl(acc + fl(w_j * y_j)) over j, then + shared.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) combine_warp_kernel(const T* __restrict__ y, const int32_t* __restrict__ slot_row,
+                                                           const float* __restrict__ w, int T_, int k, int d,
+                                                           const T* __restrict__ shared, T* __restrict__ out) {
+  constexpr int U = 4;
+  const int lane = threadIdx.x & 31;
+  const int nv = d / VEC;                       // 16-byte pieces per row
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T_; t += warps) {
+    const int my_r = lane < k ? slot_row[t * k + lane] : -1;
+    const float my_w = lane < k ? w[t * k + lane] : 0.f;
+    for (int c0 = lane; c0 < nv; c0 += 32 * U) {
+      float acc[U][VEC];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) acc[u][q] = 0.f;
+      for (int j = 0; j < k; j += 2) {
+        const int r0 = __shfl_sync(0xffffffffu, my_r, j);
+        const int r1 = j + 1 < k ? __shfl_sync(0xffffffffu, my_r, j + 1) : -1;
+        const float w0 = __shfl_sync(0xffffffffu, my_w, j);
+        const float w1 = __shfl_sync(0xffffffffu, my_w, (j + 1) & 31);
+        uint4 v0[U], v1[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int c = c0 + u * 32;
+          v0[u] = (r0 >= 0 && c < nv) ? *reinterpret_cast<const uint4*>(y + (int64_t)r0 * d + (int64_t)c * VEC)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+          v1[u] = (r1 >= 0 && c < nv) ? *reinterpret_cast<const uint4*>(y + (int64_t)r1 * d + (int64_t)c * VEC)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const T* e0 = reinterpret_cast<const T*>(&v0[u]);
+          const T* e1 = reinterpret_cast<const T*>(&v1[u]);
+          if (r0 >= 0) {
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[u][q] = __fadd_rn(acc[u][q], __fmul_rn(w0, Num<T>::to_f(e0[q])));
+          }
+          if (r1 >= 0) {
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[u][q] = __fadd_rn(acc[u][q], __fmul_rn(w1, Num<T>::to_f(e1[q])));
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32;
+        if (c >= nv) continue;
+        if (shared != nullptr) {
+          const uint4 sv = *reinterpret_cast<const uint4*>(shared + t * d + (int64_t)c * VEC);
+          const T* es = reinterpret_cast<const T*>(&sv);
+#pragma unroll
+          for (int q = 0; q < VEC; ++q) acc[u][q] = __fadd_rn(acc[u][q], Num<T>::to_f(es[q]));
+        }
+        union {
+          uint4 u4;
+          T e[VEC];
+        } o;
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) o.e[q] = Num<T>::from_f(acc[u][q]);
+        *reinterpret_cast<uint4*>(out + t * d + (int64_t)c * VEC) = o.u4;
+      }
+    }
+  }
+}
+
+// The permutation read token by token: x row t is read once and stored to each of its
+// k kept rows (slot_row[t*k + j] >= 0).  One warp per token, 16-byte vectors, 8 loads in
+// flight per lane.  Writes the same rows as permute_rows_kernel for a plan without
+// alignment padding (every row of [0, offsets[E]) is some slot's row).
+__global__ void __launch_bounds__(256) permute_tokens_kernel(const unsigned char* __restrict__ x, int64_t row_bytes,
+                                                             const int32_t* __restrict__ slot_row, int T_, int k,
+                                                             unsigned char* __restrict__ rows) {
+  constexpr int U = 8;
+  const int lane = threadIdx.x & 31;
+  const int nv = (int)(row_bytes >> 4);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T_; t += warps) {
+    const int my_r = lane < k ? slot_row[t * k + lane] : -1;
+    const unsigned live = __ballot_sync(0xffffffffu, my_r >= 0);
+    if (live == 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * row_bytes);
+    for (int c0 = lane; c0 < nv; c0 += 32 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = c0 + u * 32 < nv ? src[c0 + u * 32] : make_uint4(0u, 0u, 0u, 0u);
+      for (unsigned m = live; m != 0; m &= m - 1) {
+        const int j = __ffs(m) - 1;
+        const int r = __shfl_sync(0xffffffffu, my_r, j);
+        uint4* dst = reinterpret_cast<uint4*>(rows + (int64_t)r * row_bytes);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (c0 + u * 32 < nv) dst[c0 + u * 32] = v[u];
+      }
     }
   }
 }

@@ -3,20 +3,33 @@
 // tensor-core kernel's 128-row tiles would give the down projection of one token
 // 2 experts x 16 column tiles = 32 CTAs for 148 SMs.  Here one warp owns one output
 // column n of one group: its lanes read the weight row B[g][n][:] (and B3[g][n][:] for
-// SwiGLU) in 16-byte pieces, 8 pieces per row in flight per lane, multiply them with every row
-// of the group (A rows stay in L1/L2) and reduce across the warp.  Groups without rows
-// read nothing, so a token routed to 2 of 8 experts streams 2 experts' weights.
+// SwiGLU) in 16-byte pieces, 8 pieces per matrix in flight per lane, multiply them with
+// every row of the group (A rows stay in L1/L2) and reduce across the warp.  Groups
+// without rows read nothing, so a token routed to 2 of 8 experts streams 2 experts'
+// weights, and the warps stride over the (group with rows, column) pairs only.
+//
+// (A ring of 1-D bulk copies into shared memory, consumed by 8 warps behind a named
+// barrier, measured slower on the Mixtral decode shapes: 70 / 146 us for the down and
+// gate/up projections against 60 / 83 us here; the per-stage barrier and reduction cost
+// more than the deeper copies save.)
 //
 // Same grouping contract as the other grouped GEMMs: group g owns rows
 // [offsets[g], ends ? ends[g] : offsets[g+1]) of A [rows, K], clamped to rows_cap;
-// B is [G, N, K].  K % 8 == 0, A and B 16-byte aligned.
+// B is [G, N, K].  K % 8 == 0, A and B 16-byte aligned.  With a_index, row r of the
+// groups reads row a_index[r] of A (the dispatch plan's row_token: the layer's first GEMM
+// gathers the token rows itself, no permuted copy); an index outside [0, a_rows) reads
+// zeros.
 #pragma once
 #include "common.cuh"
 
 namespace smoe {
 namespace gemv {
 
-constexpr int THREADS = 256, MAX_ROWS = 2, MAX_GROUPS = 1024, UNROLL = 8;
+constexpr int THREADS = 256, MAX_ROWS = 2, MAX_GROUPS = 1024;
+// 16-byte weight loads in flight per lane, per matrix.  16 for the one-matrix kernel
+// measured slower on the Mixtral down projection (67 vs 60 us): it fits 2 blocks per SM
+// instead of 3, and more warps beat more bytes per warp here.
+constexpr int UNROLL = 8;
 // Batches this small take this kernel.  Measured on the Mixtral layer (1 B200, 1965 MHz):
 // one token (2 rows, one per expert) runs gate/up in 92 us and down in 62 us against 119
 // and 95 us on the tensor cores.  An earlier build of this kernel for up to 16 rows took
@@ -44,24 +57,35 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
                                                                int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                                                                const int32_t* __restrict__ offsets,
                                                                const int32_t* __restrict__ ends, int G, int N, int K,
-                                                               int rows_cap) {
-  __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS];
+                                                               int rows_cap, const int32_t* __restrict__ a_index,
+                                                               int a_rows) {
+  // Groups with rows, compacted: the warps stride over (active group, column) tasks only,
+  // so a token routed to 2 of 8 experts keeps every warp on a weight row of those 2.
+  __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS], s_act[MAX_GROUPS];
+  __shared__ int s_nact;
   for (int g = threadIdx.x; g < G; g += blockDim.x) {
     const int b = min(max(offsets[g], 0), rows_cap);
     s_beg[g] = b;
     s_fin[g] = min(max(ends != nullptr ? ends[g] : offsets[g + 1], b), min(rows_cap, b + MAX_ROWS));
   }
   __syncthreads();
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int g = 0; g < G; ++g)
+      if (s_fin[g] > s_beg[g]) s_act[n++] = g;
+    s_nact = n;
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t tasks = (int64_t)G * N;
+  const int64_t tasks = (int64_t)s_nact * N;
   const int chunks = K / 8;  // 16-byte pieces per row
   for (int64_t task = warp; task < tasks; task += nwarps) {
-    const int g = (int)(task / N);
-    const int n = (int)(task - (int64_t)g * N);
+    const int a = (int)(task / N);
+    const int g = s_act[a];
+    const int n = (int)(task - (int64_t)a * N);
     const int b = s_beg[g], nr = s_fin[g] - b;
-    if (nr <= 0) continue;
     const uint4* brow = reinterpret_cast<const uint4*>(B + ((int64_t)g * N + n) * K);
     const uint4* b3row = EPI == SMOE_EPI_SWIGLU ? reinterpret_cast<const uint4*>(B3 + ((int64_t)g * N + n) * K)
                                                 : nullptr;
@@ -78,8 +102,9 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
       }
 #pragma unroll
       for (int r = 0; r < MAX_ROWS; ++r) {
-        if (r < nr) {
-          const uint4* arow = reinterpret_cast<const uint4*>(A + (int64_t)(b + r) * K);
+        const int src = r < nr ? (a_index != nullptr ? a_index[b + r] : b + r) : -1;
+        if (src >= 0 && src < a_rows) {
+          const uint4* arow = reinterpret_cast<const uint4*>(A + (int64_t)src * K);
 #pragma unroll
           for (int u = 0; u < UNROLL; ++u) {
             const int c = c0 + u * 32;

@@ -37,7 +37,10 @@ def expected_plan(idx: np.ndarray, E: int, capacity: int, row_align: int):
 @pytest.mark.parametrize("T,k,E,cap,align", [(0, 2, 8, 0, 1), (1, 2, 8, 0, 1), (63, 2, 8, 0, 1), (64, 2, 8, 0, 1),
                                              (65, 2, 8, 0, 128), (1000, 2, 8, 0, 1), (5000, 8, 128, 0, 1),
                                              (3000, 2, 64, 100, 1), (777, 3, 7, 50, 16), (9000, 2, 8, 2000, 1),
-                                             (20000, 8, 130, 900, 8)])
+                                             (20000, 8, 130, 900, 8),
+                                             # one-block plans (T * k <= 2048: one launch)
+                                             (600, 3, 7, 50, 16), (256, 8, 128, 0, 1), (1024, 2, 8, 300, 1),
+                                             (2048, 1, 3000, 0, 1), (1, 2, 4096, 0, 4), (2049, 1, 8, 0, 1)])
 def test_plan_bit_exact(K, T, k, E, cap, align):
     rng = np.random.default_rng(T + E)
     # skewed routing: some experts much more popular

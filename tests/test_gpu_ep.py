@@ -42,6 +42,9 @@ CASES = {
 # send kernel); the host-laid-out schedules and the collective transport stay selectable
 TRANSPORTS = ["p2p", "p2p-local_first", "p2p+copy-local_first", "p2p+split-local_first", "p2p-chunked",
               "collective"]
+# SMOE_EP_TEST_TRANSPORTS=a,b,... runs a subset (machines billed per GPU-minute)
+if os.environ.get("SMOE_EP_TEST_TRANSPORTS"):
+    TRANSPORTS = [t for t in os.environ["SMOE_EP_TEST_TRANSPORTS"].split(",") if t in TRANSPORTS]
 
 
 def _rdzv(tmp_path):
@@ -56,6 +59,9 @@ def _configure(m, transport):
     m.comm.return_mode = "copy" if "copy" in opts else "fused"
     if "split" in opts:                   # own rows in two halves even with 2 ranks
         m.comm.split_min_ws = 2
+
+
+_ORACLE = {}   # (case, routing digest) -> this rank's oracle rows: one oracle run per case
 
 
 def _run_case(rank, ws, dev, case, transport):
@@ -104,8 +110,11 @@ def _run_case(rank, ws, dev, case, transport):
     p.logit_bias = bias
     if shared:
         p.sw1, p.sw3, p.sw2 = r(sw[0]), r(sw[1]), r(sw[2])
-    refs = O.moe_forward(xs, p, ws=ws, k=k, capacity_factor=cf, acc=np.float32, routing=routing)
-    ref = refs[rank]
+    import hashlib
+    key = (case, hashlib.sha1(b"".join(a.tobytes() + b.tobytes() for a, b in routing)).hexdigest())
+    if key not in _ORACLE:
+        _ORACLE[key] = O.moe_forward(xs, p, ws=ws, k=k, capacity_factor=cf, acc=np.float32, routing=routing)[rank]
+    ref = _ORACLE[key]
     # routing against the oracle's own router: differences only at near-ties
     o_idx, _, logits = O.route(xs[rank], p.gate, k, p.logit_bias)
     own = routing[rank][0]

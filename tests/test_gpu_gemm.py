@@ -170,3 +170,56 @@ def test_grouped_gemm_row_addresses(K, dtype, cap):
             assert torch.equal(got[row], want), (s, r)
     assert (got[~written] == 7.0).all()
     assert K.read_device_error("cuda") == 0
+
+
+# Decode-sized batches (at most 2 rows, the warp-per-column kernel) at the shapes that
+# matter: the Mixtral gate/up and down projections, K up to 20000, odd K / N, SwiGLU with
+# one or two rows per group, a range of columns crossing from one group to the next.
+DECODE = [
+    ([0, 1, 0, 1], 4096, 2048, 1),     # Mixtral gate/up shape: 2 SwiGLU columns per stage
+    ([1, 1], 14336, 1024, 0),          # Mixtral down shape: 1 column per stage, 5 stages
+    ([2], 16384, 512, 0),              # two rows of one group, 4 stages
+    ([1, 1], 16392, 256, 0),           # 4 stages, K % 256 != 0
+    ([0, 1], 64, 1000, 0),             # 4 columns per stage, N % 4 != 0
+    ([1, 1], 2056, 300, 1),            # 3 SwiGLU columns per stage, an odd last piece
+    ([1, 1], 6144, 700, 0),            # 2 columns per stage
+    ([1, 1], 20000, 256, 0),           # 3 stages would fit: warp-per-column kernel
+    ([1, 0, 1], 12288, 128, 1),        # SwiGLU, 3 stages would fit: warp-per-column kernel
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sizes,K_,N,epi", DECODE)
+def test_decode_gemv(K, dtype, sizes, K_, N, epi):
+    A, B, B3, offs, rows = make_groups(sizes, K_, N, dtype, seed=K_ + N, std=0.02)
+    Ad, Bd, B3d, od = A.cuda(), B.cuda(), B3.cuda(), offs.cuda()
+    if epi:
+        out = K.grouped_gemm(Ad, Bd, od, B3=B3d, epilogue=1)
+        ref = ref_swiglu(A, B, B3, offs)[:rows]
+    else:
+        out = K.grouped_gemm(Ad, Bd, od)
+        ref = ref_store(A, B, offs)[:rows]
+    assert elementwise_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2
+    again = K.grouped_gemm(Ad, Bd, od, B3=B3d, epilogue=1) if epi else K.grouped_gemm(Ad, Bd, od)
+    assert torch.equal(out, again)                     # fixed summation order
+    if not epi:
+        f32 = K.grouped_gemm(Ad, Bd, od, out_dtype=torch.float32)[:rows].cpu().numpy()
+        assert max_abs_err(f32, ref.numpy()) <= 1e-5 * np.sqrt(K_) * max(1.0, float(ref.abs().max()))
+    assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("K_,N", [(14336, 512), (16392, 64)])
+def test_decode_gemv_row_addresses(K, K_, N):
+    """Two rows stored through row addresses (one null: skipped), bit for bit the rows of
+    the plain call."""
+    A, B, _, offs, rows = make_groups([1, 0, 1], K_, N, torch.bfloat16, seed=3, std=0.02)
+    Ad, Bd, od = A.cuda(), B.cuda(), offs.cuda()
+    y = K.grouped_gemm(Ad, Bd, od)
+    buf = torch.full((4, N), 7.0, dtype=torch.bfloat16, device="cuda")
+    rb = N * 2
+    row_ptrs = torch.tensor([buf.data_ptr() + 3 * rb, 0], dtype=torch.int64, device="cuda")
+    assert K.grouped_gemm(Ad, Bd, od, row_ptrs=row_ptrs) is None
+    got = buf.cpu()
+    assert torch.equal(got[3], y[0].cpu())
+    assert (got[:3] == 7.0).all()
+    assert K.read_device_error("cuda") == 0

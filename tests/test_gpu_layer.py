@@ -71,6 +71,8 @@ def test_standard_linear_fp16_vs_reference(M):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("T,d,E,k,F,cf,shared,bias", [
     (1, 256, 8, 2, 512, None, False, False),
+    (1, 256, 8, 1, 512, None, True, True),       # decode: rows gathered by the gate/up kernel
+    (2, 512, 16, 1, 256, 1.0, True, True),
     (257, 512, 8, 2, 1024, None, False, False),
     (1000, 256, 64, 2, 256, 1.25, False, False),
     (600, 256, 32, 8, 128, None, True, True),
