@@ -221,13 +221,22 @@ template <int EPI, typename T, typename OutT>
 int launch_gemv_t(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs,
                   const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
                   cudaStream_t st, const int32_t* a_index, int a_rows) {
-  // one warp per (group with rows, column); at most min(G, rows_cap) groups have rows
-  const int64_t warps = std::min<int64_t>(G, std::max<int64_t>(rows_cap, 1)) * N;
-  const unsigned grid = (unsigned)std::max<int64_t>(
-      1, std::min<int64_t>(cdiv(warps * 32, gemv::THREADS), (int64_t)device_sms() * 8));
-  gemv::grouped_gemv_kernel<EPI, T, OutT><<<grid, gemv::THREADS, 0, st>>>(
-      (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap, a_index,
-      a_rows);
+  // one warp (two for rows of 8192 or more elements) per (group with rows, column); at
+  // most min(G, rows_cap) groups have rows
+  const int64_t cols = std::min<int64_t>(G, std::max<int64_t>(rows_cap, 1)) * N;
+  if (K >= 8192) {
+    constexpr int CPB = gemv::THREADS / 32 / 2;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(cols, CPB), 65535));
+    gemv::grouped_gemv_kernel<EPI, T, OutT, 2><<<grid, gemv::THREADS, 0, st>>>(
+        (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap, a_index,
+        a_rows);
+  } else {
+    const unsigned grid = (unsigned)std::max<int64_t>(
+        1, std::min<int64_t>(cdiv(cols * 32, gemv::THREADS), (int64_t)device_sms() * 8));
+    gemv::grouped_gemv_kernel<EPI, T, OutT, 1><<<grid, gemv::THREADS, 0, st>>>(
+        (const T*)A, (const T*)B, (const T*)B3, (OutT*)C, N, row_ptrs, offsets, ends, G, N, K, (int)rows_cap, a_index,
+        a_rows);
+  }
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }

@@ -51,7 +51,11 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-template <int EPI, typename T, typename OutT>
+// KS warps share one column: warp part p of a column reads the p-th of KS equal slices of
+// K, and the slices' sums are added in slice order (deterministic).  KS = 2 for long rows
+// (the down projection's 28 KB rows): half the load rounds per task and twice the tasks,
+// so the last wave of tasks is shorter.
+template <int EPI, typename T, typename OutT, int KS>
 __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                                const T* __restrict__ B3, OutT* __restrict__ C,
                                                                int64_t ldc, const uint64_t* __restrict__ row_ptrs,
@@ -59,10 +63,13 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
                                                                const int32_t* __restrict__ ends, int G, int N, int K,
                                                                int rows_cap, const int32_t* __restrict__ a_index,
                                                                int a_rows) {
+  constexpr int CPB = (THREADS / 32) / KS;   // columns per block and step
+  constexpr int H = EPI == SMOE_EPI_SWIGLU ? 2 : 1;
   // Groups with rows, compacted: the warps stride over (active group, column) tasks only,
   // so a token routed to 2 of 8 experts keeps every warp on a weight row of those 2.
   __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS], s_act[MAX_GROUPS];
   __shared__ int s_nact;
+  __shared__ float s_part[CPB][KS][MAX_ROWS][H];
   for (int g = threadIdx.x; g < G; g += blockDim.x) {
     const int b = min(max(offsets[g], 0), rows_cap);
     s_beg[g] = b;
@@ -77,28 +84,32 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int wib = threadIdx.x >> 5;          // warp in block
+  const int slot = wib / KS, part = wib - (wib / KS) * KS;
   const int64_t tasks = (int64_t)s_nact * N;
-  const int chunks = K / 8;  // 16-byte pieces per row
-  for (int64_t task = warp; task < tasks; task += nwarps) {
-    const int a = (int)(task / N);
+  const int chunks = K / 8;                  // 16-byte pieces per row
+  const int per = (chunks + KS - 1) / KS;
+  const int c_lo = min(chunks, part * per), c_hi = min(chunks, c_lo + per);
+  for (int64_t base = (int64_t)blockIdx.x * CPB; base < tasks; base += (int64_t)gridDim.x * CPB) {
+    const int64_t task = base + slot;
+    const bool have = task < tasks;
+    const int a = have ? (int)(task / N) : 0;
     const int g = s_act[a];
-    const int n = (int)(task - (int64_t)a * N);
-    const int b = s_beg[g], nr = s_fin[g] - b;
+    const int n = have ? (int)(task - (int64_t)a * N) : 0;
+    const int b = s_beg[g], nr = have ? s_fin[g] - b : 0;
     const uint4* brow = reinterpret_cast<const uint4*>(B + ((int64_t)g * N + n) * K);
     const uint4* b3row = EPI == SMOE_EPI_SWIGLU ? reinterpret_cast<const uint4*>(B3 + ((int64_t)g * N + n) * K)
                                                 : nullptr;
     float acc[MAX_ROWS], acc3[MAX_ROWS];
 #pragma unroll
     for (int r = 0; r < MAX_ROWS; ++r) acc[r] = acc3[r] = 0.0f;
-    for (int c0 = lane; c0 < chunks; c0 += 32 * UNROLL) {
+    for (int c0 = c_lo + lane; have && c0 < c_hi; c0 += 32 * UNROLL) {
       uint4 wv[UNROLL], w3[UNROLL];
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         const int c = c0 + u * 32;
-        wv[u] = c < chunks ? __ldcs(brow + c) : make_uint4(0u, 0u, 0u, 0u);  // weights: streamed once
-        if (EPI == SMOE_EPI_SWIGLU) w3[u] = c < chunks ? __ldcs(b3row + c) : make_uint4(0u, 0u, 0u, 0u);
+        wv[u] = c < c_hi ? __ldcs(brow + c) : make_uint4(0u, 0u, 0u, 0u);  // weights: streamed once
+        if (EPI == SMOE_EPI_SWIGLU) w3[u] = c < c_hi ? __ldcs(b3row + c) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int r = 0; r < MAX_ROWS; ++r) {
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
 #pragma unroll
           for (int u = 0; u < UNROLL; ++u) {
             const int c = c0 + u * 32;
-            if (c < chunks) {
+            if (c < c_hi) {
               const uint4 av = __ldg(arow + c);
               fma8<T>(av, wv[u], acc[r]);
               if (EPI == SMOE_EPI_SWIGLU) fma8<T>(av, w3[u], acc3[r]);
@@ -117,22 +128,43 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
         }
       }
     }
+    float v[MAX_ROWS][H];
 #pragma unroll
     for (int r = 0; r < MAX_ROWS; ++r) {
-      if (r < nr) {
-        const float v = warp_sum(acc[r]);
-        float out = v;
-        if (EPI == SMOE_EPI_SWIGLU) {
-          const float u = warp_sum(acc3[r]);
-          out = v / (1.0f + __expf(-v)) * u;
-        }
-        if (lane == 0) {
+      v[r][0] = warp_sum(acc[r]);
+      if (EPI == SMOE_EPI_SWIGLU) v[r][H - 1] = warp_sum(acc3[r]);
+    }
+    if (KS > 1) {                            // slice sums meet in shared memory
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < MAX_ROWS; ++r)
+#pragma unroll
+          for (int h = 0; h < H; ++h) s_part[slot][part][r][h] = v[r][h];
+      __syncthreads();
+      if (part == 0)
+#pragma unroll
+        for (int r = 0; r < MAX_ROWS; ++r)
+#pragma unroll
+          for (int h = 0; h < H; ++h) {
+            float t = s_part[slot][0][r][h];
+#pragma unroll
+            for (int q = 1; q < KS; ++q) t += s_part[slot][q][r][h];
+            v[r][h] = t;
+          }
+    }
+    if (part == 0 && lane == 0) {
+#pragma unroll
+      for (int r = 0; r < MAX_ROWS; ++r) {
+        if (r < nr) {
+          float out = v[r][0];
+          if (EPI == SMOE_EPI_SWIGLU) out = out / (1.0f + __expf(-out)) * v[r][H - 1];
           const int row = b + r;
           OutT* crow = row_ptrs ? reinterpret_cast<OutT*>(row_ptrs[row]) : C + (int64_t)row * ldc;
           if (crow != nullptr) crow[n] = Num<OutT>::from_f(out);
         }
       }
     }
+    if (KS > 1) __syncthreads();             // s_part is reused by the next step
   }
   if (row_ptrs) __threadfence_system();  // rows in another GPU's memory: visible before exit
 }

@@ -187,7 +187,8 @@ class ExpertParallelExchange:
         if self.schedule == "device":
             return (f"{self.transport} transport, device schedule (layout on the device, rows stored into "
                     f"the peers by the send kernel, fused return, no host wait), token dedup {self.dedup} "
-                    f"(dedup forwards use the local-first schedule), max {self.max_tokens} tokens per rank")
+                    f"(dedup forwards with k a multiple of 4 on the device schedule too, others on the host-laid-out "
+                    f"one), max {self.max_tokens} tokens per rank")
         return (f"{self.transport} transport, local_first schedule, {self.return_mode} return, "
                 f"token dedup {self.dedup}, own rows split from {self.split_min_ws} ranks")
 
