@@ -417,6 +417,12 @@ int router_small_dispatch(const void* x, const void* wg, const float* bias, int 
 template <typename T, int NT>
 int launch_router_mma(const void* x, const void* wg, const float* bias, int T_, int d, int E, int k, int32_t* idx,
                       float* w, float* logits, cudaStream_t st) {
+  if (T_ <= 64 && d % 512 == 0) {  // decode-sized: sixteen warps per 16 tokens
+    router_mma_kernel<T, NT, 16, 16><<<(unsigned)cdiv(T_, 16), 512, 0, st>>>((const T*)x, (const T*)wg, bias, T_, d,
+                                                                              E, k, idx, w, logits);
+    SMOE_CK(cudaGetLastError());
+    return SMOE_OK;
+  }
   if (d % 128 == 0) {  // four warps per 16 tokens
     const int64_t blocks = cdiv(T_, 16);
     if (blocks > INT32_MAX) return SMOE_ERR_UNSUPPORTED;

@@ -157,13 +157,17 @@ __device__ __forceinline__ void mma_step(float (&c)[4], const uint4& a0, const u
 // each dot product unchanged and makes every fragment one contiguous 16-byte load.  The
 // slice sums meet in shared memory (added in a fixed order) and one lane per token does
 // top-k + softmax.  The router reads x once: it is bound by HBM bandwidth.
-template <typename T, int NT, int KSPLIT>  // E <= 8 * NT; KSPLIT warps share 16 tokens
-__global__ void __launch_bounds__(128) router_mma_kernel(const T* __restrict__ x, const T* __restrict__ wg,
-                                                         const float* __restrict__ bias, int T_, int d, int E, int k,
-                                                         int32_t* __restrict__ idx, float* __restrict__ w,
-                                                         float* __restrict__ logits_out) {
-  constexpr int GROUPS = 4 / KSPLIT;       // 16-token groups per block of 4 warps
-  __shared__ float s_part[4][16][8 * NT];  // per warp: partial logits of its 16 tokens
+// WARPS = 16, KSPLIT = 16 (d % 512 == 0) serves decode-sized batches: one block per 16
+// tokens with 16 warps on the d columns, so a single token's router is one batch of loads
+// per warp instead of four.
+template <typename T, int NT, int KSPLIT, int WARPS = 4>  // E <= 8 * NT; KSPLIT warps share 16 tokens
+__global__ void __launch_bounds__(WARPS * 32) router_mma_kernel(const T* __restrict__ x, const T* __restrict__ wg,
+                                                                const float* __restrict__ bias, int T_, int d, int E,
+                                                                int k, int32_t* __restrict__ idx,
+                                                                float* __restrict__ w,
+                                                                float* __restrict__ logits_out) {
+  constexpr int GROUPS = WARPS / KSPLIT;       // 16-token groups per block
+  __shared__ float s_part[WARPS][16][8 * NT];  // per warp: partial logits of its 16 tokens
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, q = lane & 3;
   const int part = warp % KSPLIT;          // which slice of the d columns

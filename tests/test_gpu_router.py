@@ -61,7 +61,9 @@ def test_topk_nan_and_inf(K):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("T,d,E,k", [(1, 64, 8, 2), (63, 128, 8, 2), (64, 256, 8, 2), (65, 512, 8, 1),
                                      (300, 4096, 8, 2), (257, 96, 7, 3), (100, 128, 16, 4), (77, 64, 32, 8),
-                                     (200, 256, 64, 8), (130, 128, 128, 8), (50, 72, 40, 2), (33, 20, 5, 5)])
+                                     (200, 256, 64, 8), (130, 128, 128, 8), (50, 72, 40, 2), (33, 20, 5, 5),
+                                     # decode-sized batches (T <= 64, d % 512 == 0): 16 warps per 16 tokens
+                                     (1, 4096, 8, 2), (17, 1024, 16, 4), (64, 512, 32, 8), (40, 2048, 24, 3)])
 def test_router_fused_vs_oracle(K, dtype, T, d, E, k):
     rng = np.random.default_rng(T * 1000 + E)
     x = rounded(rng.standard_normal((T, d)).astype(np.float32), dtype)
