@@ -80,6 +80,22 @@ __device__ __forceinline__ void load_vec_f(const T* p, float (&f)[VEC]) {
   }
 }
 
+// --------------------------------------------------------------------------- launch order
+// Programmatic dependent launch.  A kernel launched with the programmatic-serialization
+// attribute (the layer forward launches its chain that way) may be scheduled while its
+// predecessor in the stream is still running; it stops here, before its first global
+// memory access, until the predecessor has completed and its writes are visible, then
+// lets its own successor start launching.  Both instructions are no-ops for a kernel
+// launched the ordinary way, so every kernel that may be launched either way calls this
+// first.  Long kernels (the grouped GEMMs) only wait: their successor is released when
+// their CTAs exit, because a successor released at their start would place its CTAs
+// beside theirs for the whole GEMM (measured 5 % slower on the 16384-token layer).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_and_release() {
+  pdl_wait();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------------------------- warps
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

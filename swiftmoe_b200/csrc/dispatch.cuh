@@ -42,6 +42,7 @@ __device__ __forceinline__ void plan_warp_counts(const int32_t* __restrict__ idx
 // Kernel 1: hist[b][e] = number of slots of block b routed to expert e.
 __global__ void __launch_bounds__(kPlanThreads) plan_count_kernel(const int32_t* __restrict__ idx, int64_t n_slots,
                                                                   int E, int32_t* __restrict__ hist) {
+  pdl_wait_and_release();
   extern __shared__ int cnt[];  // [kPlanWarps][E]
   for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
@@ -61,6 +62,7 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(const int32_t* __restri
                                                          int capacity, int row_align, int32_t* __restrict__ base,
                                                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                                                          int32_t* __restrict__ row_token) {
+  pdl_wait_and_release();
   extern __shared__ int s_kept[];  // [E] aligned kept counts, then scanned in place
   __shared__ int s_warp[32];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(const int32_
                                                                     const int32_t* __restrict__ offsets,
                                                                     int32_t* __restrict__ slot_row,
                                                                     int32_t* __restrict__ row_token) {
+  pdl_wait_and_release();
   extern __shared__ int cnt[];  // [kPlanWarps][E], turned into per-warp running positions
   for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_small_kernel(const int32_t*
                                                                   int32_t* __restrict__ offsets,
                                                                   int32_t* __restrict__ slot_row,
                                                                   int32_t* __restrict__ row_token) {
+  pdl_wait_and_release();
   extern __shared__ int sm_plan[];
   int* cnt = sm_plan;                    // [kPlanWarps][E]: counts, then running positions
   int* s_off = cnt + kPlanWarps * E;     // [E + 1]: aligned kept rows, then their exclusive scan
@@ -268,6 +272,7 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const unsigned char* 
                                                            bool vec, const int32_t* __restrict__ row_token,
                                                            const int32_t* __restrict__ offsets, int E,
                                                            unsigned char* __restrict__ rows) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int64_t first = offsets[0];
   const int64_t total = offsets[E];
@@ -308,6 +313,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ slot_row,
                                                       const float* __restrict__ w, int T_, int k, int d,
                                                       const T* __restrict__ shared, T* __restrict__ out) {
+  pdl_wait_and_release();
   const int per_row = d / VEC;
   const int64_t total = (int64_t)T_ * per_row;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
@@ -353,6 +359,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(256) combine_warp_kernel(const T* __restrict__ y, const int32_t* __restrict__ slot_row,
                                                            const float* __restrict__ w, int T_, int k, int d,
                                                            const T* __restrict__ shared, T* __restrict__ out) {
+  pdl_wait_and_release();
   constexpr int U = 4;
   const int lane = threadIdx.x & 31;
   const int nv = d / VEC;                       // 16-byte pieces per row
@@ -423,6 +430,7 @@ __global__ void __launch_bounds__(256) combine_warp_kernel(const T* __restrict__
 __global__ void __launch_bounds__(256) permute_tokens_kernel(const unsigned char* __restrict__ x, int64_t row_bytes,
                                                              const int32_t* __restrict__ slot_row, int T_, int k,
                                                              unsigned char* __restrict__ rows) {
+  pdl_wait_and_release();
   constexpr int U = 8;
   const int lane = threadIdx.x & 31;
   const int nv = (int)(row_bytes >> 4);

@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemm_f32_kernel(const floa
                                                                       const int32_t* __restrict__ offsets,
                                                                       const int32_t* __restrict__ ends, int G, int N,
                                                                       int K, int rows_cap) {
+  pdl_wait();
   __shared__ int s_beg[MAX_GROUPS], s_fin[MAX_GROUPS];
   __shared__ int s_ts[MAX_GROUPS + 1];
   __shared__ __align__(16) float As[2][BK][BM + PAD];

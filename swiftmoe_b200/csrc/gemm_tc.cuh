@@ -252,6 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                         const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
                         int K, int rows_cap, int gm, uint32_t idesc) {
+  pdl_wait();
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

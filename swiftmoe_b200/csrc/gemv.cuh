@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(THREADS, 2) grouped_gemv_kernel(const T* __res
                                                                const int32_t* __restrict__ ends, int G, int N, int K,
                                                                int rows_cap, const int32_t* __restrict__ a_index,
                                                                int a_rows) {
+  pdl_wait_and_release();
   constexpr int CPB = (THREADS / 32) / KS;   // columns per block and step
   constexpr int H = EPI == SMOE_EPI_SWIGLU ? 2 : 1;
   // Groups with rows, compacted: the warps stride over (active group, column) tasks only,

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
                                                            const float* __restrict__ bias, int T_, int d, int E,
                                                            int k, int32_t* __restrict__ idx, float* __restrict__ w,
                                                            float* __restrict__ logits_out) {
+  pdl_wait_and_release();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* s_wg = reinterpret_cast<T*>(smem_raw);
   // stage the gate matrix once per block
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(WARPS * 32) router_mma_kernel(const T* __restr
                                                                 int k, int32_t* __restrict__ idx,
                                                                 float* __restrict__ w,
                                                                 float* __restrict__ logits_out) {
+  pdl_wait_and_release();
   constexpr int GROUPS = WARPS / KSPLIT;       // 16-token groups per block
   __shared__ float s_part[WARPS][16][8 * NT];  // per warp: partial logits of its 16 tokens
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(WARPS * 32) router_mma_kernel(const T* __restr
 __global__ void __launch_bounds__(256) topk_from_logits_kernel(const float* __restrict__ logits,
                                                                const float* __restrict__ bias, int T_, int E, int k,
                                                                int32_t* __restrict__ idx, float* __restrict__ w) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= T_) return;
