@@ -427,6 +427,38 @@ SMOE_API int smoe_wgrad_gemm_rows(const void* A, int64_t lda, const void* B, int
                                   const int32_t* k_offsets, int G, int M, int N, int64_t K, float* C,
                                   smoe_stream_t stream);
 
+/* ---- The layer backward in pieces, for expert parallelism: the routed rows' part runs on
+ * the rank that owns their experts, the tokens' part on the tokens' own rank.  The
+ * reference is forward-only; these differentiate its forward (models/baseline_moe.py:
+ * 56-189, models/ultimate_moe.py:222-252, 288-295), as smoe_layer_bwd does in one call.
+ *
+ * SwiGLU rows, in place: ab[r] = [a | b] (pre-activations, [rows, 2F]) -> [da | db];
+ * g[r] (the gradient reaching h before the gate weight, dout_r W2, [rows, F]) -> w_r * h;
+ * dw_row[r] = <g_r, h_r> fp32 (the gate weight's gradient; may be NULL).  Rows r <
+ * *n_rows (n_rows NULL: all rows_cap); row_w NULL means w = 1.  16-bit, F % 8 == 0.     */
+SMOE_API int smoe_swiglu_bwd(void* ab, void* g, const float* row_w, const int32_t* n_rows, int64_t rows_cap,
+                             int F, int dtype, float* dw_row, smoe_stream_t stream);
+/* Linear-expert rows, in place: dw_row[r] = <g_r, x_r> (g = dout_r Wl), g[r] -> w_r g_r
+ * (the rows' input gradient), dr[r] -> w_r dr_r (their output gradient).  d % 8 == 0.   */
+SMOE_API int smoe_linear_bwd(void* g, const void* xr, void* dr, const float* row_w, const int32_t* n_rows,
+                             int64_t rows_cap, int d, int dtype, float* dw_row, smoe_stream_t stream);
+/* dx[t] = sum_j dxr[slot_row[t,j]] (kept slots) + dxs[t] (shared expert, may be NULL) +
+ * sum_j dsel_tj Wg[idx[t,j]], one rounding; dsel_tj = w_tj (dw_tj - sum_j' w_tj' dw_tj'),
+ * dw_tj = dw_row[slot_row[t,j]] (0 for dropped slots), the softmax-over-top-k backward of
+ * the router.  dsel_row (may be NULL) gets dsel_tj at slot_row_full[t,j] (a plan over
+ * every slot) for smoe_router_dwg.                                                      */
+SMOE_API int smoe_moe_bwd_dx(const void* dxr, const int32_t* slot_row, const int32_t* idx, const float* w,
+                             const float* dw_row, const void* gate_w, const void* dxs, int T, int k, int d,
+                             int dtype, void* dx, const int32_t* slot_row_full, float* dsel_row,
+                             smoe_stream_t stream);
+/* Gate gradient dgate[e] = sum over the rows r of expert e in a plan over every slot
+ * (offsets_full [E+1], row_token_full) of dsel_row[r] * x[row_token_full[r]], fp32 [E, d],
+ * summed in a fixed order.                                                              */
+SMOE_API size_t smoe_router_dwg_workspace_size(int d, int E);
+SMOE_API int smoe_router_dwg(const void* x, const int32_t* row_token_full, const int32_t* offsets_full,
+                             const float* dsel_row, int d, int E, int dtype, float* dgate, void* workspace,
+                             size_t workspace_bytes, smoe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

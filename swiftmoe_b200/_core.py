@@ -330,14 +330,51 @@ class MoECore(nn.Module):
         """The gradients of _grad_params() from _backward_fused's dict."""
         raise NotImplementedError
 
+    def _backward_ep(self, x: torch.Tensor, dout: torch.Tensor) -> Dict[str, torch.Tensor]:
+        """Expert parallelism (world size > 1): ``ep.ExpertParallelExchange.layer_backward``
+        with this layer's weights; the same dict as ``_backward_fused``.  The gate's and the
+        shared expert's gradients are this rank's contribution (replicated weights); the
+        local experts' gradients cover every rank's tokens."""
+        if self.comm is None:
+            raise NotImplementedError("expert-parallel backward needs the layer's exchange (world size > 1)")
+        T = x.shape[0]
+        if self.expert_type == "swiglu":
+            w1, w3, w2 = self._swiglu()
+            F = self.d_ff
+            experts = dict(kind="swiglu", w1=w1.detach(), w3=w3.detach(),
+                           w2t=self._cached("w2t", [w2], lambda: K.transpose_batched(w2.detach().contiguous())),
+                           w13t=self._cached("w13t", [w1, w3], lambda: K.transpose_batched(
+                               torch.cat([w1.detach(), w3.detach()], dim=1).contiguous())))
+        else:
+            wl, xw_layout = self._linear_xw()
+            experts = dict(kind="linear", w=wl.contiguous(), transposed=bool(xw_layout))
+        sh = None
+        if self._shared() is not None:
+            s1, s3, s2 = self._shared()
+            sh = dict(w1=s1.detach().unsqueeze(0), w3=s3.detach().unsqueeze(0),
+                      w2t=self._cached("sw2t", [s2], lambda: K.transpose_batched(s2.detach().unsqueeze(0).contiguous())),
+                      w13t=self._cached("sw13t", [s1, s3], lambda: K.transpose_batched(
+                          torch.cat([s1.detach(), s3.detach()], dim=0).unsqueeze(0).contiguous())))
+        g = self.comm.layer_backward(x.contiguous(), dout.contiguous(), self._gate().detach().contiguous(),
+                                     self._logit_bias(), self.top_k, self._capacity(T), experts, sh)
+        out = dict(x=g["x"], gate=g["gate"])
+        if self.expert_type == "swiglu":
+            out.update(w1=g["w13"][:, :F], w3=g["w13"][:, F:], w2=g["w2"])
+        else:
+            out.update(expert_w=g["lin"])
+        if sh is not None:
+            Fs = sh["w1"].shape[1]
+            out.update(sw1=g["s13"][:Fs], sw3=g["s13"][Fs:], sw2=g["s2"])
+        return out
+
     def _backward_fused(self, x: torch.Tensor, dout: torch.Tensor) -> Dict[str, torch.Tensor]:
         """One ``smoe_layer_bwd`` call: gradients (fp32 for the weights) of the output with
         respect to x ("x", x.dtype), the gate ("gate" [E, d]) and the experts ("w1", "w3"
         [E_l, F, d], "w2" [E_l, d, F]; "sw1", "sw3", "sw2" for the shared expert)."""
-        if self.ws != 1:
-            raise NotImplementedError("the backward pass runs on one GPU (expert parallelism is forward-only)")
         if self.compute_dtype == torch.float32:
             raise NotImplementedError("the backward pass covers 16-bit layers (bf16 / fp16)")
+        if self.ws != 1:
+            return self._backward_ep(x, dout)
         lib = L.load()
         dev = x.device
         T, d = x.shape

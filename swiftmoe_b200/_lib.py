@@ -98,6 +98,11 @@ SIGNATURES = {
     "smoe_layer_bwd": (_i32, [C.POINTER(LayerBwdArgs), _vp]),
     "smoe_wgrad_gemm": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _i64, _vp, _vp]),
     "smoe_wgrad_gemm_rows": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _i64, _vp, _vp]),
+    "smoe_swiglu_bwd": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "smoe_linear_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "smoe_moe_bwd_dx": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "smoe_router_dwg_workspace_size": (_sz, [_i32, _i32]),
+    "smoe_router_dwg": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _sz, _vp]),
 }
 
 _lock = threading.Lock()

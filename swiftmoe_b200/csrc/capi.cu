@@ -1450,6 +1450,90 @@ int smoe_layer_bwd(const smoe_layer_bwd_args* a, smoe_stream_t stream) {
   return smoe_wgrad_gemm_rows(dr, d, g, F, dt, offsets, E, d, F, S, a->dw2, stream);
 }
 
+// ---- the layer backward in pieces, for expert parallelism: the routed rows' part runs on
+// the rank that owns their experts, the tokens' part on the tokens' own rank.
+
+int smoe_swiglu_bwd(void* ab, void* g, const float* row_w, const int32_t* n_rows, int64_t rows_cap, int F, int dtype,
+                    float* dw_row, smoe_stream_t stream) {
+  if (rows_cap < 0 || F < 1) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (F % 8 != 0) return SMOE_ERR_UNSUPPORTED;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!ab || !g) return SMOE_ERR_INVALID;
+  if (!aligned16(ab) || !aligned16(g)) return SMOE_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  return dtype == SMOE_BF16 ? swiglu_bwd_launch<__nv_bfloat16>(ab, g, row_w, n_rows, rows_cap, F, dw_row, st)
+                            : swiglu_bwd_launch<__half>(ab, g, row_w, n_rows, rows_cap, F, dw_row, st);
+}
+
+int smoe_linear_bwd(void* g, const void* xr, void* dr, const float* row_w, const int32_t* n_rows, int64_t rows_cap,
+                    int d, int dtype, float* dw_row, smoe_stream_t stream) {
+  if (rows_cap < 0 || d < 1) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (d % 8 != 0) return SMOE_ERR_UNSUPPORTED;
+  if (rows_cap == 0) return SMOE_OK;
+  if (!g || !xr || !dr || !row_w || !n_rows || !dw_row) return SMOE_ERR_INVALID;
+  if (!aligned16(g) || !aligned16(xr) || !aligned16(dr)) return SMOE_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  return dtype == SMOE_BF16 ? linear_bwd_launch<__nv_bfloat16>(g, xr, dr, row_w, n_rows, rows_cap, d, dw_row, st)
+                            : linear_bwd_launch<__half>(g, xr, dr, row_w, n_rows, rows_cap, d, dw_row, st);
+}
+
+int smoe_moe_bwd_dx(const void* dxr, const int32_t* slot_row, const int32_t* idx, const float* w, const float* dw_row,
+                    const void* gate_w, const void* dxs, int T, int k, int d, int dtype, void* dx,
+                    const int32_t* slot_row_full, float* dsel_row, smoe_stream_t stream) {
+  if (T < 0 || k < 1 || d < 1) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (T == 0) return SMOE_OK;
+  if (!dxr || !slot_row || !idx || !w || !dw_row || !gate_w || !dx) return SMOE_ERR_INVALID;
+  if (dsel_row && !slot_row_full) return SMOE_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool vec = d % 8 == 0 && aligned16(dx) && aligned16(gate_w) && aligned16(dxr) && (!dxs || aligned16(dxs));
+  const int64_t items = (int64_t)T * (vec ? d / 8 : d);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(items, 256), (int64_t)device_sms() * 32));
+#define SMOE_BWD_DX(TY, VV)                                                                                          \
+  moe_bwd_dx_kernel<TY, VV><<<grid, 256, 0, st>>>((const TY*)dxr, slot_row, idx, w, dw_row, (const TY*)gate_w,        \
+                                                  (const TY*)dxs, T, k, d, (TY*)dx, slot_row_full, dsel_row)
+  if (dtype == SMOE_BF16) {
+    if (vec) SMOE_BWD_DX(__nv_bfloat16, 8); else SMOE_BWD_DX(__nv_bfloat16, 1);
+  } else {
+    if (vec) SMOE_BWD_DX(__half, 8); else SMOE_BWD_DX(__half, 1);
+  }
+#undef SMOE_BWD_DX
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
+size_t smoe_router_dwg_workspace_size(int d, int E) {
+  if (d < 1 || E < 1) return 0;
+  return (size_t)kDwgSlices * E * d * sizeof(float);
+}
+
+int smoe_router_dwg(const void* x, const int32_t* row_token_full, const int32_t* offsets_full, const float* dsel_row,
+                    int d, int E, int dtype, float* dgate, void* workspace, size_t workspace_bytes,
+                    smoe_stream_t stream) {
+  if (d < 1 || E < 1) return SMOE_ERR_INVALID;
+  if (dtype != SMOE_BF16 && dtype != SMOE_F16) return SMOE_ERR_UNSUPPORTED;
+  if (!x || !row_token_full || !offsets_full || !dsel_row || !dgate) return SMOE_ERR_INVALID;
+  if (!workspace || workspace_bytes < smoe_router_dwg_workspace_size(d, E)) return SMOE_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t cols = cdiv(d, 256);
+  const int slices = (int)std::max<int64_t>(1, std::min<int64_t>(kDwgSlices, cdiv((int64_t)device_sms() * 8, cols * E)));
+  dim3 g2((unsigned)cols, (unsigned)E, (unsigned)slices);
+  float* part = static_cast<float*>(workspace);
+  if (dtype == SMOE_BF16)
+    router_dwg_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>((const __nv_bfloat16*)x, row_token_full, offsets_full, dsel_row,
+                                                         d, E, part);
+  else
+    router_dwg_kernel<__half><<<g2, 256, 0, st>>>((const __half*)x, row_token_full, offsets_full, dsel_row, d, E, part);
+  SMOE_CK(cudaGetLastError());
+  const int64_t n = (int64_t)E * d;
+  router_dwg_reduce_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)device_sms() * 8), 256, 0, st>>>(
+      part, slices, n, dgate);
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
 }  // extern "C"
 
 // Allocation-free dispatch plan (static device scratch); see noalloc_plan.cu.

@@ -40,6 +40,8 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
+
 
 @dataclass
 class DispatchState:
@@ -989,13 +991,13 @@ class ExpertParallelExchange:
         send_rows = self.k.permute_rows(x, plan["row_token"], plan["offsets"], plan["rows_cap"])
         counts = plan["counts"]
         recv_counts = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        self._a2a(recv_counts, counts)
         hc, hr = self._to_host(counts, recv_counts)
         send_splits = [int(v) for v in hc.reshape(ws, El).sum(1)]
         recv_splits = [int(v) for v in hr.reshape(ws, El).sum(1)]
         n_send, n_recv = sum(send_splits), sum(recv_splits)
         recv_rows = torch.empty((max(n_recv, 1), x.shape[1]), dtype=x.dtype, device=x.device)
-        dist.all_to_all_single(recv_rows[:n_recv], send_rows[:n_send], recv_splits, send_splits, group=self.group)
+        self._a2a(recv_rows[:n_recv], send_rows[:n_send], recv_splits, send_splits)
         rg = self.k.ep_regroup_plan(recv_counts.view(ws, El), capacity, n_recv)
         xe = self.k.permute_rows(recv_rows, rg["row_src"], rg["offsets"], rg["rows_cap"])
         st = DispatchState(plan, rg, send_splits, recv_splits, n_send, n_recv, T, k)
@@ -1007,17 +1009,123 @@ class ExpertParallelExchange:
         send_p = torch.zeros(n_send + 1, dtype=torch.float32, device=x.device)   # last: spare for skipped slots
         send_p.scatter_(0, torch.where(sr >= 0, sr, torch.full_like(sr, n_send)), flat)
         recv_p = torch.empty(max(n_recv, 1), dtype=torch.float32, device=x.device)
-        dist.all_to_all_single(recv_p[:n_recv], send_p[:n_send], recv_splits, send_splits, group=self.group)
+        self._a2a(recv_p[:n_recv], send_p[:n_send], recv_splits, send_splits)
         pe = self.k.gather_rows(recv_p.view(-1, 1), rg["row_src"], rg["rows_cap"])
         return xe, rg["offsets"], st, pe.view(-1)
+
+    def return_rows(self, y: torch.Tensor, st: DispatchState) -> torch.Tensor:
+        """Rows computed for the rows ``dispatch`` delivered (``y`` in its expert-major order,
+        any width and dtype) back to their source ranks: [n_send, width] in each source's
+        send layout (row ``st.plan["slot_row"][t*k + j]`` for slot j of token t), zero rows
+        for the slots the capacity cut dropped."""
+        back = self.k.gather_rows(y, st.regroup["recv_dst"], st.n_recv)
+        ret = torch.empty((max(st.n_send, 1), y.shape[1]), dtype=y.dtype, device=y.device)
+        self._a2a(ret[:st.n_send], back[:st.n_recv], st.send_splits, st.recv_splits)
+        return ret
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits=None, in_splits=None) -> None:
+        """all_to_all_single over the group; a local copy on a one-rank group."""
+        if self.world_size == 1:
+            if out.numel():
+                out.copy_(inp)
+            return
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
     def combine(self, y: torch.Tensor, st: DispatchState, w: torch.Tensor,
                 shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
         """Return expert outputs to their source ranks and reduce the k slots."""
-        back = self.k.gather_rows(y, st.regroup["recv_dst"], st.n_recv)
-        ret = torch.empty((max(st.n_send, 1), y.shape[1]), dtype=y.dtype, device=y.device)
-        dist.all_to_all_single(ret[:st.n_send], back[:st.n_recv], st.send_splits, st.recv_splits, group=self.group)
+        ret = self.return_rows(y, st)
         return self.k.combine(ret, st.plan["slot_row"], w, st.T, st.k, shared=shared, out=out)
+
+    def layer_backward(self, x: torch.Tensor, dout: torch.Tensor, gate: torch.Tensor,
+                       logit_bias: Optional[torch.Tensor], k: int, capacity: int, experts: dict,
+                       shared: Optional[dict] = None) -> dict:
+        """Gradients of the expert-parallel layer for the upstream gradient ``dout`` of this
+        rank's tokens ``x`` [T, d] (16-bit on the GPU).
+
+        The routed rows' part runs where their experts live, the tokens' part here, as the
+        one-GPU ``smoe_layer_bwd`` splits it: the routing is recomputed, the rows of x and
+        of dout travel to the experts' ranks (the forward's dispatch, capacity cut
+        included, with the gate weights beside the dout rows), the owner recomputes the
+        gate/up pre-activations, runs the SwiGLU (or linear) backward, the input-gradient
+        GEMM and the weight-gradient GEMMs over its local experts (rows padded to 64 per
+        expert for the K-grouped GEMM), and returns one input-gradient row and one gate-
+        weight gradient per slot; this rank then adds the slots, the router's softmax-over-
+        top-k backward and the shared expert.
+
+        ``experts``: ``{"kind": "swiglu", "w1", "w3" [E_l, F, d], "w2t" [E_l, F, d] (W2
+        transposed), "w13t" [E_l, d, 2F] ([W1; W3] transposed)}`` or ``{"kind": "linear",
+        "w": [E_l, d, d] (the B operand of the dout GEMM), "transposed": bool (weights used
+        as x @ W)}``; ``shared`` (optional): ``{"w1", "w3" [1, Fs, d], "w2t" [1, Fs, d],
+        "w13t" [1, d, 2Fs]}``.  Returns ``x``, ``gate`` [E, d] fp32, ``w13`` [E_l, 2F, d]
+        and ``w2`` [E_l, d, F] (or ``lin`` [E_l, d, d]) fp32, ``s13`` / ``s2`` for the shared
+        expert.  The gate's and the shared expert's gradients are this rank's contribution
+        (those weights are replicated: sum them over ranks, as data parallelism does); the
+        local experts' gradients are complete.  The routed dispatch is host-synchronised
+        (the counts become Python ints), as in the stage-by-stage API."""
+        kk = self.k
+        El, E = self.exp_per_rank, self.num_experts
+        T, d = x.shape
+        dev = x.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        idx, w = kk.router(x, gate, k, logit_bias)
+        # ---- the routed rows on their experts' rank
+        xe, oe, st = self.dispatch(x, idx, capacity)
+        de, _, _, we = self.dispatch(dout, idx, capacity, slot_payload=w)
+        n = int(oe[El])
+        r = torch.arange(max(n, 1), device=dev, dtype=torch.int32)[:n]
+        ids = torch.searchsorted(oe[1:].contiguous(), r, right=True).to(torch.int32)
+        pa = kk.dispatch_plan(ids.view(-1, 1).contiguous(), El, 0, 64)   # groups start on 64-row boundaries
+        S, offs = pa["rows_cap"], pa["offsets"]
+        xa = kk.permute_rows(xe, pa["row_token"], offs, S)              # padding rows are zeros
+        da = kk.permute_rows(de, pa["row_token"], offs, S)
+        used = int(offs[El])                      # rows of the padded layout (padding included)
+        rw = torch.zeros(max(S, 1), **f32)        # gate weight of each padded row (0 for padding)
+        if used:
+            rt = pa["row_token"][:used].long()    # in [0, n), or -1 for padding
+            rw[:used] = torch.where(rt >= 0, we.reshape(-1)[:n].float()[rt.clamp(min=0)], torch.zeros((), **f32))
+        dwr = torch.zeros(max(S, 1), **f32)
+        out = {}
+        if experts["kind"] == "swiglu":
+            F = experts["w1"].shape[1]
+            ab = torch.empty((max(S, 1), 2 * F), dtype=x.dtype, device=dev)
+            kk.grouped_gemm(xa, experts["w1"], offs, B3=experts["w3"], epilogue=L.SMOE_EPI_GATEUP, out=ab)
+            g = kk.grouped_gemm(da, experts["w2t"], offs)                   # dout_r W2
+            kk.swiglu_bwd(ab, g, rw, offs[El:], dwr)                        # [da | db], w h, <g, h>
+            dxa = kk.grouped_gemm(ab, experts["w13t"], offs)                # input gradient of the rows
+            out["w13"] = kk.wgrad_gemm_rows(ab, xa, offs, 2 * F, d)
+            out["w2"] = kk.wgrad_gemm_rows(da, g, offs, d, F)
+        else:
+            g = kk.grouped_gemm(da, experts["w"], offs)                     # dout_r Wl
+            kk.linear_bwd(g, xa, da, rw, offs[El:], dwr)                    # w g, w dout, <g, x>
+            dxa = g
+            out["lin"] = (kk.wgrad_gemm_rows(xa, da, offs, d, d) if experts["transposed"]
+                          else kk.wgrad_gemm_rows(da, xa, offs, d, d))
+        # back in dispatch's row order, then to the source ranks (zero rows for dropped slots)
+        sr = pa["slot_row"][:n]
+        dxe = kk.gather_rows(dxa, sr, n)
+        dwe = dwr[sr.long()].reshape(-1, 1).contiguous() if n else torch.zeros((1, 1), **f32)
+        ret_dx = self.return_rows(dxe, st)
+        ret_dw = self.return_rows(dwe, st).reshape(-1).contiguous()
+        # ---- the tokens' part, here
+        dxs = None
+        if shared is not None:
+            Fs = shared["w1"].shape[1]
+            soff = torch.tensor([0, T], dtype=torch.int32, device=dev)
+            abs_ = torch.empty((max(T, 1), 2 * Fs), dtype=x.dtype, device=dev)
+            kk.grouped_gemm(x, shared["w1"], soff, B3=shared["w3"], epilogue=L.SMOE_EPI_GATEUP, out=abs_)
+            gs = kk.grouped_gemm(dout, shared["w2t"], soff)
+            kk.swiglu_bwd(abs_, gs, None, None, None)
+            dxs = kk.grouped_gemm(abs_, shared["w13t"], soff)
+            out["s13"] = kk.wgrad_gemm_rows(abs_, x, soff, 2 * Fs, d)[0]
+            out["s2"] = kk.wgrad_gemm_rows(dout, gs, soff, d, Fs)[0]
+        pf = kk.dispatch_plan(idx, E, 0)                                  # every slot, for the gate gradient
+        dsel = torch.zeros(max(pf["rows_cap"], 1), **f32)
+        dx = torch.empty_like(x)
+        kk.moe_bwd_dx(ret_dx, st.plan["slot_row"], idx, w, ret_dw, gate, dxs, dx, pf["slot_row"], dsel)
+        out["gate"] = kk.router_dwg(x, pf["row_token"], pf["offsets"], dsel, E)
+        out["x"] = dx
+        return out
 
 
 class _NullCtx:

@@ -175,6 +175,57 @@ def wgrad_gemm_rows(A: torch.Tensor, B: torch.Tensor, k_offsets: torch.Tensor, M
     return out
 
 
+def swiglu_bwd(ab: torch.Tensor, g: torch.Tensor, row_w: Optional[torch.Tensor], n_rows: Optional[torch.Tensor],
+               dw_row: Optional[torch.Tensor]) -> None:
+    """SwiGLU backward of the routed rows, in place: ab [rows, 2F] = [a | b] -> [da | db],
+    g [rows, F] (dout_r W2) -> w_r * h, dw_row[r] = <g_r, h_r>; rows r < n_rows[0] (device
+    int32, None: all); row_w fp32 [rows] (None: 1)."""
+    _need_cuda(ab, g, row_w, n_rows, dw_row)
+    rows_cap, F = g.shape
+    L.check(L.load().smoe_swiglu_bwd(L.ptr(ab), L.ptr(g), L.ptr(row_w), L.ptr(n_rows), rows_cap, F,
+                                     L.dtype_code(g.dtype), L.ptr(dw_row), L.stream_handle(g.device)),
+            "smoe_swiglu_bwd")
+
+
+def linear_bwd(g: torch.Tensor, xr: torch.Tensor, dr: torch.Tensor, row_w: torch.Tensor, n_rows: torch.Tensor,
+               dw_row: torch.Tensor) -> None:
+    """Linear-expert backward of the routed rows, in place: dw_row[r] = <g_r, x_r>,
+    g -> w_r g, dr -> w_r dr, for rows r < n_rows[0]."""
+    _need_cuda(g, xr, dr, row_w, n_rows, dw_row)
+    rows_cap, d = g.shape
+    L.check(L.load().smoe_linear_bwd(L.ptr(g), L.ptr(xr), L.ptr(dr), L.ptr(row_w), L.ptr(n_rows), rows_cap, d,
+                                     L.dtype_code(g.dtype), L.ptr(dw_row), L.stream_handle(g.device)),
+            "smoe_linear_bwd")
+
+
+def moe_bwd_dx(dxr: torch.Tensor, slot_row: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, dw_row: torch.Tensor,
+               gate_w: torch.Tensor, dxs: Optional[torch.Tensor], dx: torch.Tensor,
+               slot_row_full: Optional[torch.Tensor] = None, dsel_row: Optional[torch.Tensor] = None) -> None:
+    """dx [T, d] from the slots' input-gradient rows dxr (at slot_row), the gate weights'
+    gradients dw_row (per dxr row), the router backward and the shared expert's dxs."""
+    _need_cuda(dxr, slot_row, idx, w, dw_row, gate_w, dxs, dx, slot_row_full, dsel_row)
+    T, k = idx.shape
+    d = dx.shape[1]
+    L.check(L.load().smoe_moe_bwd_dx(L.ptr(dxr), L.ptr(slot_row), L.ptr(idx), L.ptr(w), L.ptr(dw_row), L.ptr(gate_w),
+                                     L.ptr(dxs), T, k, d, L.dtype_code(dx.dtype), L.ptr(dx), L.ptr(slot_row_full),
+                                     L.ptr(dsel_row), L.stream_handle(dx.device)), "smoe_moe_bwd_dx")
+
+
+def router_dwg(x: torch.Tensor, row_token_full: torch.Tensor, offsets_full: torch.Tensor, dsel_row: torch.Tensor,
+               E: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gate gradient fp32 [E, d] from dsel per row of a plan over every slot."""
+    _need_cuda(x, row_token_full, offsets_full, dsel_row)
+    d = x.shape[1]
+    lib = L.load()
+    ws = torch.empty(max(int(lib.smoe_router_dwg_workspace_size(d, E)), 1), dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty((E, d), dtype=torch.float32, device=x.device)
+    L.check(lib.smoe_router_dwg(L.ptr(x), L.ptr(row_token_full), L.ptr(offsets_full), L.ptr(dsel_row), d, E,
+                                L.dtype_code(x.dtype), L.ptr(out), L.ptr(ws), ws.numel(), L.stream_handle(x.device)),
+            "smoe_router_dwg")
+    return out
+
+
 def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
     """[G, R, C] -> [G, C, R]."""
     _need_cuda(src)
@@ -198,7 +249,9 @@ def ep_regroup_plan(recv_counts: torch.Tensor, capacity: int, n_recv: int, pos_b
     rows_cap = n_recv if capacity <= 0 else min(n_recv, capacity * El)
     counts = torch.empty(El, dtype=torch.int32, device=dev)
     offsets = torch.empty(El + 1, dtype=torch.int32, device=dev)
-    row_src = torch.empty(max(rows_cap, 1), dtype=torch.int32, device=dev)
+    # the plan writes row_src for the kept rows only; the rest of rows_cap (an upper bound
+    # under a capacity) holds -1, "no row", for readers that take all rows_cap entries
+    row_src = torch.full((max(rows_cap, 1),), -1, dtype=torch.int32, device=dev)
     recv_dst = torch.empty(max(n_recv, 1), dtype=torch.int32, device=dev)
     wsb = _workspace(dev, lib.smoe_ep_regroup_workspace_size(ws_, El))
     L.check(lib.smoe_ep_regroup_plan(L.ptr(recv_counts), ws_, El, capacity, L.ptr(pos_base), n_recv, L.ptr(counts),

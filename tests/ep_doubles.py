@@ -14,7 +14,8 @@ def dispatch_plan(idx, num_experts, capacity=0, row_align=1):
     flat = idx_n.ravel()
     counts = np.bincount(flat[flat >= 0], minlength=E).astype(np.int32)   # -1: skipped slot
     kept = np.minimum(counts, capacity) if capacity > 0 else counts
-    offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
+    aligned = (kept + row_align - 1) // row_align * row_align     # padding rows carry token -1
+    offsets = np.concatenate([[0], np.cumsum(aligned)]).astype(np.int32)
     slot_row = -np.ones(T * k, np.int32)
     row_token = -np.ones(max(int(offsets[-1]), 1), np.int32)
     seen = np.zeros(E, np.int64)
@@ -58,7 +59,10 @@ def ep_regroup_plan(recv_counts, capacity, n_recv, pos_base=None):
     kept = kept_seg.sum(0)
     offsets = np.concatenate([[0], np.cumsum(kept)]).astype(np.int32)
     recv_dst = -np.ones(max(n_recv, 1), np.int32)
-    row_src = -np.ones(max(int(offsets[-1]), 1), np.int32)
+    # rows_cap as the CUDA wrapper sizes it (an upper bound under a capacity); the entries
+    # past the kept rows are -1
+    rows_cap = n_recv if capacity <= 0 else min(n_recv, capacity * El)
+    row_src = -np.ones(max(rows_cap, int(offsets[-1]), 1), np.int32)
     r = 0
     for s in range(ws):
         for le in range(El):
@@ -71,7 +75,7 @@ def ep_regroup_plan(recv_counts, capacity, n_recv, pos_base=None):
                 r += 1
     return dict(counts=torch.from_numpy(tot.astype(np.int32)), offsets=torch.from_numpy(offsets),
                 row_src=torch.from_numpy(row_src), recv_dst=torch.from_numpy(recv_dst),
-                rows_cap=int(max(offsets[-1], 1)))
+                rows_cap=int(max(rows_cap, 1)))
 
 
 def combine(y, slot_row, w, T, k, shared=None, out=None):
@@ -235,3 +239,116 @@ def store_rows(src, row_ptrs, n_rows):
 def copy_rows_count(dst, src, n_rows):
     n = int(n_rows.numpy().reshape(-1)[0])
     dst[:n] = src[:n]
+
+
+# ---- the layer backward's kernels (expert-parallel backward on gloo ranks)
+
+def router(x, gate_w, k, logit_bias=None, return_logits=False):
+    xn = x.numpy().astype(np.float32)
+    lg = xn @ gate_w.numpy().astype(np.float32).T
+    lb = lg + (logit_bias.numpy() if logit_bias is not None else 0)
+    T, E = lg.shape
+    idx = np.zeros((T, k), np.int32)
+    w = np.zeros((T, k), np.float32)
+    for t in range(T):
+        order = sorted(range(E), key=lambda e: (-lb[t, e], e))[:k]
+        v = lb[t, order]
+        ex = np.exp(v - v[0])
+        idx[t], w[t] = order, ex / ex.sum()
+    res = (torch.from_numpy(idx), torch.from_numpy(w))
+    return res + (torch.from_numpy(lg),) if return_logits else res
+
+
+def transpose_batched(src, out=None):
+    return src.transpose(1, 2).contiguous()
+
+
+def grouped_gemm(A, B, offsets, *, B3=None, epilogue=0, out_dtype=None, out=None, ends=None, row_ptrs=None):
+    An, Bn = A.numpy().astype(np.float64), B.numpy().astype(np.float64)
+    rows_cap, (G, N, _) = An.shape[0], Bn.shape
+    off = offsets.numpy()
+    width = 2 * N if epilogue == 3 else N
+    C = np.zeros((max(rows_cap, 1), width))
+    for g in range(G):
+        r0, r1 = min(max(int(off[g]), 0), rows_cap), min(max(int(off[g + 1]), 0), rows_cap)
+        if r1 <= r0:
+            continue
+        a = An[r0:r1] @ Bn[g].T
+        if epilogue == 0:
+            C[r0:r1] = a
+        else:
+            b = An[r0:r1] @ B3.numpy().astype(np.float64)[g].T
+            C[r0:r1] = np.concatenate([a, b], 1) if epilogue == 3 else a / (1 + np.exp(-a)) * b
+    res = torch.from_numpy(C.astype(np.float32))
+    if out is not None:
+        out[:res.shape[0]].copy_(res[:out.shape[0]])
+        return out
+    return res
+
+
+def swiglu_bwd(ab, g, row_w, n_rows, dw_row):
+    abn, gn = ab.numpy(), g.numpy()
+    rows = int(n_rows[0]) if n_rows is not None else gn.shape[0]
+    F = gn.shape[1]
+    a, b, gg = abn[:rows, :F].astype(np.float64), abn[:rows, F:].astype(np.float64), gn[:rows].astype(np.float64)
+    wr = row_w.numpy()[:rows, None].astype(np.float64) if row_w is not None else 1.0
+    sg = 1 / (1 + np.exp(-a))
+    si = a * sg
+    h = si * b
+    dh = wr * gg
+    if dw_row is not None:
+        dw_row.numpy()[:rows] = (gg * h).sum(1)
+    abn[:rows, :F] = dh * b * sg * (1 + a * (1 - sg))
+    abn[:rows, F:] = dh * si
+    gn[:rows] = wr * h
+
+
+def linear_bwd(g, xr, dr, row_w, n_rows, dw_row):
+    rows = int(n_rows[0])
+    gn, xn, dn = g.numpy(), xr.numpy(), dr.numpy()
+    wr = row_w.numpy()[:rows, None]
+    dw_row.numpy()[:rows] = (gn[:rows].astype(np.float64) * xn[:rows]).sum(1)
+    gn[:rows] = wr * gn[:rows]
+    dn[:rows] = wr * dn[:rows]
+
+
+def wgrad_gemm_rows(A, B, k_offsets, M=None, N=None, out=None):
+    An, Bn = A.numpy().astype(np.float64), B.numpy().astype(np.float64)
+    M = An.shape[1] if M is None else M
+    N = Bn.shape[1] if N is None else N
+    off = k_offsets.numpy()
+    G = off.shape[0] - 1
+    C = np.zeros((G, M, N))
+    for g in range(G):
+        k0, k1 = int(off[g]), int(off[g + 1])
+        C[g] = An[k0:k1, :M].T @ Bn[k0:k1, :N]
+    return torch.from_numpy(C.astype(np.float32))
+
+
+def moe_bwd_dx(dxr, slot_row, idx, w, dw_row, gate_w, dxs, dx, slot_row_full=None, dsel_row=None):
+    T, k = idx.shape
+    sr = slot_row.numpy().reshape(T, k)
+    idn, wn = idx.numpy(), w.numpy().astype(np.float64)
+    dxrn, dwn, gn = dxr.numpy().astype(np.float64), dw_row.numpy().astype(np.float64), gate_w.numpy()
+    dwj = np.where(sr >= 0, dwn[np.maximum(sr, 0)], 0.0)
+    ds = wn * (dwj - (wn * dwj).sum(1, keepdims=True))
+    acc = np.zeros((T, dx.shape[1]))
+    for j in range(k):
+        m = sr[:, j] >= 0
+        acc[m] += dxrn[sr[m, j]]
+        acc += ds[:, j, None] * gn[idn[:, j]]
+    if dxs is not None:
+        acc += dxs.numpy()
+    dx.copy_(torch.from_numpy(acc.astype(np.float32)))
+    if dsel_row is not None:
+        srf = slot_row_full.numpy().reshape(T, k)
+        dsel_row.numpy()[srf[srf >= 0]] = ds[srf >= 0]
+
+
+def router_dwg(x, row_token_full, offsets_full, dsel_row, E, out=None):
+    xn, rt, off, ds = x.numpy().astype(np.float64), row_token_full.numpy(), offsets_full.numpy(), dsel_row.numpy()
+    G = np.zeros((E, xn.shape[1]))
+    for e in range(E):
+        for r in range(int(off[e]), int(off[e + 1])):
+            G[e] += ds[r] * xn[rt[r]]
+    return torch.from_numpy(G.astype(np.float32))
