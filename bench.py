@@ -516,11 +516,12 @@ def backward_timing(model, T: int, R: Ranks, pk, steps: int, warmup: int):
     x = torch.randn((T, d), device=R.dev, dtype=torch.bfloat16, generator=torch.Generator(R.dev).manual_seed(300))
     dout = torch.randn((T, d), device=R.dev, dtype=torch.bfloat16, generator=torch.Generator(R.dev).manual_seed(301))
     ms = time_steps(lambda i=None: model._backward_fused(x, dout), steps, warmup, R)
-    S = T * model.top_k
+    S = T * model.top_k      # routed rows per rank (under expert parallelism: on average)
     flops = 2.0 * S * d * 2 * F * 3 + 2.0 * S * d * F * 2
     return {"ms_per_backward": ms, "tokens_per_gpu": T, "gemm_tflops": flops / (ms / 1e3) / 1e12,
             "frac_of_burst_peak": flops / (ms / 1e3) / 1e12 / pk["burst"], "gemm_flops": flops,
-            "what": "gradients of x, gate, w1, w3, w2 (bf16 layer, fp32 weight gradients), one GPU"}
+            "what": "gradients of x, gate, w1, w3, w2 (bf16 layer, fp32 weight gradients); one GPU: "
+                    "smoe_layer_bwd, N > 1: the expert-parallel backward (max over ranks)"}
 
 
 def extra_workloads(R: Ranks, pk, steps: int, warmup: int, decode_model=None, sample: int = 32):
@@ -605,11 +606,24 @@ def _main():
     import torch
     import torch.distributed as dist
     if args.mode == "backward":
-        torch.cuda.set_device(0)
-        R = Ranks(1, 0, 0, torch.device("cuda", 0))
+        # one GPU: smoe_layer_bwd; under torchrun: the expert-parallel backward on every rank
+        bws = int(os.environ.get("WORLD_SIZE", "1"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        if bws > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        R = Ranks(bws, int(os.environ.get("RANK", "0")), local, dev)
         model, _ = make_layer(wl, R, 1, profiling=False)
         res = backward_timing(model, args.tokens, R, peaks(), args.steps, args.warmup)
-        print(json.dumps({"mode": "backward", "workload": WORKLOAD, **res}), flush=True)
+        if bws > 1:
+            model.comm.close()
+        if R.rank == 0:
+            print(json.dumps({"mode": "backward", "workload": WORKLOAD, "n_gpus": bws, **res}), flush=True)
+        if bws > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
         return
 
     ws = int(os.environ.get("WORLD_SIZE", "1"))
