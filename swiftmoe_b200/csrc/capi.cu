@@ -261,7 +261,9 @@ int launch_gemv_t(const void* A, const void* B, const void* B3, void* C, const u
                   const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
                   cudaStream_t st, const int32_t* a_index, int a_rows) {
   // one warp (two for rows of 8192 or more elements) per (group with rows, column); at
-  // most min(G, rows_cap) groups have rows
+  // most min(G, rows_cap) groups have rows.  Measured on the Mixtral decode shapes: two
+  // warps take the 14336-element down rows in 54 us (one: 60, four: 57); the 4096-element
+  // gate/up rows stay on one warp (two: 97 us against 84).
   const int64_t cols = std::min<int64_t>(G, std::max<int64_t>(rows_cap, 1)) * N;
   if (K >= 8192) {
     constexpr int CPB = gemv::THREADS / 32 / 2;
