@@ -8,7 +8,9 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "dispatch.cuh"
@@ -214,6 +216,61 @@ int raster_band(int epi) {
   return (epi == SMOE_EPI_SWIGLU || epi == SMOE_EPI_GATEUP) ? 32 : tc::GM_DEFAULT;
 }
 
+// Split-K scratch of the tensor-core GEMM (its kernel decides on the device whether to
+// split): one per (device, stream), so launches on different streams never share one --
+// device_sms() fp32 [BM, BN] slots and as many arrival counters, zero between launches.
+// Allocated at the first launch on the stream, in relaxed capture mode so that a stream
+// being captured into a CUDA graph may allocate it too; the counters are zeroed on a
+// private stream that is never captured.  SMOE_SPLITK=0 turns the split off.
+struct SplitScratch {
+  float* ws = nullptr;
+  int* cnt = nullptr;
+  int units = 0;
+};
+std::mutex g_split_mu;
+std::map<std::pair<int, cudaStream_t>, SplitScratch> g_split;
+
+SplitScratch split_scratch(cudaStream_t st) {
+  static const bool off = getenv("SMOE_SPLITK") != nullptr && strcmp(getenv("SMOE_SPLITK"), "0") == 0;
+  int dev = 0;
+  if (off || cudaGetDevice(&dev) != cudaSuccess) return {};
+  std::lock_guard<std::mutex> lk(g_split_mu);
+  const auto key = std::make_pair(dev, st);
+  const auto it = g_split.find(key);
+  if (it != g_split.end()) return it->second;
+  SplitScratch s;
+  s.units = device_sms();
+  const size_t ws_bytes = (size_t)s.units * tc::BM * tc::BN * sizeof(float);
+  const size_t cnt_bytes = (size_t)s.units * sizeof(int);
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  void* p = nullptr;
+  cudaStream_t init = nullptr;
+  bool ok = cudaMalloc(&p, ws_bytes + cnt_bytes) == cudaSuccess;
+  ok = ok && cudaStreamCreateWithFlags(&init, cudaStreamNonBlocking) == cudaSuccess;
+  ok = ok && cudaMemsetAsync(static_cast<char*>(p) + ws_bytes, 0, cnt_bytes, init) == cudaSuccess;
+  ok = ok && cudaStreamSynchronize(init) == cudaSuccess;
+  if (init) cudaStreamDestroy(init);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (!ok) {  // no scratch: this stream's launches run unsplit
+    if (p) cudaFree(p);
+    cudaGetLastError();
+    s = SplitScratch{};
+  } else {
+    s.ws = static_cast<float*>(p);
+    s.cnt = reinterpret_cast<int*>(static_cast<char*>(p) + ws_bytes);
+  }
+  g_split[key] = s;
+  return s;
+}
+
+// After a device wait gave up, a split launch may have left tile counters part-counted.
+void reset_split_counters(int dev) {
+  std::lock_guard<std::mutex> lk(g_split_mu);
+  for (auto& kv : g_split)
+    if (kv.first.first == dev && kv.second.cnt) cudaMemset(kv.second.cnt, 0, (size_t)kv.second.units * sizeof(int));
+}
+
 template <int EPI, typename OutT>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
               const uint64_t* row_ptrs, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
@@ -222,8 +279,9 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
   auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
   constexpr int smem = EPI == tc::EPI_ROWS ? tc::SMEM_BYTES_ROWS : tc::SMEM_BYTES;
   SMOE_CK(ensure_smem(kern, smem, &done));
+  const SplitScratch sc = split_scratch(st);
   SMOE_CK(launch_k(kern, device_sms(), tc::THREADS, smem, st, ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
-                                                         K, (int)rows_cap, raster_band(EPI), idesc));
+                                                         K, (int)rows_cap, raster_band(EPI), idesc, sc.ws, sc.cnt, sc.units));
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
@@ -555,6 +613,12 @@ int smoe_read_device_error(int* flag, smoe_stream_t stream) {
   SMOE_CK(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
   const int zero = 0;
   SMOE_CK(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  if (v != 0) {
+    int dev = 0;
+    SMOE_CK(cudaDeviceSynchronize());
+    SMOE_CK(cudaGetDevice(&dev));
+    reset_split_counters(dev);
+  }
   *flag = v;
   return SMOE_OK;
 }

@@ -245,13 +245,111 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool r
   }
 }
 
+// ---------------------------------------------------------------------------- split-K
+// A launch with few tiles -- decode-sized groups in a large row buffer: the down
+// projection of one expert is 16 tiles of 256 columns for 148 SMs -- leaves most SMs idle
+// while a few stream the weights.  The kernel decides on the device, from the tile count
+// of the group table it builds, whether to cut every tile's K range into ksplit slices
+// (at least SPLIT_MIN_KB k-blocks each), one work unit per slice: only when at least
+// twice as many scratch units as tiles exist, so each unit still runs on its own CTA.
+// A unit stores its fp32 partial tile (valid rows and columns only) into its slot of the
+// launch's scratch; the last unit of a tile to finish -- found with the tile's arrival
+// counter, which it resets to zero for the next launch -- sums the partials in slice
+// order (a fixed order: the result does not depend on which unit finishes last) and
+// applies the epilogue.
+constexpr int SPLIT_MIN_KB = 4, MAX_SPLIT = 16;
+
+__device__ __forceinline__ int split_count(int tiles, int KB, int units) {
+  if (tiles <= 0 || 2 * tiles > units) return 1;
+  return max(1, min(min(units / tiles, KB / SPLIT_MIN_KB), MAX_SPLIT));
+}
+
+// The four epilogue warps (128 threads) meet on hardware barrier 1.
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// This warp's 32 accumulator rows (one per thread) into the unit's fp32 slot, laid out
+// piece-major: the 4-column piece p (columns 4p .. 4p+3) of row r at float (p * BM + r) * 4,
+// so the 32 lanes of a warp store 512 contiguous bytes.  Only accumulator columns below
+// `valid` (per [gate | up] half for the paired epilogues) are stored.  tcgen05.ld is
+// warp-wide, so every lane loads and row_ok masks the stores.
+template <bool kPair>
+__device__ __forceinline__ void split_store_partial(uint32_t tbase, float* slot, int r, bool row_ok, int valid) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int cc = kPair ? (c * 32) % 128 : c * 32;
+    if (cc >= valid) continue;  // warp-uniform
+    uint32_t v[32];
+    tmem_ld32(tbase + c * 32, v);
+    tmem_ld_wait();
+    if (row_ok)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4*>(slot + ((int64_t)(c * 8 + j) * BM + r) * 4) =
+            make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+template <typename OutT> __device__ __forceinline__ void store4(OutT* p, float a, float b, float c, float d) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack2<OutT>(a, b), pack2<OutT>(c, d));
+}
+template <> __device__ __forceinline__ void store4<float>(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+
+__device__ __forceinline__ void add4(float4& s, const float* p) {
+  const float4 x = __ldcg(reinterpret_cast<const float4*>(p));
+  s.x += x.x;
+  s.y += x.y;
+  s.z += x.z;
+  s.w += x.w;
+}
+
+// The last unit of a tile: partial sums of the ks_n slots starting at tile_ws, in slot
+// order, then the epilogue; et = this thread's index among the 128 epilogue threads.
+// Consecutive threads take consecutive rows of one piece, so the slot reads coalesce.
+template <int EPI, typename OutT>
+__device__ __forceinline__ void split_fixup(const float* tile_ws, int ks_n, const TileCoord& t, OutT* C, int64_t ldc,
+                                            const uint64_t* row_ptrs, int N, int et) {
+  constexpr bool kPair = EpiTraits<EPI>::kPair;
+  const int col0 = kPair ? t.nb * 128 : t.nb * BN;
+  // output pieces of the tile that lie below N (N % 8 == 0: a piece is all in or all out)
+  const int np = min((kPair ? 128 : BN) / 4, (N - col0) / 4);
+  const int rows = t.rows_valid;
+  for (int i = et; i < np * rows; i += 128) {
+    const int p = i / rows, row = i - p * rows, c = 4 * p;
+    bool ok = true;
+    OutT* dst = out_row(C, ldc, row_ptrs, t.row0 + row, ok);
+    if (!ok) continue;
+    const float* pa = tile_ws + ((int64_t)p * BM + row) * 4;
+    const float* pb = tile_ws + ((int64_t)(p + 32) * BM + row) * 4;  // [gate | up]: the up piece
+    float4 a = __ldcg(reinterpret_cast<const float4*>(pa));
+    float4 b = kPair ? __ldcg(reinterpret_cast<const float4*>(pb)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 1; q < ks_n; ++q) {
+      add4(a, pa + (int64_t)q * BM * BN);
+      if (kPair) add4(b, pb + (int64_t)q * BM * BN);
+    }
+    if constexpr (EPI == SMOE_EPI_SWIGLU) {
+      store4<OutT>(dst + col0 + c, a.x / (1.0f + __expf(-a.x)) * b.x, a.y / (1.0f + __expf(-a.y)) * b.y,
+                   a.z / (1.0f + __expf(-a.z)) * b.z, a.w / (1.0f + __expf(-a.w)) * b.w);
+    } else if constexpr (EPI == EPI_GATEUP) {
+      store4<OutT>(dst + col0 + c, a.x, a.y, a.z, a.w);
+      store4<OutT>(dst + N + col0 + c, b.x, b.y, b.z, b.w);
+    } else {
+      store4<OutT>(dst + col0 + c, a.x, a.y, a.z, a.w);
+    }
+  }
+}
+
 // EPI: SMOE_EPI_STORE or SMOE_EPI_SWIGLU.  OutT: float, __nv_bfloat16 or __half.
+// split_ws / split_cnt: split-K scratch of split_units fp32 [BM, BN] slots and as many
+// counters (all zero between launches), or null for no split.
 template <int EPI, typename OutT>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                         const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
-                        int K, int rows_cap, int gm, uint32_t idesc) {
+                        int K, int rows_cap, int gm, uint32_t idesc, float* __restrict__ split_ws,
+                        int* __restrict__ split_cnt, int split_units) {
   pdl_wait();
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -261,6 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);  // set when a wait gives up
+  volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem + 2);   // split-K: 1 last unit, -1 abort
   int* s_beg = reinterpret_cast<int*>(s_tmem + 4);
   int* s_fin = s_beg + (MAX_GROUPS + 1);
   int* s_ts = s_fin + (MAX_GROUPS + 1);
@@ -304,7 +403,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
-  const int total = s_ts[G];
+  const int tiles = s_ts[G];
+  const int ks_n = split_ws != nullptr && split_cnt != nullptr ? split_count(tiles, KB, min(split_units, (int)gridDim.x)) : 1;
+  const int total = tiles * ks_n;  // work units: (tile, K slice), slices of a tile adjacent
 
   if (warp == 0) {
     if (lane == 0) {
@@ -314,9 +415,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
-        const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
+        const int tile = L / ks_n, ks = L - tile * ks_n;
+        const TileCoord t = decode_tile_t<BM>(tile, s_ts, s_beg, s_fin, G, NB, gm);
         const int n0 = kPair ? t.nb * 128 : t.nb * BN;
-        for (int kb = 0; kb < KB; ++kb) {
+        const int kb_lo = ks * KB / ks_n, kb_hi = (ks + 1) * KB / ks_n;
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
@@ -345,17 +448,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
+        const int ks = L % ks_n;
+        const int kb_lo = ks * KB / ks_n, kb_hi = (ks + 1) * KB / ks_n;
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, s_abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, s_abort)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
           const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -374,12 +479,45 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int L = blockIdx.x; L < total; L += gridDim.x) {
-      const TileCoord t = decode_tile_t<BM>(L, s_ts, s_beg, s_fin, G, NB, gm);
-      if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
-      tc_fence_after();
+      const int tile = L / ks_n;
+      const TileCoord t = decode_tile_t<BM>(tile, s_ts, s_beg, s_fin, G, NB, gm);
       bool row_ok = r < t.rows_valid;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = kPair ? t.nb * 128 : t.nb * BN;
+      if (ks_n > 1) {
+        // every epilogue warp reaches both barriers of every unit, whether its wait
+        // succeeded or not, and leaves the loop on the decision published between them
+        if (mbar_wait(tfull_bar(acc), acc_phase, s_abort)) {
+          tc_fence_after();
+          split_store_partial<kPair>(tbase, split_ws + (int64_t)L * BM * BN, r, row_ok, N - col0);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar(acc));
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+        __threadfence();
+        epi_bar_sync();
+        if (threadIdx.x == 64) {
+          int last = -1;
+          if (!*s_abort) {
+            last = atomicAdd(split_cnt + tile, 1) == ks_n - 1 ? 1 : 0;
+            if (last) split_cnt[tile] = 0;
+          }
+          *s_last = last;
+        }
+        epi_bar_sync();
+        const int last = *s_last;
+        if (last < 0) break;
+        if (last) {
+          __threadfence();
+          split_fixup<EPI, OutT>(split_ws + (int64_t)tile * ks_n * BM * BN, ks_n, t, C, ldc, row_ptrs, N,
+                                 (int)threadIdx.x - 64);
+        }
+        continue;
+      }
+      if (!mbar_wait(tfull_bar(acc), acc_phase, s_abort)) break;
+      tc_fence_after();
       if constexpr (EPI == EPI_ROWS) {
         const uint64_t addr = row_ok ? row_ptrs[t.row0 + r] : 0;
         epilogue_rows<OutT>(tbase, addr, col0, N, s_stage + q * ROWS_STAGE_BYTES, lane);

@@ -223,3 +223,82 @@ def test_decode_gemv_row_addresses(K, K_, N):
     assert torch.equal(got[3], y[0].cpu())
     assert (got[:3] == 7.0).all()
     assert K.read_device_error("cuda") == 0
+
+
+# Launches with few tiles (at most half as many as SMs) and long K: the kernel cuts each
+# tile's K range into slices on the device and the last slice of a tile to finish sums
+# the fp32 partials in slice order.  Ragged N (partly valid tiles), paired [gate | up]
+# tiles, fp32 output and output row addresses all go through that path.
+SPLIT = [
+    ([5, 0, 9], 14336, 4096, 0),      # the Mixtral down projection of a few rows: 32 tiles
+    ([7], 8192, 1024, 0),             # 4 tiles, 16 slices
+    ([9, 3], 4096, 264, 0),           # N % 256 != 0: the second tile of a group is 8 columns
+    ([1, 0, 6], 4096, 2048, 1),       # SwiGLU, 16 paired tiles per group
+    ([130], 2048, 200, 1),            # SwiGLU, 2 m-tiles, N % 128 != 0
+    ([3, 40], 2048, 512, 3),          # gate and up side by side
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sizes,K_,N,epi", SPLIT)
+def test_split_k_few_tiles(K, dtype, sizes, K_, N, epi):
+    A, B, B3, offs, rows = make_groups(sizes, K_, N, dtype, seed=K_ + N + epi, std=0.02)
+    Ad, Bd, B3d, od = A.cuda(), B.cuda(), B3.cuda(), offs.cuda()
+
+    def run():
+        if epi == 1:
+            return K.grouped_gemm(Ad, Bd, od, B3=B3d, epilogue=1)
+        if epi == 3:                                   # [rows, 2N]: gate | up
+            ab = torch.empty((rows, 2 * N), dtype=dtype, device="cuda")
+            return K.grouped_gemm(Ad, Bd, od, B3=B3d, epilogue=3, out=ab)
+        return K.grouped_gemm(Ad, Bd, od)
+
+    out = run()
+    if epi == 1:
+        ref = ref_swiglu(A, B, B3, offs)[:rows]
+    elif epi == 3:
+        ref = torch.cat([ref_store(A, B, offs), ref_store(A, B3, offs)], dim=1)[:rows]
+    else:
+        ref = ref_store(A, B, offs)[:rows]
+    assert elementwise_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2
+    assert torch.equal(out, run())                     # slices summed in a fixed order
+    if epi == 0:
+        f32 = K.grouped_gemm(Ad, Bd, od, out_dtype=torch.float32)[:rows].cpu().numpy()
+        assert max_abs_err(f32, ref.numpy()) <= 1e-5 * np.sqrt(K_) * max(1.0, float(ref.abs().max()))
+    assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_split_k_row_addresses(K, dtype):
+    """Few tiles with output row addresses: rows land at their addresses (a null
+    address skips its row), equal to the rows of the plain call."""
+    sizes, K_, N = [4, 0, 3], 14336, 512
+    A, B, _, offs, rows = make_groups(sizes, K_, N, dtype, seed=21, std=0.02)
+    Ad, Bd, od = A.cuda(), B.cuda(), offs.cuda()
+    y = K.grouped_gemm(Ad, Bd, od).cpu()
+    buf = torch.full((rows + 2, N), 7.0, dtype=dtype, device="cuda")
+    rb = N * buf.element_size()
+    dst = [rows + 1 - r if r != 2 else -1 for r in range(rows)]    # reversed, row 2 skipped
+    ptrs = torch.tensor([buf.data_ptr() + d * rb if d >= 0 else 0 for d in dst], dtype=torch.int64)
+    assert K.grouped_gemm(Ad, Bd, od, row_ptrs=ptrs.cuda()) is None
+    got = buf.cpu()
+    for r, d in enumerate(dst):
+        if d >= 0:
+            assert torch.equal(got[d], y[r]), r
+    written = {d for d in dst if d >= 0}
+    for i in range(rows + 2):
+        if i not in written:
+            assert (got[i] == 7.0).all(), i
+    assert K.read_device_error("cuda") == 0
+
+
+def test_split_k_interleaved_shapes(K):
+    """Split launches of different shapes back to back on one stream: every tile's
+    arrival counter is reset by its last slice, so each launch starts from zero."""
+    cases = [([3], 14336, 1024), ([2, 2], 4096, 4096), ([5], 14336, 1024)]
+    for i, (sizes, K_, N) in enumerate(cases * 2):
+        A, B, _, offs, rows = make_groups(sizes, K_, N, torch.bfloat16, seed=i, std=0.02)
+        out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
+        ref = ref_store(A, B, offs)[:rows]
+        assert elementwise_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2, i
+    assert K.read_device_error("cuda") == 0
