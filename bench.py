@@ -528,8 +528,8 @@ def extra_workloads(R: Ranks, pk, steps: int, warmup: int, decode_model=None, sa
     """The other layer shapes of the benchmark set, a few seconds each: the fp32 layer
     (one GPU), the capacity-limited and fine-grained expert-parallel layers (every N),
     and the decode sweep of the Mixtral layer (1 and 8 GPUs).  Throughput, expert-FLOP
-    fraction of the burst bf16 peak (fp32: of the FFMA peak at the sampled clock is not
-    claimed), exposed exchange time and a sampled parity check each."""
+    fraction of the burst bf16 peak (not claimed for fp32, whose GEMMs run three tf32
+    products per fp32 product), exposed exchange time and a sampled parity check each."""
     import torch
     res = {}
     names = ["ep-capacity", "fine-grained"] + (["cpu-runnable-fp32"] if R.ws == 1 else [])
@@ -689,7 +689,7 @@ def _main():
         gemm1_ms = stage_ms["Expert_GEMM1"]
         flops = 2.0 * S_rows * D_MODEL * 2 * D_FF
         kname = "grouped SwiGLU gate/up GEMM (tcgen05)" if cdtype != torch.float32 else \
-            "grouped SwiGLU gate/up GEMM (fp32 FFMA)"
+            "grouped SwiGLU gate/up GEMM (fp32 as split tf32 operands on tcgen05)"
     else:
         gemm1_ms = stage_ms["Expert_Compute"]
         flops = 6.0 * S_rows * D_MODEL * D_FF

@@ -149,7 +149,9 @@ SMOE_API int smoe_combine(const void* y, int dtype, const int32_t* slot_row, con
  * bf16 / fp16 run on tcgen05 tensor cores (TMEM accumulators, TMA-fed shared memory,
  * requires K % 8 == 0 and N % 8 == 0), except batches of at most 2 rows, which stream the
  * weights of the groups that have rows on the SIMT pipes (one warp per output column);
- * fp32 runs on FFMA (SIMT) for full fp32 accuracy.
+ * fp32 keeps fp32 accuracy: on the tf32 tensor cores with split operands (3xTF32: each
+ * value = its tf32 rounding + the remainder, three tf32 products summed in fp32) when
+ * K % 4 == 0 and N % 8 == 0, else on FFMA (SIMT).
  * C may be fp32 for the bf16/fp16 STORE epilogue when out_dtype == SMOE_F32.
  * Replaces: the per-expert loop of torch.mm at models/ultimate_moe.py:237-250 and
  * nn.Linear experts at models/baseline_moe.py:151-162.                               */

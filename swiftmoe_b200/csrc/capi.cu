@@ -140,12 +140,12 @@ EncodeTiledFn encode_fn() {
 }
 
 // 2-D map over a row-major [rows, K] 16-bit matrix; box = 64 (K) x 128 rows, 128 B swizzle.
-bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t rows, int64_t K) {
+bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t rows, int64_t K, int es = 2) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint64_t strides[1] = {(cuuint64_t)K * es};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 128};  // one 128-byte swizzle row of K
   cuuint32_t estr[2] = {1, 1};
   return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -182,13 +182,15 @@ bool make_map_2d_box(CUtensorMap* m, const void* base, CUtensorMapDataType dt, i
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 3-D map over [G, N, K] weights; box = 64 (K) x 128 (N) x 1 group.
-bool make_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t G, int64_t N, int64_t K) {
+// 3-D map over [G, N, K] weights; box = one 128-byte row of K (64 16-bit or 32 fp32
+// elements) x 128 (N) x 1 group.
+bool make_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int64_t G, int64_t N, int64_t K,
+                 int es = 2) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, (cuuint64_t)G};
-  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)K * es, (cuuint64_t)N * K * es};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -271,17 +273,54 @@ void reset_split_counters(int dev) {
     if (kv.first.first == dev && kv.second.cnt) cudaMemset(kv.second.cnt, 0, (size_t)kv.second.units * sizeof(int));
 }
 
-template <int EPI, typename OutT>
+// Scratch of the fp32 GEMMs on tf32 tensor cores (the [hi | lo | hi] rows of A and
+// [lo | hi | hi] rows of the weights), one per (device, stream), grown to the largest
+// request.  A stream being captured into a CUDA graph never allocates or grows it: that
+// call runs on the FFMA kernel instead.  SMOE_FP32_GEMM=simt keeps every fp32 GEMM on
+// the FFMA kernel.
+struct Tf32Scratch {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_tf32_mu;
+std::map<std::pair<int, cudaStream_t>, Tf32Scratch> g_tf32;
+
+void* tf32_scratch(cudaStream_t st, size_t bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(g_tf32_mu);
+  Tf32Scratch& s = g_tf32[std::make_pair(dev, st)];
+  if (s.bytes >= bytes) return s.p;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  if (s.p) {
+    cudaFree(s.p);  // waits for the device: no launch still reads the old buffer
+    s = Tf32Scratch{};
+  }
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  s.p = p;
+  s.bytes = bytes;
+  return p;
+}
+
+// forced: a split-K scratch of the caller's with at least min_split slices per tile;
+// otherwise the stream's own (the kernel then splits only launches with few tiles).
+template <int EPI, typename OutT, int ES = 2>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb3, void* C, int64_t ldc,
               const uint64_t* row_ptrs, const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, uint32_t idesc,
-              cudaStream_t st) {
+              cudaStream_t st, const SplitScratch* forced = nullptr, int min_split = 1) {
   static SmemGrant done;
-  auto kern = tc::grouped_gemm_kernel<EPI, OutT>;
+  auto kern = tc::grouped_gemm_kernel<EPI, OutT, ES>;
   constexpr int smem = EPI == tc::EPI_ROWS ? tc::SMEM_BYTES_ROWS : tc::SMEM_BYTES;
   SMOE_CK(ensure_smem(kern, smem, &done));
-  const SplitScratch sc = split_scratch(st);
+  const SplitScratch sc = forced ? *forced : split_scratch(st);
   SMOE_CK(launch_k(kern, device_sms(), tc::THREADS, smem, st, ma, mb, mb3, reinterpret_cast<OutT*>(C), ldc, row_ptrs, offsets, ends, G, N,
-                                                         K, (int)rows_cap, raster_band(EPI), idesc, sc.ws, sc.cnt, sc.units));
+                                                         K, (int)rows_cap, raster_band(EPI), idesc, sc.ws, sc.cnt, sc.units,
+                                                         forced ? min_split : 1));
   SMOE_CK(cudaGetLastError());
   return SMOE_OK;
 }
@@ -382,6 +421,70 @@ bool use_pair_kernel(int64_t rows_cap, int G) {
   return forced != nullptr && strcmp(forced, "2sm") == 0;
 }
 
+// The fp32 grouped GEMM on tf32 tensor cores (3xTF32, see tc::tf32_split3_kernel):
+// SMOE_ERR_WORKSPACE when no scratch could be had (the caller then uses the FFMA kernel).
+int tf32x3_gemm(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs, int epi,
+                const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, cudaStream_t st) {
+  const int64_t K3 = 3 * (int64_t)K;
+  const size_t a_el = (size_t)rows_cap * K3, b_el = (size_t)G * N * K3;
+  // Accumulation chains of at most kTf32ChainKb k-blocks (48 x 32 tf32 elements of the
+  // tripled K): the error of the tensor cores' fp32 accumulation grows with the chain --
+  // measured on unit-scale outputs, 2e-6 at 4-6 k-blocks, 5e-6 at 12, 1.0e-5 at 24,
+  // 1.7e-5 at 48, 2.9e-5 at 84, 8.6e-5 at 336 -- against the fp32 bar of 1e-5 x the
+  // output scale (~4.4e-5 here), so longer K is cut into split-K slices that the last
+  // slice sums in fp32, rounding to nearest.
+  constexpr int64_t kTf32ChainKb = 48;
+  const int min_split = (int)cdiv(cdiv(K3, 32), kTf32ChainKb);
+  const int64_t nb = epi == SMOE_EPI_SWIGLU ? cdiv(N, 128) : cdiv(N, tc::BN);
+  const int64_t tiles_max = min_split > 1 ? (cdiv(rows_cap, tc::BM) + G) * nb : 0;
+  const size_t slot_el = (size_t)tiles_max * min_split * tc::BM * tc::BN;
+  if (tiles_max * min_split > INT32_MAX) return SMOE_ERR_WORKSPACE;
+  // one counter per slot: the kernel splits only while tiles x slices fit the slots, so
+  // every tile index of a split launch has a counter, overlapping row ranges included
+  const size_t cnt_bytes = (size_t)tiles_max * min_split * sizeof(int);
+  const size_t bytes = (a_el + b_el * (epi == SMOE_EPI_SWIGLU ? 2 : 1) + slot_el) * sizeof(float) + cnt_bytes;
+  float* s = static_cast<float*>(tf32_scratch(st, bytes));
+  if (!s) return SMOE_ERR_WORKSPACE;
+  float* a3 = s;
+  float* b3 = a3 + a_el;
+  float* b33 = b3 + b_el;
+  SplitScratch chain;
+  if (min_split > 1) {
+    chain.ws = b33 + (epi == SMOE_EPI_SWIGLU ? b_el : 0);
+    chain.cnt = reinterpret_cast<int*>(chain.ws + slot_el);
+    chain.units = (int)(tiles_max * min_split);
+    SMOE_CK(cudaMemsetAsync(chain.cnt, 0, cnt_bytes, st));
+  }
+  const SplitScratch* forced = min_split > 1 ? &chain : nullptr;
+  auto split = [&](const void* src, float* dst, int64_t rows, int lo_pos) {
+    const int64_t n = rows * (K / 4);
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)device_sms() * 16));
+    return launch_k(tc::tf32_split3_kernel, grid, 256, 0, st, static_cast<const float*>(src), dst, rows, K, lo_pos);
+  };
+  SMOE_CK(split(A, a3, rows_cap, 1));  // [hi | lo | hi]
+  SMOE_CK(split(B, b3, (int64_t)G * N, 0));  // [lo | hi | hi]
+  if (epi == SMOE_EPI_SWIGLU) SMOE_CK(split(B3, b33, (int64_t)G * N, 0));
+  CUtensorMap ma, mb, mb3;
+  if (!make_map_2d(&ma, a3, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rows_cap, K3, 4)) return SMOE_ERR_CUDA;
+  if (!make_map_3d(&mb, b3, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G, N, K3, 4)) return SMOE_ERR_CUDA;
+  if (epi == SMOE_EPI_SWIGLU) {
+    if (!make_map_3d(&mb3, b33, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G, N, K3, 4)) return SMOE_ERR_CUDA;
+  } else {
+    mb3 = mb;
+  }
+  const uint32_t idesc = umma_idesc_f16(2u, tc::BM, tc::BN);  // a/b format 2: tf32
+  if (epi == SMOE_EPI_SWIGLU)
+    return launch_tc<SMOE_EPI_SWIGLU, float, 4>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, (int)K3,
+                                                idesc, st, forced, min_split);
+  return launch_tc<SMOE_EPI_STORE, float, 4>(ma, mb, mb3, C, N, row_ptrs, offsets, ends, G, rows_cap, N, (int)K3,
+                                             idesc, st, forced, min_split);
+}
+
+bool tf32x3_enabled() {
+  static const bool off = getenv("SMOE_FP32_GEMM") != nullptr && strcmp(getenv("SMOE_FP32_GEMM"), "simt") == 0;
+  return !off;
+}
+
 // C [rows_cap, N] (ldc = N), or, when row_ptrs is given, output row r at the address
 // row_ptrs[r] (null: row skipped) and C unused.
 int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
@@ -396,7 +499,14 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   if (rows_cap == 0) return SMOE_OK;
   if (rows_cap > INT32_MAX) return SMOE_ERR_UNSUPPORTED;
   if (dtype == SMOE_F32) {
-    if (out_dtype != SMOE_F32 || G > simt::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
+    if (out_dtype != SMOE_F32) return SMOE_ERR_UNSUPPORTED;
+    // fp32 on the tensor cores where the shapes allow (3xTF32), else FFMA
+    if (tf32x3_enabled() && K % 4 == 0 && N % 8 == 0 && G <= tc::MAX_GROUPS && (int64_t)3 * K <= INT32_MAX &&
+        aligned16(A) && aligned16(B) && (!C || aligned16(C)) && (!B3 || aligned16(B3))) {
+      const int rc = tf32x3_gemm(A, B, B3, C, row_ptrs, epi, offsets, ends, G, rows_cap, N, K, st);
+      if (rc != SMOE_ERR_WORKSPACE) return rc;
+    }
+    if (G > simt::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
     dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, simt::BN / 2) : cdiv(N, simt::BN)));
     if (epi == SMOE_EPI_SWIGLU)
       SMOE_CK(launch_k(simt::grouped_gemm_f32_kernel<SMOE_EPI_SWIGLU>, grid, simt::THREADS, 0, st, 

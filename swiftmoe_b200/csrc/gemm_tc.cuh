@@ -223,7 +223,16 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool r
         const float u = __uint_as_float(uv[j]);
         h[j] = g / (1.0f + __expf(-g)) * u;
       }
-      if (row_ok) Store16<OutT>::cols32(crow, col0 + c * 32, N, h);
+      if (row_ok) {
+        if constexpr (sizeof(OutT) == 4) {
+          uint32_t hb[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) hb[j] = __float_as_uint(h[j]);
+          Store<float>::cols32(reinterpret_cast<float*>(crow), col0 + c * 32, N, hb);
+        } else {
+          Store16<OutT>::cols32(crow, col0 + c * 32, N, h);
+        }
+      }
     }
   } else {
 #pragma unroll 1
@@ -242,6 +251,41 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, OutT* crow, bool r
         }
       }
     }
+  }
+}
+
+// -------------------------------------------------------------- fp32 on tf32 tensor cores
+// An fp32 product a*b on tf32 tensor cores to about fp32 accuracy ("3xTF32"): with
+// hi(v) = v rounded to tf32 (10 explicit mantissa bits, to nearest, ties away from zero)
+// and lo(v) = v - hi(v) (exact in fp32), a*b = hi(a)hi(b) + hi(a)lo(b) + lo(a)hi(b) up to
+// lo(a)lo(b) and the tf32 truncation of the lo terms, both below 2^-21 |a b|.  The three
+// products are one tf32 GEMM over a K axis three times as long: every row of A becomes
+// [hi | lo | hi] and every weight row [lo | hi | hi], so the two small cross terms are
+// accumulated first and hi(a)hi(b) last.  The tensor cores' fp32 accumulation loses up
+// to an ulp of the running sum per step, so steps taken while the sum is still small
+// (2^-11 of the result) cost almost nothing and the error grows with K/8 steps, not 3K/8.
+// This kernel writes those rows (lo_pos = 1 for A, 0 for B); K % 4 == 0, 16-byte aligned
+// rows.
+__device__ __forceinline__ float tf32_hi(float v) {
+  const uint32_t u = __float_as_uint(v);
+  if ((u & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan as they are
+  return __uint_as_float((u + 0x1000u) & 0xffffe000u);
+}
+
+__global__ void tf32_split3_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t rows, int K,
+                                   int lo_pos) {
+  pdl_wait();
+  const int q = K / 4;  // float4 pieces per row
+  const int64_t n = rows * q;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / q;
+    const int c = (int)(i - r * q);
+    const float4 v = *reinterpret_cast<const float4*>(src + r * K + 4 * c);
+    const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+    const float4 l = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    float* row = dst + r * 3 * (int64_t)K + 4 * c;
+#pragma unroll
+    for (int seg = 0; seg < 3; ++seg) *reinterpret_cast<float4*>(row + seg * (int64_t)K) = seg == lo_pos ? l : h;
   }
 }
 
@@ -296,60 +340,99 @@ template <> __device__ __forceinline__ void store4<float>(float* p, float a, flo
   *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
 }
 
-__device__ __forceinline__ void add4(float4& s, const float* p) {
-  const float4 x = __ldcg(reinterpret_cast<const float4*>(p));
-  s.x += x.x;
-  s.y += x.y;
-  s.z += x.z;
-  s.w += x.w;
-}
-
 // The last unit of a tile: partial sums of the ks_n slots starting at tile_ws, in slot
-// order, then the epilogue; et = this thread's index among the 128 epilogue threads.
-// Consecutive threads take consecutive rows of one piece, so the slot reads coalesce.
+// order (from zero: the first add is exact), then the epilogue; et = this thread's index
+// among the 128 epilogue threads.  Consecutive threads take consecutive rows of one
+// piece, so the slot reads coalesce; each thread keeps U items x 4 slots of loads in
+// flight, since a full tile is 64 items per thread and L2 latency would otherwise
+// serialise them.
 template <int EPI, typename OutT>
 __device__ __forceinline__ void split_fixup(const float* tile_ws, int ks_n, const TileCoord& t, OutT* C, int64_t ldc,
                                             const uint64_t* row_ptrs, int N, int et) {
   constexpr bool kPair = EpiTraits<EPI>::kPair;
+  constexpr int U = kPair ? 4 : 8, QB = 4;
   const int col0 = kPair ? t.nb * 128 : t.nb * BN;
   // output pieces of the tile that lie below N (N % 8 == 0: a piece is all in or all out)
   const int np = min((kPair ? 128 : BN) / 4, (N - col0) / 4);
   const int rows = t.rows_valid;
-  for (int i = et; i < np * rows; i += 128) {
-    const int p = i / rows, row = i - p * rows, c = 4 * p;
-    bool ok = true;
-    OutT* dst = out_row(C, ldc, row_ptrs, t.row0 + row, ok);
-    if (!ok) continue;
-    const float* pa = tile_ws + ((int64_t)p * BM + row) * 4;
-    const float* pb = tile_ws + ((int64_t)(p + 32) * BM + row) * 4;  // [gate | up]: the up piece
-    float4 a = __ldcg(reinterpret_cast<const float4*>(pa));
-    float4 b = kPair ? __ldcg(reinterpret_cast<const float4*>(pb)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 1; q < ks_n; ++q) {
-      add4(a, pa + (int64_t)q * BM * BN);
-      if (kPair) add4(b, pb + (int64_t)q * BM * BN);
+  const int total = np * rows;
+  const int64_t slot = (int64_t)BM * BN;
+  for (int i0 = et; i0 < total; i0 += 128 * U) {
+    float4 a[U], b[U];
+    int off[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * 128;
+      const int p = i / rows, row = i - p * rows;
+      off[u] = i < total ? (p * BM + row) * 4 : -1;
+      a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if constexpr (EPI == SMOE_EPI_SWIGLU) {
-      store4<OutT>(dst + col0 + c, a.x / (1.0f + __expf(-a.x)) * b.x, a.y / (1.0f + __expf(-a.y)) * b.y,
-                   a.z / (1.0f + __expf(-a.z)) * b.z, a.w / (1.0f + __expf(-a.w)) * b.w);
-    } else if constexpr (EPI == EPI_GATEUP) {
-      store4<OutT>(dst + col0 + c, a.x, a.y, a.z, a.w);
-      store4<OutT>(dst + N + col0 + c, b.x, b.y, b.z, b.w);
-    } else {
-      store4<OutT>(dst + col0 + c, a.x, a.y, a.z, a.w);
+    for (int q0 = 0; q0 < ks_n; q0 += QB) {
+      float4 la[U][QB], lb[U][QB];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int qq = 0; qq < QB; ++qq)
+          if (off[u] >= 0 && q0 + qq < ks_n) {
+            const float* pq = tile_ws + (q0 + qq) * slot + off[u];
+            la[u][qq] = __ldcg(reinterpret_cast<const float4*>(pq));
+            if (kPair) lb[u][qq] = __ldcg(reinterpret_cast<const float4*>(pq + 32 * BM * 4));  // the up piece
+          }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int qq = 0; qq < QB; ++qq)
+          if (off[u] >= 0 && q0 + qq < ks_n) {
+            a[u].x += la[u][qq].x;
+            a[u].y += la[u][qq].y;
+            a[u].z += la[u][qq].z;
+            a[u].w += la[u][qq].w;
+            if (kPair) {
+              b[u].x += lb[u][qq].x;
+              b[u].y += lb[u][qq].y;
+              b[u].z += lb[u][qq].z;
+              b[u].w += lb[u][qq].w;
+            }
+          }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (off[u] < 0) continue;
+      const int i = i0 + u * 128;
+      const int p = i / rows, row = i - p * rows, c = 4 * p;
+      bool ok = true;
+      OutT* dst = out_row(C, ldc, row_ptrs, t.row0 + row, ok);
+      if (!ok) continue;
+      const float4 x = a[u], y = b[u];
+      if constexpr (EPI == SMOE_EPI_SWIGLU) {
+        store4<OutT>(dst + col0 + c, x.x / (1.0f + __expf(-x.x)) * y.x, x.y / (1.0f + __expf(-x.y)) * y.y,
+                     x.z / (1.0f + __expf(-x.z)) * y.z, x.w / (1.0f + __expf(-x.w)) * y.w);
+      } else if constexpr (EPI == EPI_GATEUP) {
+        store4<OutT>(dst + col0 + c, x.x, x.y, x.z, x.w);
+        store4<OutT>(dst + N + col0 + c, y.x, y.y, y.z, y.w);
+      } else {
+        store4<OutT>(dst + col0 + c, x.x, x.y, x.z, x.w);
+      }
     }
   }
 }
 
 // EPI: SMOE_EPI_STORE or SMOE_EPI_SWIGLU.  OutT: float, __nv_bfloat16 or __half.
 // split_ws / split_cnt: split-K scratch of split_units fp32 [BM, BN] slots and as many
-// counters (all zero between launches), or null for no split.
-template <int EPI, typename OutT>
+// counters (all zero between launches), or null for no split; a split launch has at most
+// split_units tiles x slices, so each of its tiles has a counter.  min_split: at least that
+// many K slices per tile (a bound on the length of each accumulation chain), as far as
+// the scratch holds them.
+// ES: operand element size -- 2 for bf16/fp16 (kind::f16, 64 elements per 128-byte
+// swizzle row), 4 for tf32 (fp32 operands, kind::tf32, 32 elements per row); either way a
+// k-block is one 128-byte row per operand row and 4 MMAs of 32 bytes of K.
+template <int EPI, typename OutT, int ES = 2>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmB3, OutT* __restrict__ C, int64_t ldc, const uint64_t* __restrict__ row_ptrs,
                         const int32_t* __restrict__ offsets, const int32_t* __restrict__ ends, int G, int N,
                         int K, int rows_cap, int gm, uint32_t idesc, float* __restrict__ split_ws,
-                        int* __restrict__ split_cnt, int split_units) {
+                        int* __restrict__ split_cnt, int split_units, int min_split) {
   pdl_wait();
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -371,7 +454,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x & 31;
   constexpr bool kPair = EpiTraits<EPI>::kPair;
   const int NB = kPair ? (N + 127) / 128 : (N + BN - 1) / BN;
-  const int KB = (K + BK - 1) / BK;
+  constexpr int BKE = 128 / ES;  // K elements per k-block
+  const int KB = (K + BKE - 1) / BKE;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -404,7 +488,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
   const int tiles = s_ts[G];
-  const int ks_n = split_ws != nullptr && split_cnt != nullptr ? split_count(tiles, KB, min(split_units, (int)gridDim.x)) : 1;
+  int ks_n = 1;
+  if (split_ws != nullptr && split_cnt != nullptr && tiles > 0) {
+    ks_n = max(split_count(tiles, KB, min(split_units, (int)gridDim.x)), min(min_split, KB));
+    if ((int64_t)tiles * ks_n > split_units) ks_n = max(1, split_units / tiles);  // never past the scratch
+  }
   const int total = tiles * ks_n;  // work units: (tile, K slice), slices of a tile adjacent
 
   if (warp == 0) {
@@ -425,10 +513,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
-          tma_load_2d(a_dst, &tmA, fb, kb * BK, t.row0);
-          tma_load_3d(b_dst, &tmB, fb, kb * BK, n0, t.g);
-          if (kPair) tma_load_3d(b_dst + B_BYTES / 2, &tmB3, fb, kb * BK, n0, t.g);
-          else tma_load_3d(b_dst + B_BYTES / 2, &tmB, fb, kb * BK, n0 + 128, t.g);
+          tma_load_2d(a_dst, &tmA, fb, kb * BKE, t.row0);
+          tma_load_3d(b_dst, &tmB, fb, kb * BKE, n0, t.g);
+          if (kPair) tma_load_3d(b_dst + B_BYTES / 2, &tmB3, fb, kb * BKE, n0, t.g);
+          else tma_load_3d(b_dst + B_BYTES / 2, &tmB, fb, kb * BKE, n0 + 128, t.g);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -459,8 +547,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t a_desc = umma_desc_sw128(smem_u32(sA + stage * A_BYTES));
           const uint64_t b_desc = umma_desc_sw128(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K each: 16 f16 or 8 tf32 elements
+            if constexpr (ES == 4)
+              umma_tf32(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
+          }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }

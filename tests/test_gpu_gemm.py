@@ -84,7 +84,8 @@ def test_grouped_swiglu_tc(K, dtype, sizes, K_, N):
                                          ([64] * 9, 96, 64)])
 def test_grouped_fp32_simt(K, sizes, K_, N):
     A, B, B3, offs, rows = make_groups(sizes, K_, N, torch.float32, seed=3)
-    # fp32 FFMA accumulation: 1e-5 absolute at unit output scale
+    # fp32 accuracy, 1e-5 absolute at unit output scale: FFMA for K % 4 != 0 or N % 8 != 0,
+    # the tf32 tensor cores with split operands (3xTF32) otherwise
     out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
     ref = ref_store(A, B, offs)[:rows].numpy()
     assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * max(1.0, np.abs(ref).max())
@@ -301,4 +302,30 @@ def test_split_k_interleaved_shapes(K):
         out = K.grouped_gemm(A.cuda(), B.cuda(), offs.cuda())
         ref = ref_store(A, B, offs)[:rows]
         assert elementwise_rel_err(out[:rows].float().cpu().numpy(), ref.numpy()) <= 2e-2, i
+    assert K.read_device_error("cuda") == 0
+
+
+# fp32 grouped GEMMs on the tf32 tensor cores with split operands (3xTF32): the fp32
+# layer shapes (d 512, F 2048), ragged and empty groups, a K not a multiple of 32,
+# SwiGLU, and launches with few tiles (split-K).  Bar: 1e-5 absolute at unit scale
+# against fp64, as for the FFMA kernel; the same call twice is bit-identical.
+TF32X3 = [
+    ([1000, 0, 1500, 1596], 512, 2048),   # the fp32 layer's gate/up shape (SwiGLU: 2 x 2048)
+    ([1000, 0, 1500, 1596], 2048, 512),   # its down projection
+    ([37, 300, 5], 100, 264),             # K % 32 != 0, N % 256 != 0
+    ([3], 4096, 512),                     # few tiles: split-K slices
+    ([700, 300], 14336, 256),             # K > 4096: accumulation chains cut into K slices
+]
+
+
+@pytest.mark.parametrize("sizes,K_,N", TF32X3)
+@pytest.mark.parametrize("epi", [0, 1])
+def test_fp32_tensor_core_3xtf32(K, sizes, K_, N, epi):
+    A, B, B3, offs, rows = make_groups(sizes, K_, N, torch.float32, seed=K_ + N + epi, std=1.0 / np.sqrt(K_))
+    Ad, Bd, B3d, od = A.cuda(), B.cuda(), B3.cuda(), offs.cuda()
+    run = (lambda: K.grouped_gemm(Ad, Bd, od, B3=B3d, epilogue=1)) if epi else (lambda: K.grouped_gemm(Ad, Bd, od))
+    out = run()
+    ref = (ref_swiglu(A, B, B3, offs) if epi else ref_store(A, B, offs))[:rows].numpy()
+    assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * max(1.0, np.abs(ref).max())
+    assert torch.equal(out, run())
     assert K.read_device_error("cuda") == 0
