@@ -293,12 +293,17 @@ void* tf32_scratch(cudaStream_t st, size_t bytes) {
   if (s.bytes >= bytes) return s.p;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  // relaxed capture mode: another thread may be capturing a graph on another stream
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
   if (s.p) {
     cudaFree(s.p);  // waits for the device: no launch still reads the old buffer
     s = Tf32Scratch{};
   }
   void* p = nullptr;
-  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+  const bool ok = cudaMalloc(&p, bytes) == cudaSuccess;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (!ok) {
     cudaGetLastError();
     return nullptr;
   }
