@@ -329,3 +329,35 @@ def test_fp32_tensor_core_3xtf32(K, sizes, K_, N, epi):
     assert max_abs_err(out[:rows].cpu().numpy(), ref) <= 1e-5 * max(1.0, np.abs(ref).max())
     assert torch.equal(out, run())
     assert K.read_device_error("cuda") == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_grouped_gemm_in_cuda_graph(K, dtype):
+    """A grouped GEMM captured into a CUDA graph equals the eager call bit for bit: bf16
+    with few tiles (split-K; the capture stream's scratch is allocated during the
+    capture), fp32 on the tensor-core path (its scratch grown by an eager call on the
+    capture stream first)."""
+    sizes, K_, N = ([5, 0, 3], 14336, 1024) if dtype == torch.bfloat16 else ([300, 200], 2048, 512)
+    A, B, _, offs, rows = make_groups(sizes, K_, N, dtype, seed=31, std=0.02)
+    Ad, Bd, od = A.cuda(), B.cuda(), offs.cuda()
+    eager = K.grouped_gemm(Ad, Bd, od)
+    out = torch.full_like(eager, 5.0)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    if dtype == torch.float32:                      # the fp32 scratch must exist before capture
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            K.grouped_gemm(Ad, Bd, od, out=out)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        out.fill_(5.0)
+    with torch.cuda.graph(g, stream=s):
+        K.grouped_gemm(Ad, Bd, od, out=out)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out[:rows], eager[:rows])
+    g.replay()                                      # counters reset by the first replay
+    torch.cuda.synchronize()
+    assert torch.equal(out[:rows], eager[:rows])
+    del g
+    assert K.read_device_error("cuda") == 0
