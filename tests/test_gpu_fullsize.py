@@ -112,3 +112,31 @@ def test_full_size_plan_bit_exact(T, k, E, cf):
     assert (plan["slot_row"].cpu().numpy() == expect).all()
     if cap:
         assert kept_n.max() <= cap and (np.bincount(idx_n.ravel(), minlength=E) > cap).any()
+
+
+@torch.no_grad()
+def test_fp32_layer_token_sample():
+    """The fp32 layer (d 512, 8 experts, top-2, SwiGLU 2048, 4096 tokens; the reference's
+    use_fp16=False path), whose expert GEMMs run as split tf32 products on the tensor
+    cores: 64 sampled tokens against float64 on the layer's own routing, within the fp32
+    bar of 1e-5 x the output scale."""
+    import swiftmoe_b200 as S
+    from swiftmoe_b200 import kernels
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(5)
+    m = S.UltimateMoE(8, 512, use_fp16=False, dtype=torch.float32, top_k=2, expert_type="swiglu", d_ff=2048,
+                      use_nccl_opt=False, device=dev)
+    x = torch.randn(4096, 512, device=dev, generator=torch.Generator(dev).manual_seed(6))
+    out = m(x)
+    idx, _ = kernels.router(x, m.gate_weight, 2)
+    tok = torch.randperm(4096, generator=torch.Generator().manual_seed(7))[:64].to(dev)
+    xs = x[tok].double()
+    sel = idx[tok].long()
+    w = torch.softmax((xs @ m.gate_weight.double().T).gather(1, sel), dim=-1)
+    ref = torch.zeros_like(xs)
+    for e in torch.unique(sel).tolist():
+        rows, slots = torch.nonzero(sel == e, as_tuple=True)
+        h = torch.nn.functional.silu(xs[rows] @ m.w1[e].double().T) * (xs[rows] @ m.w3[e].double().T)
+        ref.index_add_(0, rows, (h @ m.w2[e].double().T) * w[rows, slots].view(-1, 1))
+    err = (out[tok].double() - ref).abs().max().item()
+    assert err <= 1e-5 * max(1.0, ref.abs().max().item()), err
