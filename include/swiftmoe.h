@@ -42,6 +42,11 @@ typedef struct CUstream_st* smoe_stream_t; /* == cudaStream_t */
 #define SMOE_F32 0
 #define SMOE_F16 1
 #define SMOE_BF16 2
+/* smoe_layer_args.dtype only: an fp32 layer whose routed expert weights (w1, w3, w2 or
+ * w_lin) are given split by smoe_tf32_split_weights, [E, N, 3K] instead of [E, N, K]
+ * (the shared expert's stay plain).  The layer then skips splitting them on every call;
+ * it needs d_model % 8 == 0 and d_ff % 8 == 0 (else SMOE_ERR_UNSUPPORTED).             */
+#define SMOE_F32_SPLITW 16
 
 /* ----------------------------------------------------------------------- expert kinds */
 #define SMOE_EXPERT_LINEAR 0 /* y = x W_e^T           (one bias-free d x d linear)      */
@@ -172,6 +177,14 @@ SMOE_API int smoe_grouped_gemm_rows(const void* A, const void* B, const void* B3
                                     int dtype, int out_dtype, int epilogue, const int32_t* offsets,
                                     const int32_t* ends, int G, int64_t rows_cap, int N, int K,
                                     smoe_stream_t stream);
+
+/* out[r, :] = [lo(w[r, :]) | hi(w[r, :]) | hi(w[r, :])] for `rows` fp32 rows of K (K % 4
+ * == 0, 16-byte aligned): hi = the tf32 rounding (to nearest, ties away from zero), lo =
+ * the exact remainder -- the weight layout the fp32 grouped GEMMs run on the tf32 tensor
+ * cores (three tf32 products per fp32 product).  A layer that keeps this copy of its
+ * weights passes dtype SMOE_F32_SPLITW to smoe_layer_fwd.  No counterpart in the
+ * reference (its fp32 experts are torch.mm / nn.Linear, models/ultimate_moe.py:237-250). */
+SMOE_API int smoe_tf32_split_weights(const float* w, float* out, int64_t rows, int K, smoe_stream_t stream);
 
 /* dst[g, c, r] = src[g, r, c] for G matrices of [R, C] (weight relayout, e.g. the
  * reference's x@W expert_weights [E, d_in, d_out] -> nn.Linear layout [E, d_out, d_in]). */

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 from typing import Dict, List, Optional
 
 import torch
@@ -226,6 +227,13 @@ class MoECore(nn.Module):
         T = x.shape[0]
         a.tokens, a.d_model, a.num_experts, a.top_k = T, self.d_model, self.num_experts, self.top_k
         a.dtype = L.dtype_code(self.compute_dtype)
+        # fp32 layers keep their routed expert weights split for the tf32 tensor cores
+        # (rebuilt when a weight changes), instead of the library splitting them per call
+        split = (self.compute_dtype == torch.float32 and self.d_model % 8 == 0 and
+                 (self.expert_type != "swiglu" or self.d_ff % 8 == 0) and
+                 os.environ.get("SMOE_FP32_GEMM") != "simt" and os.environ.get("SMOE_FP32_SPLIT_CACHE") != "0")
+        if split:
+            a.dtype = L.SMOE_F32_SPLITW
         a.capacity = self._capacity(T)
         a.x, a.gate_w, a.out = x.data_ptr(), self._gate().data_ptr(), out.data_ptr()
         bias = self._logit_bias()
@@ -233,11 +241,16 @@ class MoECore(nn.Module):
         keep = [bias]
         if self.expert_type == "swiglu":
             w1, w3, w2 = self._swiglu()
+            if split:
+                w1, w3, w2 = (self._cached(name, [w], lambda w=w: K.tf32_split_weights(w.detach()))
+                              for name, w in (("w1_tf32", w1), ("w3_tf32", w3), ("w2_tf32", w2)))
             a.expert_type, a.d_ff = L.SMOE_EXPERT_SWIGLU, self.d_ff
             a.w1, a.w3, a.w2 = w1.data_ptr(), w3.data_ptr(), w2.data_ptr()
             keep += [w1, w3, w2]
         else:
             wl = self._linear_kmajor()
+            if split:
+                wl = self._cached("wl_tf32", [wl], lambda: K.tf32_split_weights(wl.detach()))
             a.expert_type, a.d_ff = L.SMOE_EXPERT_LINEAR, 0
             a.w_lin = wl.data_ptr()
             keep.append(wl)

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libswiftmoe.so"
 
 SMOE_OK = 0
 SMOE_F32, SMOE_F16, SMOE_BF16 = 0, 1, 2
+SMOE_F32_SPLITW = 16   # layer dtype: fp32 with routed expert weights split for the tf32 tensor cores
 SMOE_EXPERT_LINEAR, SMOE_EXPERT_SWIGLU = 0, 1
 SMOE_EPI_STORE, SMOE_EPI_SWIGLU, SMOE_EPI_GATEUP = 0, 1, 3
 
@@ -71,6 +72,7 @@ SIGNATURES = {
     "smoe_grouped_gemm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp]),
     "smoe_grouped_gemm_rows": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp]),
     "smoe_transpose_batched": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "smoe_tf32_split_weights": (_i32, [_vp, _vp, _i64, _i32, _vp]),
     "smoe_gather_rows": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _vp]),
     "smoe_ep_regroup_workspace_size": (_sz, [_i32, _i32]),
     "smoe_ep_regroup_plan": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -428,8 +428,11 @@ bool use_pair_kernel(int64_t rows_cap, int G) {
 
 // The fp32 grouped GEMM on tf32 tensor cores (3xTF32, see tc::tf32_split3_kernel):
 // SMOE_ERR_WORKSPACE when no scratch could be had (the caller then uses the FFMA kernel).
+// b_split: B (and B3) are already the [G, N, 3K] rows [lo | hi | hi] of
+// smoe_tf32_split_weights, so only A is split here.
 int tf32x3_gemm(const void* A, const void* B, const void* B3, void* C, const uint64_t* row_ptrs, int epi,
-                const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, cudaStream_t st) {
+                const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K, cudaStream_t st,
+                bool b_split = false) {
   const int64_t K3 = 3 * (int64_t)K;
   const size_t a_el = (size_t)rows_cap * K3, b_el = (size_t)G * N * K3;
   // Accumulation chains of at most kTf32ChainKb k-blocks (48 x 32 tf32 elements of the
@@ -447,15 +450,16 @@ int tf32x3_gemm(const void* A, const void* B, const void* B3, void* C, const uin
   // one counter per slot: the kernel splits only while tiles x slices fit the slots, so
   // every tile index of a split launch has a counter, overlapping row ranges included
   const size_t cnt_bytes = (size_t)tiles_max * min_split * sizeof(int);
-  const size_t bytes = (a_el + b_el * (epi == SMOE_EPI_SWIGLU ? 2 : 1) + slot_el) * sizeof(float) + cnt_bytes;
+  const size_t b_own = b_split ? 0 : b_el * (epi == SMOE_EPI_SWIGLU ? 2 : 1);
+  const size_t bytes = (a_el + b_own + slot_el) * sizeof(float) + cnt_bytes;
   float* s = static_cast<float*>(tf32_scratch(st, bytes));
   if (!s) return SMOE_ERR_WORKSPACE;
   float* a3 = s;
-  float* b3 = a3 + a_el;
-  float* b33 = b3 + b_el;
+  float* b3 = b_split ? static_cast<float*>(const_cast<void*>(B)) : a3 + a_el;
+  float* b33 = b_split ? static_cast<float*>(const_cast<void*>(B3)) : b3 + b_el;
   SplitScratch chain;
   if (min_split > 1) {
-    chain.ws = b33 + (epi == SMOE_EPI_SWIGLU ? b_el : 0);
+    chain.ws = a3 + a_el + b_own;
     chain.cnt = reinterpret_cast<int*>(chain.ws + slot_el);
     chain.units = (int)(tiles_max * min_split);
     SMOE_CK(cudaMemsetAsync(chain.cnt, 0, cnt_bytes, st));
@@ -467,8 +471,10 @@ int tf32x3_gemm(const void* A, const void* B, const void* B3, void* C, const uin
     return launch_k(tc::tf32_split3_kernel, grid, 256, 0, st, static_cast<const float*>(src), dst, rows, K, lo_pos);
   };
   SMOE_CK(split(A, a3, rows_cap, 1));  // [hi | lo | hi]
-  SMOE_CK(split(B, b3, (int64_t)G * N, 0));  // [lo | hi | hi]
-  if (epi == SMOE_EPI_SWIGLU) SMOE_CK(split(B3, b33, (int64_t)G * N, 0));
+  if (!b_split) {
+    SMOE_CK(split(B, b3, (int64_t)G * N, 0));  // [lo | hi | hi]
+    if (epi == SMOE_EPI_SWIGLU) SMOE_CK(split(B3, b33, (int64_t)G * N, 0));
+  }
   CUtensorMap ma, mb, mb3;
   if (!make_map_2d(&ma, a3, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rows_cap, K3, 4)) return SMOE_ERR_CUDA;
   if (!make_map_3d(&mb, b3, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, G, N, K3, 4)) return SMOE_ERR_CUDA;
@@ -494,7 +500,7 @@ bool tf32x3_enabled() {
 // row_ptrs[r] (null: row skipped) and C unused.
 int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int dtype, int out_dtype, int epi,
                       const int32_t* offsets, const int32_t* ends, int G, int64_t rows_cap, int N, int K,
-                      cudaStream_t st, const uint64_t* row_ptrs = nullptr) {
+                      cudaStream_t st, const uint64_t* row_ptrs = nullptr, bool b_split = false) {
   if (row_ptrs) C = nullptr;
   if (!A || !B || (!C && !row_ptrs) || !offsets || G < 1 || N < 1 || K < 1 || rows_cap < 0) return SMOE_ERR_INVALID;
   if (epi != SMOE_EPI_STORE && epi != SMOE_EPI_SWIGLU && epi != SMOE_EPI_GATEUP) return SMOE_ERR_INVALID;
@@ -506,10 +512,13 @@ int grouped_gemm_impl(const void* A, const void* B, const void* B3, void* C, int
   if (dtype == SMOE_F32) {
     if (out_dtype != SMOE_F32) return SMOE_ERR_UNSUPPORTED;
     // fp32 on the tensor cores where the shapes allow (3xTF32), else FFMA
-    if (tf32x3_enabled() && K % 4 == 0 && N % 8 == 0 && G <= tc::MAX_GROUPS && (int64_t)3 * K <= INT32_MAX &&
-        aligned16(A) && aligned16(B) && (!C || aligned16(C)) && (!B3 || aligned16(B3))) {
-      const int rc = tf32x3_gemm(A, B, B3, C, row_ptrs, epi, offsets, ends, G, rows_cap, N, K, st);
-      if (rc != SMOE_ERR_WORKSPACE) return rc;
+    const bool tc_ok = tf32x3_enabled() && K % 4 == 0 && N % 8 == 0 && G <= tc::MAX_GROUPS &&
+                       (int64_t)3 * K <= INT32_MAX && aligned16(A) && aligned16(B) && (!C || aligned16(C)) &&
+                       (!B3 || aligned16(B3));
+    if (b_split && !tc_ok) return SMOE_ERR_UNSUPPORTED;  // split weights fit the tensor-core path only
+    if (tc_ok) {
+      const int rc = tf32x3_gemm(A, B, B3, C, row_ptrs, epi, offsets, ends, G, rows_cap, N, K, st, b_split);
+      if (rc != SMOE_ERR_WORKSPACE || b_split) return rc;
     }
     if (G > simt::MAX_GROUPS) return SMOE_ERR_UNSUPPORTED;
     dim3 grid((unsigned)(cdiv(rows_cap, simt::BM) + G), (unsigned)(epi == SMOE_EPI_SWIGLU ? cdiv(N, simt::BN / 2) : cdiv(N, simt::BN)));
@@ -938,6 +947,17 @@ int smoe_grouped_gemm_rows(const void* A, const void* B, const void* B3, const u
                            (cudaStream_t)stream, row_ptrs);
 }
 
+int smoe_tf32_split_weights(const float* w, float* out, int64_t rows, int K, smoe_stream_t stream) {
+  if (!w || !out || rows < 0 || K < 4 || K % 4 != 0) return SMOE_ERR_INVALID;
+  if (!aligned16(w) || !aligned16(out)) return SMOE_ERR_UNSUPPORTED;
+  if (rows == 0) return SMOE_OK;
+  const int64_t n = rows * (K / 4);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)device_sms() * 16));
+  SMOE_CK(launch_k(tc::tf32_split3_kernel, grid, 256, 0, (cudaStream_t)stream, w, out, rows, K, 0));
+  SMOE_CK(cudaGetLastError());
+  return SMOE_OK;
+}
+
 int smoe_transpose_batched(const void* src, void* dst, int dtype, int G, int R, int C, smoe_stream_t stream) {
   const int es = elt_size(dtype);
   if (es == 0 || G < 0 || R < 0 || C < 0) return SMOE_ERR_INVALID;
@@ -1243,11 +1263,28 @@ int smoe_event_elapsed(void* start, void* end, float* ms) {
 
 size_t smoe_layer_workspace_size(const smoe_layer_args* a) {
   LayerPlan p;
+  if (a && a->dtype == SMOE_F32_SPLITW) {
+    smoe_layer_args b = *a;
+    b.dtype = SMOE_F32;
+    return layer_plan(&b, &p) ? p.total : 0;
+  }
   if (!a || !layer_plan(a, &p)) return 0;
   return p.total;
 }
 
+static int layer_fwd_impl(const smoe_layer_args* a, smoe_stream_t stream, bool split_w);
+
+// dtype SMOE_F32_SPLITW: an fp32 layer whose routed expert weights come split
 int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
+  if (a && a->dtype == SMOE_F32_SPLITW) {
+    smoe_layer_args b = *a;
+    b.dtype = SMOE_F32;
+    return layer_fwd_impl(&b, stream, true);
+  }
+  return layer_fwd_impl(a, stream, false);
+}
+
+static int layer_fwd_impl(const smoe_layer_args* a, smoe_stream_t stream, bool split_w) {
   if (!a) return SMOE_ERR_INVALID;
   // Decode-sized batches (a one-block dispatch plan) launch the chain below with
   // programmatic dependent launch: measured 0.158 -> 0.147 ms for one token of the
@@ -1317,13 +1354,15 @@ int smoe_layer_fwd(const smoe_layer_args* a, smoe_stream_t stream) {
     rc = gather ? launch_gemv(a->x, a->w1, a->w3, h, nullptr, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E,
                               p.rows_cap, F, d, st, row_token, T)
                 : grouped_gemm_impl(xrows, a->w1, a->w3, h, dt, dt, SMOE_EPI_SWIGLU, offsets, nullptr, E, p.rows_cap,
-                                    F, d, st);
+                                    F, d, st, nullptr, split_w);
     if (rc) return rc;
     if ((rc = mark(3))) return rc;
-    rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, F, st);
+    rc = grouped_gemm_impl(h, a->w2, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, F, st,
+                           nullptr, split_w);
     if (rc) return rc;
   } else {
-    rc = grouped_gemm_impl(xrows, a->w_lin, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, d, st);
+    rc = grouped_gemm_impl(xrows, a->w_lin, nullptr, y, dt, dt, SMOE_EPI_STORE, offsets, nullptr, E, p.rows_cap, d, d, st,
+                           nullptr, split_w);
     if (rc) return rc;
     if ((rc = mark(3))) return rc;
   }

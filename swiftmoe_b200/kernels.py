@@ -226,6 +226,21 @@ def router_dwg(x: torch.Tensor, row_token_full: torch.Tensor, offsets_full: torc
     return out
 
 
+def tf32_split_weights(w: torch.Tensor) -> torch.Tensor:
+    """fp32 [..., K] -> [..., 3K] rows [lo | hi | hi] (hi: the tf32 rounding, lo: the exact
+    remainder), the weight layout of the fp32 GEMMs on the tf32 tensor cores
+    (``smoe_tf32_split_weights``); K % 4 == 0."""
+    _need_cuda(w)
+    if w.dtype != torch.float32:
+        raise L.SwiftMoEError("tf32_split_weights takes fp32 weights")
+    w = w.contiguous()
+    Kd = w.shape[-1]
+    out = torch.empty(tuple(w.shape[:-1]) + (3 * Kd,), dtype=torch.float32, device=w.device)
+    L.check(L.load().smoe_tf32_split_weights(L.ptr(w), L.ptr(out), w.numel() // max(Kd, 1), Kd,
+                                             L.stream_handle(w.device)), "smoe_tf32_split_weights")
+    return out
+
+
 def transpose_batched(src: torch.Tensor, out: Optional[torch.Tensor] = None):
     """[G, R, C] -> [G, C, R]."""
     _need_cuda(src)

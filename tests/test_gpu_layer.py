@@ -231,3 +231,28 @@ def test_bench_records_schema():
     assert {"Router", "Dispatch_Comm", "Expert_Compute", "Combine_Comm"} <= set(r)
     b = run_single_config("baseline", 16, 256, 300, device=torch.device("cuda", 0), warmup=2, iterations=3)
     assert REFERENCE_RECORD_KEYS <= set(b) and b["throughput_tokens_per_sec"] > 0
+
+
+@torch.no_grad()
+def test_fp32_layer_keeps_split_weights(monkeypatch):
+    """An fp32 layer passes its routed expert weights pre-split (SMOE_F32_SPLITW): the
+    output equals the call that splits them inside the library bit for bit, and after an
+    in-place weight update the kept copy is rebuilt (equal again, and different from the
+    output before the update)."""
+    import swiftmoe_b200 as S
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(11)
+    m = S.UltimateMoE(8, 512, use_fp16=False, dtype=torch.float32, top_k=2, expert_type="swiglu", d_ff=2048,
+                      use_nccl_opt=False, device=dev)
+    x = torch.randn(777, 512, device=dev)
+    kept = m(x)
+    assert any(k.endswith("_tf32") for k in m._wcache)
+    monkeypatch.setenv("SMOE_FP32_SPLIT_CACHE", "0")
+    plain = m(x)
+    monkeypatch.delenv("SMOE_FP32_SPLIT_CACHE")
+    assert torch.equal(kept, plain)
+    m.w2.mul_(1.5)
+    kept2 = m(x)
+    monkeypatch.setenv("SMOE_FP32_SPLIT_CACHE", "0")
+    plain2 = m(x)
+    assert torch.equal(kept2, plain2) and not torch.equal(kept, kept2)
